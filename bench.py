@@ -1,0 +1,567 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fused tensor-parallel RMSNorm.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P bench.py --gpus N ...
+
+Workload (the configuration the metric is quoted on): Llama-3-8B-shaped rows,
+hidden 4096, 4096 rows, bf16, eps 1e-6, tensor parallel over the N ranks
+(TP = N: local width 4096 / N), x ~ N(0,1), weight ~ 1 + 0.1 N(0,1), per-rank
+seed 1000 + rank. One step = one forward call of every rank over one batch.
+The total work is fixed as N grows (strong scaling); ``value`` is the whole
+job's effective HBM GB/s: sum over ranks of the algorithmic bytes
+(2 * rows * local_hidden * 2 + local_hidden * 2: read x, write y, read w once)
+divided by the max-over-ranks time per step.
+
+Our arm prints one JSON line with the device-timed value (inputs resident in
+HBM, several input/output sets rotated so that they exceed L2), the roofline of
+the forward kernel, an end-to-end figure through the public API with pinned
+host buffers copied in and out inside the timed region, the CPU baseline, and
+clocks sampled with nvidia-smi during the timed region.
+
+``--impl reference`` times the reference's own CPU path (its AllReduce TP
+RMSNorm restated op for op on torch CPU tensors, all ranks' slices in one
+process, every host thread) on rank 0; other ranks exit without work.
+
+``--sweep decode|prefill|llama|all`` additionally writes per-point JSON lines
+(decode latency, prefill GB/s, TP scaling) to --out.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+WORKLOAD = dict(name="llama3_8b", hidden=4096, rows=4096, dtype=torch.bfloat16, eps=1e-6,
+                seed_base=1000)
+METRIC = "effective HBM GB/s, fused TP RMSNorm forward (Llama-3-8B rows, TP=N)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="bound on the CPU baseline sample (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", choices=["none", "decode", "prefill", "llama", "all"], default="none")
+    ap.add_argument("--out", default=None, help="JSON-lines file for sweep points")
+    return ap.parse_args(argv)
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return world, rank, local
+
+
+def measured_peak_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def algorithmic_bytes(rows, hl, elem):
+    return 2 * rows * hl * elem + hl * elem
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of the job's GPUs during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = set(uuids)
+        self.proc = None
+        self.tmp = None
+
+    def start(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "nvidia-smi unavailable"}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.tmp.flush()
+        self.tmp.seek(0)
+        sm, smax, power, reasons = [], [], [], set()
+        for line in self.tmp.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10 or (self.uuids and parts[1] not in self.uuids):
+                continue
+            try:
+                sm.append(float(parts[2]))
+                smax.append(float(parts[3]))
+                power.append(float(parts[4]))
+            except ValueError:
+                continue
+            for name, val in zip(self.REASONS, parts[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.tmp.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "power_w_max": max(power), "samples": len(sm)}
+
+
+def gpu_uuid(device):
+    try:
+        u = str(torch.cuda.get_device_properties(device).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_reference_time(xs, ws, eps, seconds, max_calls=10**6, min_calls=3):
+    """Mean seconds per call of the reference's AllReduce path on torch CPU."""
+    from oracle import torch_port  # CPU baseline leg only
+
+    torch_port.allreduce_path_group(xs, ws, eps)   # warm
+    n, t0 = 0, time.perf_counter()
+    while n < min_calls or (time.perf_counter() - t0 < seconds and n < max_calls):
+        torch_port.allreduce_path_group(xs, ws, eps)
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+def run_reference_arm(args):
+    """--impl reference: rank 0 times the reference's CPU path on all ranks' data."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from rmsnorm_tp_b200.workloads import make_group
+
+    tp = max(1, args.gpus)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w = WORKLOAD
+    xs, ws = make_group(w["rows"], w["hidden"], tp, w["dtype"], w["seed_base"])
+    hl = w["hidden"] // tp
+    from oracle import torch_port
+
+    for _ in range(max(args.warmup, 1)):
+        torch_port.allreduce_path_group(xs, ws, w["eps"])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        torch_port.allreduce_path_group(xs, ws, w["eps"])
+        times.append(time.perf_counter() - t0)
+    s = sum(times) / len(times)
+    total = tp * algorithmic_bytes(w["rows"], hl, 2)
+    value = total / s / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": tp, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(s * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": w["name"], "hidden": w["hidden"], "rows": w["rows"], "tp": tp,
+                   "local_hidden": hl, "eps": w["eps"], "device": "cpu"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} full calls, all {tp} ranks' slices of "
+                                   f"{w['rows']}x{w['hidden']} bf16 in one process (torch CPU)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- our arm
+def setup_group(world, local):
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+        return dist.group.WORLD
+    return None
+
+
+def max_over_ranks(values, world):
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def make_rotating_sets(rows, hl, dtype, seed, min_bytes):
+    """Enough (x, out) pairs that one pass over them moves more than `min_bytes`."""
+    from rmsnorm_tp_b200.workloads import make_slice
+
+    elem = torch.tensor([], dtype=dtype).element_size()
+    per = 2 * rows * hl * elem
+    n = max(2, math.ceil(min_bytes / per))
+    xs, outs = [], []
+    w = None
+    for i in range(n):
+        x, wi = make_slice(rows, hl, dtype, seed + 7919 * i, device="cuda")
+        xs.append(x)
+        outs.append(torch.empty_like(x))
+        if w is None:
+            w = wi
+    return xs, w, outs
+
+
+def time_steps(fn, steps, per_launch_events=True):
+    """CUDA-event timing on the current stream: total ms and mean ms between
+    per-step event pairs (the kernel's own duration when a step is one launch)."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)] if per_launch_events else []
+    start.record()
+    for i in range(steps):
+        if per_launch_events:
+            evs[i][0].record()
+        fn(i)
+        if per_launch_events:
+            evs[i][1].record()
+    end.record()
+    torch.cuda.synchronize()
+    total = start.elapsed_time(end)
+    per = (sum(a.elapsed_time(b) for a, b in evs) / steps) if evs else total / steps
+    return total, per
+
+
+def run_our_arm(args):
+    import rmsnorm_tp_b200 as rtp
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    group = setup_group(world, local)
+    dev = torch.device("cuda", local)
+    w = WORKLOAD
+    tp = world
+    hl = w["hidden"] // tp
+    rows = w["rows"]
+    elem = 2
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    module = rtp.FusedTPRMSNorm(w["hidden"], eps=w["eps"], tp_group=group, num_max_rows=rows)
+    xs, wt, outs = make_rotating_sets(rows, hl, w["dtype"], w["seed_base"] + rank, 3 * l2)
+    nsets = len(xs)
+    set_bytes = 2 * rows * hl * elem
+
+    uuids = [gpu_uuid(dev)]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, uuids[0])
+        uuids = gathered
+    sampler = ClockSampler([u for u in uuids if u]) if rank == 0 else None
+
+    def step(i):
+        module.forward(xs[i % nsets], wt, out=outs[i % nsets])
+
+    # ---- device-timed region (the `value`)
+    if sampler:
+        sampler.start()
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    total_ms, kernel_ms = time_steps(step, args.steps)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    total_ms, kernel_ms = max_over_ranks([total_ms, kernel_ms], world)
+    ms_per_step = total_ms / args.steps
+    bytes_rank = algorithmic_bytes(rows, hl, elem)
+    value = tp * bytes_rank / (ms_per_step * 1e-3) / 1e9
+
+    # ---- the same steps replayed from a CUDA graph (no host launch cost)
+    graph_ms = None
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        n_cap = nsets * max(1, 64 // nsets)
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n_cap):
+                step(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        reps = max(1, args.steps // n_cap)
+        g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        graph_ms = max_over_ranks([e0.elapsed_time(e1) / (reps * n_cap)], world)[0]
+        del g
+    except Exception as exc:  # reported, not fatal
+        graph_ms = None
+        if rank == 0:
+            print(f"# graph replay skipped: {exc}", file=sys.stderr)
+
+    # ---- end to end through the public API with pinned host buffers
+    x_host = xs[0].cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(xs[0])
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step(_i):
+        x_dev.copy_(x_host, non_blocking=True)
+        y = module.forward(x_dev, wt)
+        y_host.copy_(y, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_total, _ = time_steps(e2e_step, e2e_steps, per_launch_events=False)
+    e2e_total = max_over_ranks([e2e_total], world)[0]
+    e2e_ms = e2e_total / e2e_steps
+    e2e_value = tp * bytes_rank / (e2e_ms * 1e-3) / 1e9
+
+    # ---- CPU baseline (rank 0, N = 1): the reference's CPU path on a bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        torch.set_num_threads(cores)
+        cx = [xs[0].cpu()]
+        cw = [wt.cpu()]
+        sec, n = cpu_reference_time(cx, cw, w["eps"], args.cpu_seconds)
+        cpu = {"value": round(bytes_rank / sec / 1e9, 3), "unit": "GB/s", "cores": cores,
+               "kind": "port", "ms_per_call": round(sec * 1e3, 3),
+               "sample": f"{n} full calls of {rows}x{hl} bf16 (TP=1), torch CPU, {cores} threads"}
+
+    peak, peak_kind = measured_peak_hbm()
+    achieved = bytes_rank / (kernel_ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                per_row = json.load(f)["bytes_per_row"][f"bf16_hl{hl}"]
+            traffic = int(per_row * rows)
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": w["name"], "hidden": w["hidden"], "rows": rows, "tp": tp,
+                       "local_hidden": hl, "eps": w["eps"], "parallelism": f"tp{tp}",
+                       "l2": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
+                             f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB L2)"},
+            "us_per_call": round(ms_per_step * 1e3, 3),
+            "kernel_us": round(kernel_ms * 1e3, 3),
+            "graph_us_per_call": round(graph_ms * 1e3, 3) if graph_ms else None,
+            "graph_value": round(tp * bytes_rank / (graph_ms * 1e-3) / 1e9, 2) if graph_ms else None,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_kind": peak_kind,
+                         "kernel": "tp_rmsnorm_vec_kernel" if tp > 0 else None,
+                         "bytes_per_launch": bytes_rank},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                    "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
+                    "ms_per_step": round(e2e_ms, 4), "path": "FusedTPRMSNorm.forward"},
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+    if args.sweep != "none":
+        run_sweeps(args, module, group, world, rank, dev)
+
+    module.destroy()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# --------------------------------------------------------------------------- sweeps
+def emit(args, rank, rec):
+    if rank != 0:
+        return
+    print(json.dumps(rec), flush=True)
+    if args.out:
+        with open(args.out, "a") as f:
+            f.write(json.dumps(rec) + "\n")
+
+
+def run_sweeps(args, module, group, world, rank, dev):
+    import rmsnorm_tp_b200 as rtp
+    from rmsnorm_tp_b200.workloads import BY_NAME, make_slice
+
+    tp = world
+    kinds = ["decode", "prefill", "llama"] if args.sweep == "all" else [args.sweep]
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+
+    def measure(mod, rows, hl, dtype, seed, steps, rotate=True):
+        elem = torch.tensor([], dtype=dtype).element_size()
+        if rotate:
+            xs, wt, outs = make_rotating_sets(rows, hl, dtype, seed, 3 * l2)
+        else:
+            x, wt = make_slice(rows, hl, dtype, seed, device="cuda")
+            xs, outs = [x], [torch.empty_like(x)]
+        n = len(xs)
+
+        def step(i):
+            mod.forward(xs[i % n], wt, out=outs[i % n])
+
+        for i in range(10):
+            step(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        total, per = time_steps(step, steps)
+        eager_us, kern_us = [v * 1e3 for v in max_over_ranks([total / steps, per], world)]
+        graph_us = None
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            ncap = max(n, 100)
+            with torch.cuda.graph(g, stream=s):
+                for i in range(ncap):
+                    step(i)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            reps = max(1, steps // ncap)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if world > 1:
+                dist.barrier()
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            graph_us = max_over_ranks([e0.elapsed_time(e1) * 1e3 / (reps * ncap)], world)[0]
+            del g
+        except Exception as exc:
+            if rank == 0:
+                print(f"# graph skipped: {exc}", file=sys.stderr)
+        b = algorithmic_bytes(rows, hl, elem)
+        return {"rows": rows, "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
+                "eager_us_per_call": round(eager_us, 3), "kernel_us": round(kern_us, 3),
+                "graph_us_per_call": round(graph_us, 3) if graph_us else None,
+                "kernel_GBps_per_rank": round(b / (kern_us * 1e-6) / 1e9, 1),
+                "graph_GBps_per_rank": round(b / (graph_us * 1e-6) / 1e9, 1) if graph_us else None,
+                "bytes_per_rank": b, "rotating_sets": n}
+
+    if "decode" in kinds:
+        cfg = BY_NAME["decode_llama70b"]
+        hl = cfg.hidden // tp
+        mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=256)
+        for rows in cfg.rows:
+            rec = measure(mod, rows, hl, cfg.dtype, cfg.seed_base + rank, 10000, rotate=False)
+            rec.update(sweep="decode", hidden=cfg.hidden)
+            emit(args, rank, rec)
+        if tp > 1 and mod.comm_buf is not None:
+            ns = probe_roundtrip(mod, rank, tp)
+            emit(args, rank, {"sweep": "decode", "probe": "one-hop store->poll round trip",
+                              "roundtrip_ns_rank0_rank1": ns, "one_hop_ns": ns / 2 if ns else None})
+        mod.destroy()
+    if "prefill" in kinds and tp > 1:
+        cfg = BY_NAME["prefill"]
+        hl = cfg.hidden // tp
+        mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=65536)
+        for dtype in (torch.bfloat16, torch.float16):
+            for rows in cfg.rows:
+                rec = measure(mod, rows, hl, dtype, cfg.seed_base + rank, 200)
+                rec.update(sweep="prefill", hidden=cfg.hidden)
+                emit(args, rank, rec)
+        mod.destroy()
+    if "llama" in kinds:
+        cfg = BY_NAME["llama3_8b"]
+        hl = cfg.hidden // tp
+        for rows in (1, 16, 128, 1024, 4096, 16384, 65536):
+            mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=rows)
+            rec = measure(mod, rows, hl, cfg.dtype, cfg.seed_base + rank, 1000 if rows <= 1024 else 200)
+            rec.update(sweep="llama", hidden=cfg.hidden)
+            emit(args, rank, rec)
+            mod.destroy()
+
+
+def probe_roundtrip(mod, rank, tp, iters=2000):
+    """Average store->poll round trip between ranks 0 and 1 (ns), or None."""
+    import ctypes
+
+    from rmsnorm_tp_b200._lib import LIB
+
+    out = torch.zeros(1, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    dist.barrier()
+    if rank in (0, 1):
+        peer = 1 - rank
+        rc = LIB.rmsnorm_tp_probe_roundtrip(mod.comm_buf._comm, peer, iters,
+                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                            ctypes.c_void_p(out.data_ptr()))
+        if rc != 0:
+            return None
+    torch.cuda.synchronize()
+    dist.barrier()
+    v = int(out.item())
+    return v if rank == 0 and v > 0 else (None if rank == 0 else v)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_our_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,205 @@
+/*
+ * rmsnorm_tp_b200 -- C ABI of the B200-native fused tensor-parallel RMSNorm.
+ *
+ * Drop-in native boundary for the reference's pybind11 module `rmsnorm_tp_cpp`
+ * (haowen-han/RmsnormTP, csrc/bindings.cpp:150-197). Plain pointers, sizes and
+ * integer status codes only: no torch or C++ types cross this boundary, and no
+ * C++ exception escapes it. Every function returns RMSNORM_TP_OK (0) or an
+ * rmsnorm_tp_error code; rmsnorm_tp_last_error() gives the message of the last
+ * failure on the calling thread.
+ *
+ * Threading: one host thread drives one communicator. rmsnorm_tp_forward is a
+ * collective: every rank of the TP group calls it the same number of times, in
+ * the same order, with the same number of rows (the reference's implicit
+ * contract, rmsnorm_tp/__init__.py:87-131).
+ *
+ * Data layout: x and out are [rows, local_hidden] row-major, weight is
+ * [local_hidden], all of one dtype, on the communicator's device. The fast
+ * kernels need 16-byte aligned x/out/weight and local_hidden * sizeof(dtype)
+ * a multiple of 16; other shapes run a slower generic kernel (still on the GPU).
+ */
+#ifndef RMSNORM_TP_B200_H_
+#define RMSNORM_TP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RMSNORM_TP_MAX_TP 8          /* reference csrc/common.hpp:9 (MAX_TP_SIZE) */
+#define RMSNORM_TP_HANDLE_BYTES 128  /* reference csrc/common.hpp:10 (HANDLE_SIZE) */
+
+/* Element types of x, weight and out. */
+enum rmsnorm_tp_dtype {
+  RMSNORM_TP_F32 = 0,   /* the only type the reference supports (__init__.py:96-97) */
+  RMSNORM_TP_BF16 = 1,
+  RMSNORM_TP_F16 = 2
+};
+
+/* Host-side status codes returned by every function. */
+enum rmsnorm_tp_error {
+  RMSNORM_TP_OK = 0,
+  RMSNORM_TP_ERR_INVALID = 1,  /* bad argument (null pointer, size, dtype, rank) */
+  RMSNORM_TP_ERR_CUDA = 2,     /* a CUDA runtime call failed */
+  RMSNORM_TP_ERR_STATE = 3,    /* call out of order (not finalized, peer missing) */
+  RMSNORM_TP_ERR_ROWS = 4,     /* rows > num_max_rows (reference __init__.py:109 assert) */
+  RMSNORM_TP_ERR_DEVICE = 5,   /* an earlier launch recorded a device-side failure
+                                  (a peer's partial sum never arrived); call
+                                  rmsnorm_tp_reset on every rank */
+  RMSNORM_TP_ERR_HANDLE = 6    /* peer handle bytes malformed or from another group */
+};
+
+/* Device-side failure codes (rmsnorm_tp_status_info.code). */
+enum rmsnorm_tp_device_status {
+  RMSNORM_TP_STATUS_OK = 0,
+  RMSNORM_TP_STATUS_TIMEOUT = 1,  /* a wait for a peer's partial sum ran out */
+  RMSNORM_TP_STATUS_ABORTED = 2   /* gave up because another CTA timed out */
+};
+
+typedef struct rmsnorm_tp_comm rmsnorm_tp_comm;
+
+typedef struct rmsnorm_tp_status_info {
+  uint32_t code;          /* rmsnorm_tp_device_status */
+  uint32_t src_rank;      /* rank whose partial sum did not arrive */
+  int64_t row;            /* row that timed out */
+  uint32_t expected_tag;  /* tag that was awaited */
+  uint32_t seen_tag;      /* tag found in the slot when the wait ended */
+  uint64_t generation;    /* call number of the failing launch */
+  uint64_t next_generation; /* device generation counter now */
+} rmsnorm_tp_status_info;
+
+typedef struct rmsnorm_tp_plan_info {
+  int32_t variant;        /* -1 = generic kernel */
+  int32_t vec_per_lane;
+  int32_t team_warps;
+  int32_t rows_per_tile;
+  int32_t block_threads;
+  int32_t teams_per_cta;
+  int64_t tiles;
+  int32_t grid;
+  int32_t reserved;
+} rmsnorm_tp_plan_info;
+
+/* ---- communicator lifecycle -------------------------------------------- */
+
+/* Allocate this rank's mailbox (zeroed) and device state on `device`.
+ * Replaces CommBuffer(rank, tp_size, num_max_rows) + allocate()
+ * (reference csrc/bindings.cpp:20-53, rmsnorm_tp/__init__.py:67-68). */
+int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
+                      rmsnorm_tp_comm** out);
+
+/* Serialise this rank's mailbox handle into RMSNORM_TP_HANDLE_BYTES bytes.
+ * Replaces get_ipc_handle() + IpcHandle.to_bytes()
+ * (reference csrc/bindings.cpp:55-61, :154-156). */
+int rmsnorm_tp_export_handle(const rmsnorm_tp_comm* comm, void* out, size_t cap,
+                             size_t* len);
+
+/* Map peer `peer`'s mailbox from its exported handle bytes (validated).
+ * Replaces IpcHandle.from_bytes() + open_remote_handle()
+ * (reference csrc/bindings.cpp:157-162, :63-77). */
+int rmsnorm_tp_open_peer(rmsnorm_tp_comm* comm, int peer, const void* bytes,
+                         size_t len);
+
+/* Use an already-mapped device pointer as peer `peer`'s mailbox (memory that
+ * the caller mapped itself, or a stand-in that no rank serves, for the
+ * bounded-wait test). No counterpart in the reference. */
+int rmsnorm_tp_attach_peer(rmsnorm_tp_comm* comm, int peer, void* mailbox);
+
+/* This rank's mailbox base and size in bytes. Analogue of the pointer-table
+ * getters sums_ptrs_gpu()/gen_ptrs_gpu() (reference csrc/bindings.cpp:171-176). */
+int rmsnorm_tp_mailbox(const rmsnorm_tp_comm* comm, void** ptr, size_t* bytes);
+
+/* Check that every peer is mapped and wait for set-up work on the device.
+ * Replaces finalize_setup() (reference csrc/bindings.cpp:79-82). */
+int rmsnorm_tp_finalize(rmsnorm_tp_comm* comm);
+
+/* Close peer mappings and free. Call only after every rank has stopped
+ * launching (the Python layer puts a barrier first; the reference has none,
+ * csrc/bindings.cpp:84-99). Accepts NULL. */
+int rmsnorm_tp_destroy(rmsnorm_tp_comm* comm);
+
+/* ---- hot path ------------------------------------------------------------ */
+
+/* out = x * rsqrt(S / hidden + eps) * weight, S = sum over the TP group of the
+ * fp32 sum of squares of the row. One kernel: load, reduce, push the partial to
+ * every peer's mailbox, poll the local mailbox, normalise. Stream-ordered on
+ * `stream` (a cudaStream_t; NULL = legacy default). The generation is
+ * device-resident, so the launch can be captured in a CUDA graph.
+ * Replaces launch_fused_rmsnorm (reference csrc/rmsnorm_tp.cu:184-207,
+ * csrc/bindings.cpp:182-196), whose `generation` argument is dropped. */
+int rmsnorm_tp_forward(rmsnorm_tp_comm* comm, void* out, const void* x,
+                       const void* weight, int64_t rows, int64_t local_hidden,
+                       int64_t hidden, int dtype, float eps, void* stream);
+
+/* TP = 1: local RMSNorm, no communicator. Replaces the eager torch path of
+ * FusedTPRMSNorm.forward at tp_size == 1 (reference rmsnorm_tp/__init__.py:103-107). */
+int rmsnorm_local_forward(void* out, const void* x, const void* weight,
+                          int64_t rows, int64_t hidden, int dtype, float eps,
+                          void* stream);
+
+/* ---- failure detection and recovery (no reference counterpart) ---------- */
+
+/* Limit on each wait for a peer's partial sum, in nanoseconds (default
+ * 10 s, or RMSNORM_TP_TIMEOUT_MS from the environment at create time). */
+int rmsnorm_tp_set_timeout(rmsnorm_tp_comm* comm, uint64_t timeout_ns);
+
+/* Non-blocking: nonzero in *code once a launch has recorded a device failure
+ * (reads host-mapped memory the kernel writes; no CUDA call). */
+int rmsnorm_tp_poll_error(const rmsnorm_tp_comm* comm, uint32_t* code);
+
+/* Blocking: synchronise the device and read the full failure record. */
+int rmsnorm_tp_status(rmsnorm_tp_comm* comm, rmsnorm_tp_status_info* out);
+
+/* Blocking: wait for the device, zero the mailbox, clear the failure record
+ * and set the generation counter to `generation`. Every rank must call it
+ * between two group barriers, with the same generation. */
+int rmsnorm_tp_reset(rmsnorm_tp_comm* comm, uint64_t generation);
+
+/* Blocking: read the device generation counter (launches completed). */
+int rmsnorm_tp_get_generation(rmsnorm_tp_comm* comm, uint64_t* out);
+
+/* ---- test and measurement helpers (no reference counterpart) ----------- */
+
+/* Run all `tp` ranks of a group on ONE GPU in one cooperative launch
+ * (grid.y = rank), so the push/poll protocol can be checked without several
+ * GPUs. comms[r] must be rank r of a group whose peers were attached with
+ * rmsnorm_tp_attach_peer to each other's mailboxes. */
+int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp,
+                                void* const* outs, const void* const* xs,
+                                const void* const* weights, int64_t rows,
+                                int64_t local_hidden, int dtype, float eps,
+                                void* stream);
+
+/* One-hop NVLink latency probe between this rank and `peer`: `iters` round
+ * trips of a store into the peer's mailbox and a poll of the local one. Both
+ * ranks call it at the same time; the lower rank starts. Writes the average
+ * round-trip time in ns to *dev_out_ns (device memory). Bounded waits. */
+int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
+                               void* stream, int64_t* dev_out_ns);
+
+/* The launch plan the forward call would use (pure host arithmetic; no GPU). */
+int rmsnorm_tp_plan(int64_t rows, int64_t local_hidden, int dtype, int aligned,
+                    int resident_ctas, rmsnorm_tp_plan_info* out);
+
+/* Count, for every row, how many teams of `plan` visit it (coverage check of
+ * the row -> team mapping the kernels use; host only). counts has `rows` slots. */
+int rmsnorm_tp_plan_coverage(const rmsnorm_tp_plan_info* plan, int64_t rows,
+                             int32_t* counts);
+
+/* Generation arithmetic the kernels use (host copies, for tests). */
+uint32_t rmsnorm_tp_tag_of(uint64_t generation);
+uint32_t rmsnorm_tp_buffer_of(uint64_t generation);
+
+/* Message of the last failure on this thread ("" if none). */
+const char* rmsnorm_tp_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+int rmsnorm_tp_abi_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* RMSNORM_TP_B200_H_ */

@@ -1,0 +1,49 @@
+"""torch-CPU port of the reference's AllReduce TP RMSNorm (test oracle / CPU baseline).
+
+The reference path (bench_rmsnorm_tp.py:16-22) is a handful of torch ops around
+an all_reduce; this module restates those ops so they can run where the
+reference cannot travel:
+
+* ``allreduce_path_group`` -- one process holds every rank's slice and the
+  all_reduce becomes an in-process sum in rank order (what bench.py times as
+  the CPU baseline, with all host threads);
+* ``allreduce_path_dist`` -- one slice per process, the all_reduce done by
+  torch.distributed (gloo on CPU in the multi-process tests).
+
+The steps must match the reference's op for op (x.pow(2) in x's dtype, mean
+with dtype=float32, SUM then divide by tp, x * rsqrt(v + eps) * w), because
+that arithmetic is what parity is measured against.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def _local_variance(x: torch.Tensor) -> torch.Tensor:
+    # bench_rmsnorm_tp.py:18
+    return x.pow(2).mean(dim=-1, keepdim=True, dtype=torch.float32)
+
+
+def allreduce_path_group(xs: Sequence[torch.Tensor], ws: Sequence[torch.Tensor],
+                         eps: float) -> List[torch.Tensor]:
+    """Every rank's output of the AllReduce path, computed in one process."""
+    tp = len(xs)
+    total = _local_variance(xs[0])
+    for x in xs[1:]:
+        total = total + _local_variance(x)           # all_reduce SUM (:20)
+    variance = total / tp if tp > 1 else total      # (:21)
+    inv = torch.rsqrt(variance + eps)               # (:22)
+    return [x * inv * w for x, w in zip(xs, ws)]
+
+
+def allreduce_path_dist(x: torch.Tensor, w: torch.Tensor, eps: float, group=None) -> torch.Tensor:
+    """This rank's output of the AllReduce path, the all_reduce done by torch.distributed."""
+    tp = dist.get_world_size(group)
+    variance = _local_variance(x)
+    if tp > 1:
+        dist.all_reduce(variance, op=dist.ReduceOp.SUM, group=group)   # (:20)
+        variance = variance / tp                                       # (:21)
+    return x * torch.rsqrt(variance + eps) * w                         # (:22)

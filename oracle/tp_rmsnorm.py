@@ -1,0 +1,164 @@
+"""numpy restatement of the reference's tensor-parallel RMSNorm (test oracle).
+
+Two functions, both taking every rank's slice at once:
+
+``allreduce_path`` follows the reference's AllReduce path,
+bench_rmsnorm_tp.py:16-22 (identical to test_rmsnorm_tp.py:15-26):
+    variance_k = mean over the local slice of x_k.pow(2)   (:18; the square is
+                 rounded to x's dtype, the mean accumulates in fp32)
+    variance   = (sum_k variance_k) / tp                    (:19-21, all_reduce SUM)
+    y_k        = x_k * rsqrt(variance + eps) * w_k          (:22, fp32 result)
+
+``fused_path`` follows the reference's fused kernel, csrc/rmsnorm_tp.cu:
+    s_k        = sum of fp32 squares of the local slice     (:72-96)
+    S          = s_0 + ... + s_{tp-1}                       (:143-151)
+    inv        = rsqrt(S / hidden + eps)                    (:156-157)
+    y_k        = (x_k * inv) * w_k                          (:162-170)
+which is what the CUDA kernels of this repository compute (in bf16/fp16 too).
+
+Arrays: fp32 values are np.float32; bf16 values are carried as np.uint16 bit
+patterns; fp16 values as np.float16. Sums are taken in float64 and rounded to
+fp32 once, which is within an ulp or two of torch's fp32 reductions.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import numpy as np
+
+DTYPES = ("f32", "bf16", "f16")
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns (uint16) -> float32 (exact)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bf16 bit patterns, round to nearest even; NaN stays a quiet NaN."""
+    u = np.asarray(x, dtype=np.float32).view(np.uint32)
+    rounded = ((u + (np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1)))) >> 16).astype(np.uint16)
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    return np.where(nan, ((u >> 16) | np.uint32(0x40)).astype(np.uint16), rounded)
+
+
+def to_f32(dtype: str, a: np.ndarray) -> np.ndarray:
+    """Stored array of `dtype` -> float32 values."""
+    if dtype == "f32":
+        return np.asarray(a, dtype=np.float32)
+    if dtype == "bf16":
+        return bf16_bits_to_f32(a)
+    if dtype == "f16":
+        return np.asarray(a, dtype=np.float16).astype(np.float32)
+    raise ValueError(f"unknown dtype {dtype}")
+
+
+def from_f32(dtype: str, a: np.ndarray) -> np.ndarray:
+    """float32 values -> stored array of `dtype` (round to nearest even)."""
+    a = np.asarray(a, dtype=np.float32)
+    if dtype == "f32":
+        return a
+    if dtype == "bf16":
+        return f32_to_bf16_bits(a)
+    if dtype == "f16":
+        return a.astype(np.float16)
+    raise ValueError(f"unknown dtype {dtype}")
+
+
+def round_to(dtype: str, a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the grid of `dtype`, returned as float32."""
+    return to_f32(dtype, from_f32(dtype, a))
+
+
+def _rsqrt_f32(v: np.ndarray) -> np.ndarray:
+    with np.errstate(divide="ignore", invalid="ignore"):
+        return (1.0 / np.sqrt(np.asarray(v, dtype=np.float64))).astype(np.float32)
+
+
+def allreduce_path(xs: Sequence[np.ndarray], ws: Sequence[np.ndarray], eps: float,
+                   dtype: str) -> List[np.ndarray]:
+    """Reference AllReduce TP RMSNorm (bench_rmsnorm_tp.py:16-22) over all ranks.
+
+    Returns each rank's fp32 output (the reference returns fp32 for bf16/fp16
+    inputs because x * rsqrt(fp32) promotes); round with ``from_f32`` to compare
+    with an output in x's dtype.
+    """
+    tp = len(xs)
+    variances = []
+    for x in xs:
+        xf = to_f32(dtype, x)
+        with np.errstate(over="ignore"):
+            sq = round_to(dtype, xf * xf)                        # x.pow(2) in x.dtype (:18)
+        hl = xf.shape[-1]
+        mean = (sq.astype(np.float64).sum(axis=-1, keepdims=True) / hl).astype(np.float32)
+        variances.append(mean)                                   # mean(dtype=float32) (:18)
+    total = variances[0].copy()
+    for v in variances[1:]:
+        total = (total + v).astype(np.float32)                   # all_reduce SUM (:20)
+    variance = (total / np.float32(tp)).astype(np.float32) if tp > 1 else total   # (:21)
+    inv = _rsqrt_f32((variance + np.float32(eps)).astype(np.float32))            # (:22)
+    outs = []
+    for x, w in zip(xs, ws):
+        xf = to_f32(dtype, x)
+        wf = to_f32(dtype, w)
+        outs.append(((xf * inv).astype(np.float32) * wf).astype(np.float32))    # (:22)
+    return outs
+
+
+def partial_sums(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Per-row fp32 sum of squares of one rank's slice (rmsnorm_tp.cu:72-96)."""
+    xf = to_f32(dtype, x).astype(np.float64)
+    return (xf * xf).sum(axis=-1).astype(np.float32)
+
+
+def fused_path(xs: Sequence[np.ndarray], ws: Sequence[np.ndarray], eps: float,
+               dtype: str) -> List[np.ndarray]:
+    """Reference fused-kernel formula (rmsnorm_tp.cu:143-170), any dtype, fp32 math.
+
+    Returns each rank's fp32 output before the final rounding to x's dtype.
+    """
+    tp = len(xs)
+    hidden = xs[0].shape[-1] * tp                                # total_hidden (__init__.py:101)
+    S = partial_sums(xs[0], dtype)
+    for x in xs[1:]:
+        S = (S + partial_sums(x, dtype)).astype(np.float32)      # rank order (:145-148)
+    var = (S / np.float32(hidden)).astype(np.float32)            # (:156)
+    inv = _rsqrt_f32((var + np.float32(eps)).astype(np.float32))[..., None]   # (:157)
+    outs = []
+    for x, w in zip(xs, ws):
+        xf = to_f32(dtype, x)
+        wf = to_f32(dtype, w)
+        outs.append(((xf * inv).astype(np.float32) * wf).astype(np.float32))  # (:166-169)
+    return outs
+
+
+# Tolerances of the parity bar: fp32 relative 1e-5; bf16/fp16 one ulp of the
+# output type (atol 1e-2, rtol 1.6e-2).
+TOLERANCE = {
+    "f32": dict(rtol=1e-5, atol=1e-6),
+    "bf16": dict(rtol=1.6e-2, atol=1e-2),
+    "f16": dict(rtol=1.6e-2, atol=1e-2),
+}
+
+
+def compare(dtype: str, got_f32: np.ndarray, want_f32: np.ndarray) -> dict:
+    """Compare two outputs (float32 arrays) against the tolerance of `dtype`.
+
+    Returns {"ok", "max_abs", "max_rel", "bad"} where ``bad`` counts elements
+    outside ``atol + rtol * |want|`` (NaN mismatches included).
+    """
+    tol = TOLERANCE[dtype]
+    got = np.asarray(got_f32, dtype=np.float64)
+    want = np.asarray(want_f32, dtype=np.float64)
+    diff = np.abs(got - want)
+    nan_mismatch = np.isnan(got) != np.isnan(want)
+    both_nan = np.isnan(got) & np.isnan(want)
+    diff = np.where(both_nan, 0.0, diff)
+    bad = (diff > tol["atol"] + tol["rtol"] * np.abs(want)) | nan_mismatch
+    rel = diff / np.maximum(np.abs(want), 1e-30)
+    return {
+        "ok": not bool(bad.any()),
+        "max_abs": float(np.nanmax(diff)) if diff.size else 0.0,
+        "max_rel": float(np.nanmax(np.where(np.abs(want) > 1e-3, rel, 0.0))) if diff.size else 0.0,
+        "bad": int(bad.sum()),
+    }

@@ -1,0 +1,38 @@
+"""B200-native fused tensor-parallel RMSNorm.
+
+Drop-in for the reference package ``rmsnorm_tp`` (haowen-han/RmsnormTP):
+``FusedTPRMSNorm(hidden_dim, eps, tp_group, num_max_rows).forward(x, weight)``
+and ``destroy()``. The compute runs in the C-ABI library
+``_C/librmsnorm_tp_b200.so`` (hand-written sm_100a kernels); importing this
+package fails if that library has not been built.
+"""
+from ._lib import RMSNormTPDeviceError, RMSNormTPError
+from .api import (
+    EmulatedTPGroup,
+    exchange_handles,
+    FusedTPRMSNorm,
+    IpcHandle,
+    TPCommBuffer,
+    buffer_of,
+    dtype_code,
+    local_rmsnorm,
+    plan,
+    plan_coverage,
+    tag_of,
+)
+
+__all__ = [
+    "FusedTPRMSNorm",
+    "TPCommBuffer",
+    "IpcHandle",
+    "EmulatedTPGroup",
+    "exchange_handles",
+    "local_rmsnorm",
+    "RMSNormTPError",
+    "RMSNormTPDeviceError",
+    "plan",
+    "plan_coverage",
+    "tag_of",
+    "buffer_of",
+    "dtype_code",
+]

@@ -1,0 +1,552 @@
+// C-ABI host side of the fused TP RMSNorm: communicator (mailbox + peer
+// mappings), launch entry points, failure record, recovery.
+//
+// Replaces the reference's pybind11 CommBuffer / IpcHandle / launch binding
+// (csrc/bindings.cpp:18-197, csrc/common.hpp:1-18). Differences that matter:
+//   * the mailbox is u64 slot[2][tp][num_max_rows] (partial sum and tag in one
+//     word, two generation buffers, rows strided by num_max_rows);
+//   * the generation lives on the device and is advanced by the kernel itself;
+//   * peer pointers travel as kernel parameters (constant bank), not as a
+//     device pointer table that the kernel must load first;
+//   * handle bytes carry a magic, version, group shape and device UUID, checked
+//     on open;
+//   * errors come back as status codes plus a thread-local message, never as
+//     exceptions, and launch errors are checked (the reference does not check,
+//     csrc/rmsnorm_tp.cu:203-206).
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/rmsnorm_tp_b200.h"
+#include "internal.h"
+#include "rtp_common.h"
+
+using rtp::DeviceState;
+using rtp::KArgs;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(RMSNORM_TP_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define RTP_CUDA(call, what)                 \
+  do {                                       \
+    cudaError_t e_ = (call);                 \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// Makes `device` current for the scope, restoring the caller's device after.
+struct DeviceGuard {
+  int prev = -1;
+  bool switched = false;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceGuard(int device) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != device) {
+      err = cudaSetDevice(device);
+      switched = (err == cudaSuccess);
+    }
+  }
+  ~DeviceGuard() {
+    if (switched) cudaSetDevice(prev);
+  }
+};
+
+// Serialised mailbox handle: same size as the reference's IpcHandle bytes
+// (common.hpp:13-16, bindings.cpp:154-162), with metadata checked on open.
+struct HandleBytes {
+  cudaIpcMemHandle_t ipc;       // 64 bytes
+  uint32_t magic;
+  uint32_t version;
+  int32_t rank;
+  int32_t tp;
+  int64_t nmax;
+  uint64_t mailbox_bytes;
+  unsigned char uuid[16];
+  unsigned char reserved[16];
+};
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t is 64 bytes");
+static_assert(sizeof(HandleBytes) == rtp::kHandleBytes, "handle is 128 bytes");
+
+constexpr size_t kProbeBytes = 256;   // after the slots: one probe word per source rank
+constexpr unsigned long long kDefaultTimeoutNs = 10ull * 1000ull * 1000ull * 1000ull;
+
+size_t slots_bytes(int tp, int64_t nmax) {
+  size_t b = (size_t)rtp::mailbox_slots(tp, nmax) * sizeof(unsigned long long);
+  return (b + 255) & ~(size_t)255;
+}
+
+bool valid_dtype(int dtype) { return dtype >= RMSNORM_TP_F32 && dtype <= RMSNORM_TP_F16; }
+
+}  // namespace
+
+struct rmsnorm_tp_comm {
+  int rank = 0;
+  int tp = 1;
+  int device = 0;
+  int64_t nmax = 0;
+  unsigned long long* mailbox = nullptr;   // local, cudaMalloc'd (IPC-exportable)
+  size_t mailbox_bytes = 0;
+  unsigned long long* peers[rtp::kMaxTP] = {};
+  bool opened[rtp::kMaxTP] = {};           // mapped with cudaIpcOpenMemHandle (must be closed)
+  DeviceState* state = nullptr;            // local device memory
+  unsigned int* host_flag = nullptr;       // pinned host memory, mapped
+  unsigned int* host_flag_dev = nullptr;   // its device alias
+  unsigned long long timeout_ns = kDefaultTimeoutNs;
+  bool finalized = false;
+  unsigned long long probe_seq = 0;
+  unsigned char uuid[16] = {};
+};
+
+static void release(rmsnorm_tp_comm* c) {
+  for (int q = 0; q < rtp::kMaxTP; ++q) {
+    if (c->opened[q] && c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
+    c->opened[q] = false;
+    c->peers[q] = nullptr;
+  }
+  if (c->mailbox) cudaFree(c->mailbox);
+  if (c->state) cudaFree(c->state);
+  if (c->host_flag) cudaFreeHost(c->host_flag);
+  c->mailbox = nullptr;
+  c->state = nullptr;
+  c->host_flag = nullptr;
+  c->host_flag_dev = nullptr;
+}
+
+extern "C" {
+
+const char* rmsnorm_tp_last_error(void) { return g_last_error.c_str(); }
+
+int rmsnorm_tp_abi_version(void) { return 100; }
+
+uint32_t rmsnorm_tp_tag_of(uint64_t generation) { return rtp::tag_of(generation); }
+uint32_t rmsnorm_tp_buffer_of(uint64_t generation) { return rtp::buffer_of(generation); }
+
+int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
+                      rmsnorm_tp_comm** out) {
+  if (!out) return fail(RMSNORM_TP_ERR_INVALID, "create: out is NULL");
+  *out = nullptr;
+  if (tp_size < 1 || tp_size > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "create: tp_size %d outside [1, %d]", tp_size, rtp::kMaxTP);
+  if (rank < 0 || rank >= tp_size)
+    return fail(RMSNORM_TP_ERR_INVALID, "create: rank %d outside [0, %d)", rank, tp_size);
+  if (num_max_rows < 1 || num_max_rows > (int64_t(1) << 31))
+    return fail(RMSNORM_TP_ERR_INVALID, "create: num_max_rows %lld outside [1, 2^31]",
+                (long long)num_max_rows);
+  int ndev = 0;
+  RTP_CUDA(cudaGetDeviceCount(&ndev), "create: cudaGetDeviceCount");
+  if (device < 0 || device >= ndev)
+    return fail(RMSNORM_TP_ERR_INVALID, "create: device %d outside [0, %d)", device, ndev);
+
+  DeviceGuard guard(device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "create: cudaSetDevice");
+
+  rmsnorm_tp_comm* c = new (std::nothrow) rmsnorm_tp_comm();
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "create: out of host memory");
+  c->rank = rank;
+  c->tp = tp_size;
+  c->device = device;
+  c->nmax = num_max_rows;
+  c->mailbox_bytes = slots_bytes(tp_size, num_max_rows) + kProbeBytes;
+  if (const char* env = std::getenv("RMSNORM_TP_TIMEOUT_MS")) {
+    const long long ms = std::atoll(env);
+    if (ms > 0) c->timeout_ns = (unsigned long long)ms * 1000000ull;
+  }
+
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->mailbox), c->mailbox_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->mailbox, 0, c->mailbox_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->state), sizeof(DeviceState));
+  if (e == cudaSuccess) e = cudaMemset(c->state, 0, sizeof(DeviceState));
+  if (e == cudaSuccess)
+    e = cudaHostAlloc(reinterpret_cast<void**>(&c->host_flag), 256,
+                      cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e == cudaSuccess) {
+    std::memset(c->host_flag, 0, 256);
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->host_flag_dev), c->host_flag, 0);
+  }
+  cudaDeviceProp prop;
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, device);
+  if (e == cudaSuccess) std::memcpy(c->uuid, prop.uuid.bytes, 16);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();   // zeroed before any peer can map it
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(e, "create: allocation");
+    release(c);
+    delete c;
+    return rc;
+  }
+  c->peers[rank] = c->mailbox;
+  *out = c;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_export_handle(const rmsnorm_tp_comm* c, void* out, size_t cap, size_t* len) {
+  if (!c || !out) return fail(RMSNORM_TP_ERR_INVALID, "export_handle: NULL argument");
+  if (cap < sizeof(HandleBytes))
+    return fail(RMSNORM_TP_ERR_INVALID, "export_handle: buffer of %zu bytes < %zu", cap,
+                sizeof(HandleBytes));
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "export_handle: cudaSetDevice");
+  HandleBytes h;
+  std::memset(&h, 0, sizeof(h));
+  RTP_CUDA(cudaIpcGetMemHandle(&h.ipc, c->mailbox), "export_handle: cudaIpcGetMemHandle");
+  h.magic = rtp::kHandleMagic;
+  h.version = rtp::kHandleVersion;
+  h.rank = c->rank;
+  h.tp = c->tp;
+  h.nmax = c->nmax;
+  h.mailbox_bytes = c->mailbox_bytes;
+  std::memcpy(h.uuid, c->uuid, 16);
+  std::memcpy(out, &h, sizeof(h));
+  if (len) *len = sizeof(h);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_open_peer(rmsnorm_tp_comm* c, int peer, const void* bytes, size_t len) {
+  if (!c || !bytes) return fail(RMSNORM_TP_ERR_INVALID, "open_peer: NULL argument");
+  if (peer < 0 || peer >= c->tp || peer == c->rank)
+    return fail(RMSNORM_TP_ERR_INVALID, "open_peer: peer %d invalid for rank %d of %d", peer,
+                c->rank, c->tp);
+  if (len != sizeof(HandleBytes))
+    return fail(RMSNORM_TP_ERR_HANDLE, "open_peer: handle is %zu bytes, expected %zu", len,
+                sizeof(HandleBytes));
+  if (c->peers[peer])
+    return fail(RMSNORM_TP_ERR_STATE, "open_peer: peer %d already mapped", peer);
+  HandleBytes h;
+  std::memcpy(&h, bytes, sizeof(h));
+  if (h.magic != rtp::kHandleMagic || h.version != rtp::kHandleVersion)
+    return fail(RMSNORM_TP_ERR_HANDLE, "open_peer: not a mailbox handle (magic %08x version %u)",
+                h.magic, h.version);
+  if (h.rank != peer || h.tp != c->tp || h.nmax != c->nmax || h.mailbox_bytes != c->mailbox_bytes)
+    return fail(RMSNORM_TP_ERR_HANDLE,
+                "open_peer: handle of rank %d (tp %d, num_max_rows %lld) does not match peer %d "
+                "(tp %d, num_max_rows %lld)",
+                h.rank, h.tp, (long long)h.nmax, peer, c->tp, (long long)c->nmax);
+  if (std::memcmp(h.uuid, c->uuid, 16) == 0)
+    return fail(RMSNORM_TP_ERR_HANDLE,
+                "open_peer: peer %d is on this rank's GPU; one GPU per rank is required", peer);
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "open_peer: cudaSetDevice");
+  void* p = nullptr;
+  RTP_CUDA(cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess),
+           "open_peer: cudaIpcOpenMemHandle");
+  c->peers[peer] = reinterpret_cast<unsigned long long*>(p);
+  c->opened[peer] = true;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_attach_peer(rmsnorm_tp_comm* c, int peer, void* mailbox) {
+  if (!c || !mailbox) return fail(RMSNORM_TP_ERR_INVALID, "attach_peer: NULL argument");
+  if (peer < 0 || peer >= c->tp || peer == c->rank)
+    return fail(RMSNORM_TP_ERR_INVALID, "attach_peer: peer %d invalid for rank %d of %d", peer,
+                c->rank, c->tp);
+  if (reinterpret_cast<uintptr_t>(mailbox) & 7u)
+    return fail(RMSNORM_TP_ERR_INVALID, "attach_peer: mailbox not 8-byte aligned");
+  if (c->peers[peer])
+    return fail(RMSNORM_TP_ERR_STATE, "attach_peer: peer %d already mapped", peer);
+  c->peers[peer] = reinterpret_cast<unsigned long long*>(mailbox);
+  c->opened[peer] = false;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_mailbox(const rmsnorm_tp_comm* c, void** ptr, size_t* bytes) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "mailbox: NULL communicator");
+  if (ptr) *ptr = c->mailbox;
+  if (bytes) *bytes = c->mailbox_bytes;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_finalize(rmsnorm_tp_comm* c) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "finalize: NULL communicator");
+  for (int q = 0; q < c->tp; ++q)
+    if (!c->peers[q]) return fail(RMSNORM_TP_ERR_STATE, "finalize: peer %d not mapped", q);
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "finalize: cudaSetDevice");
+  RTP_CUDA(cudaDeviceSynchronize(), "finalize: cudaDeviceSynchronize");
+  c->finalized = true;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_destroy(rmsnorm_tp_comm* c) {
+  if (!c) return RMSNORM_TP_OK;
+  int rc = RMSNORM_TP_OK;
+  {
+    DeviceGuard guard(c->device);
+    if (guard.err == cudaSuccess) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) rc = cuda_fail(e, "destroy: cudaDeviceSynchronize");
+    }
+    release(c);
+  }
+  delete c;
+  return rc;
+}
+
+int rmsnorm_tp_set_timeout(rmsnorm_tp_comm* c, uint64_t timeout_ns) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "set_timeout: NULL communicator");
+  if (timeout_ns == 0) return fail(RMSNORM_TP_ERR_INVALID, "set_timeout: timeout must be > 0");
+  c->timeout_ns = timeout_ns;
+  return RMSNORM_TP_OK;
+}
+
+static int check_shape(const char* who, int64_t rows, int64_t hl, int64_t hidden, int dtype,
+                       const void* out, const void* x, const void* w) {
+  if (!valid_dtype(dtype)) return fail(RMSNORM_TP_ERR_INVALID, "%s: unknown dtype %d", who, dtype);
+  if (rows < 0) return fail(RMSNORM_TP_ERR_INVALID, "%s: rows %lld < 0", who, (long long)rows);
+  if (hl < 1 || hl > (int64_t(1) << 31))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: local_hidden %lld outside [1, 2^31]", who,
+                (long long)hl);
+  if (hidden < hl)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: hidden %lld < local_hidden %lld", who,
+                (long long)hidden, (long long)hl);
+  if (rows > 0 && (!out || !x || !w))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL tensor pointer", who);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_forward(rmsnorm_tp_comm* c, void* out, const void* x, const void* w, int64_t rows,
+                       int64_t hl, int64_t hidden, int dtype, float eps, void* stream) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "forward: NULL communicator");
+  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "forward: communicator not finalized");
+  int rc = check_shape("forward", rows, hl, hidden, dtype, out, x, w);
+  if (rc != RMSNORM_TP_OK) return rc;
+  if (rows > c->nmax)
+    return fail(RMSNORM_TP_ERR_ROWS, "forward: rows %lld > num_max_rows %lld", (long long)rows,
+                (long long)c->nmax);
+  const unsigned flag = *reinterpret_cast<volatile unsigned*>(c->host_flag);
+  if (flag != 0u)
+    return fail(RMSNORM_TP_ERR_DEVICE,
+                "forward: an earlier launch recorded device failure %u (a peer's partial sum "
+                "never arrived); reset the communicator on every rank",
+                flag);
+  if (rows == 0) return RMSNORM_TP_OK;
+  KArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rp[0] = rtp::RankPtrs{out, x, w, c->state, c->host_flag_dev};
+  for (int q = 0; q < c->tp; ++q) a.mbox[q] = c->peers[q];
+  a.rows = rows;
+  a.hl = hl;
+  a.nmax = c->nmax;
+  a.hidden_f = (float)hidden;
+  a.eps = eps;
+  a.rank = c->rank;
+  a.tp = c->tp;
+  a.emulated = 0;
+  a.timeout_ns = c->timeout_ns;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  cudaError_t e;
+  if (cur == c->device) {
+    e = rtp::launch_forward(a, dtype, c->device, 1, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  } else {
+    DeviceGuard guard(c->device);
+    e = rtp::launch_forward(a, dtype, c->device, 1, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "forward: kernel launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_local_forward(void* out, const void* x, const void* w, int64_t rows, int64_t hidden,
+                          int dtype, float eps, void* stream) {
+  int rc = check_shape("local_forward", rows, hidden, hidden, dtype, out, x, w);
+  if (rc != RMSNORM_TP_OK) return rc;
+  if (rows == 0) return RMSNORM_TP_OK;
+  KArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rp[0] = rtp::RankPtrs{out, x, w, nullptr, nullptr};
+  a.rows = rows;
+  a.hl = hidden;
+  a.nmax = rows;
+  a.hidden_f = (float)hidden;
+  a.eps = eps;
+  a.rank = 0;
+  a.tp = 1;
+  int dev = 0;
+  RTP_CUDA(cudaGetDevice(&dev), "local_forward: cudaGetDevice");
+  cudaError_t e =
+      rtp::launch_forward(a, dtype, dev, 1, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  if (e != cudaSuccess) return cuda_fail(e, "local_forward: kernel launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
+                                const void* const* xs, const void* const* ws, int64_t rows,
+                                int64_t hl, int dtype, float eps, void* stream) {
+  if (!comms || !outs || !xs || !ws)
+    return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: NULL argument");
+  if (tp < 2 || tp > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: tp %d outside [2, %d]", tp, rtp::kMaxTP);
+  for (int r = 0; r < tp; ++r) {
+    const rmsnorm_tp_comm* c = comms[r];
+    if (!c) return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: comms[%d] is NULL", r);
+    if (c->rank != r || c->tp != tp || c->device != comms[0]->device || c->nmax != comms[0]->nmax)
+      return fail(RMSNORM_TP_ERR_INVALID,
+                  "forward_emulated: comms[%d] is rank %d of %d on device %d; expected rank %d of "
+                  "%d on device %d",
+                  r, c->rank, c->tp, c->device, r, tp, comms[0]->device);
+    if (!c->finalized)
+      return fail(RMSNORM_TP_ERR_STATE, "forward_emulated: comms[%d] not finalized", r);
+    int rc = check_shape("forward_emulated", rows, hl, hl * tp, dtype, outs[r], xs[r], ws[r]);
+    if (rc != RMSNORM_TP_OK) return rc;
+    if (*reinterpret_cast<volatile unsigned*>(c->host_flag) != 0u)
+      return fail(RMSNORM_TP_ERR_DEVICE, "forward_emulated: rank %d recorded a device failure", r);
+  }
+  if (rows > comms[0]->nmax)
+    return fail(RMSNORM_TP_ERR_ROWS, "forward_emulated: rows %lld > num_max_rows %lld",
+                (long long)rows, (long long)comms[0]->nmax);
+  if (rows == 0) return RMSNORM_TP_OK;
+  KArgs a;
+  std::memset(&a, 0, sizeof(a));
+  for (int r = 0; r < tp; ++r) {
+    a.rp[r] = rtp::RankPtrs{outs[r], xs[r], ws[r], comms[r]->state, comms[r]->host_flag_dev};
+    a.mbox[r] = comms[r]->mailbox;
+  }
+  a.rows = rows;
+  a.hl = hl;
+  a.nmax = comms[0]->nmax;
+  a.hidden_f = (float)(hl * tp);
+  a.eps = eps;
+  a.rank = 0;
+  a.tp = tp;
+  a.emulated = 1;
+  a.timeout_ns = comms[0]->timeout_ns;
+  DeviceGuard guard(comms[0]->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "forward_emulated: cudaSetDevice");
+  cudaError_t e = rtp::launch_forward(a, dtype, comms[0]->device, tp,
+                                      reinterpret_cast<cudaStream_t>(stream), nullptr);
+  if (e != cudaSuccess) return cuda_fail(e, "forward_emulated: cooperative launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_poll_error(const rmsnorm_tp_comm* c, uint32_t* code) {
+  if (!c || !code) return fail(RMSNORM_TP_ERR_INVALID, "poll_error: NULL argument");
+  *code = *reinterpret_cast<volatile unsigned*>(c->host_flag);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_status(rmsnorm_tp_comm* c, rmsnorm_tp_status_info* out) {
+  if (!c || !out) return fail(RMSNORM_TP_ERR_INVALID, "status: NULL argument");
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "status: cudaSetDevice");
+  RTP_CUDA(cudaDeviceSynchronize(), "status: cudaDeviceSynchronize");
+  DeviceState st;
+  RTP_CUDA(cudaMemcpy(&st, c->state, sizeof(st), cudaMemcpyDeviceToHost), "status: copy state");
+  std::memset(out, 0, sizeof(*out));
+  out->code = st.err_code;
+  out->src_rank = st.err_src;
+  out->row = st.err_row;
+  out->expected_tag = st.err_expected;
+  out->seen_tag = st.err_seen;
+  out->generation = st.err_call;
+  out->next_generation = st.call;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_reset(rmsnorm_tp_comm* c, uint64_t generation) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "reset: NULL communicator");
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "reset: cudaSetDevice");
+  RTP_CUDA(cudaDeviceSynchronize(), "reset: cudaDeviceSynchronize");
+  RTP_CUDA(cudaMemset(c->mailbox, 0, c->mailbox_bytes), "reset: zero mailbox");
+  DeviceState st;
+  std::memset(&st, 0, sizeof(st));
+  st.call = generation;
+  RTP_CUDA(cudaMemcpy(c->state, &st, sizeof(st), cudaMemcpyHostToDevice), "reset: write state");
+  RTP_CUDA(cudaDeviceSynchronize(), "reset: cudaDeviceSynchronize");
+  *reinterpret_cast<volatile unsigned*>(c->host_flag) = 0u;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_get_generation(rmsnorm_tp_comm* c, uint64_t* out) {
+  if (!c || !out) return fail(RMSNORM_TP_ERR_INVALID, "get_generation: NULL argument");
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "get_generation: cudaSetDevice");
+  RTP_CUDA(cudaDeviceSynchronize(), "get_generation: cudaDeviceSynchronize");
+  unsigned long long g = 0;
+  RTP_CUDA(cudaMemcpy(&g, &c->state->call, sizeof(g), cudaMemcpyDeviceToHost),
+           "get_generation: copy");
+  *out = g;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* c, int peer, int iters, void* stream,
+                               int64_t* dev_out_ns) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "probe_roundtrip: NULL communicator");
+  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "probe_roundtrip: not finalized");
+  if (peer < 0 || peer >= c->tp || peer == c->rank)
+    return fail(RMSNORM_TP_ERR_INVALID, "probe_roundtrip: peer %d invalid", peer);
+  if (iters < 1 || iters > (1 << 30))
+    return fail(RMSNORM_TP_ERR_INVALID, "probe_roundtrip: iters %d outside [1, 2^30]", iters);
+  const size_t probe_off = slots_bytes(c->tp, c->nmax) / sizeof(unsigned long long);
+  unsigned long long* remote = c->peers[peer] + probe_off + c->rank;
+  unsigned long long* local = c->mailbox + probe_off + peer;
+  c->probe_seq += 1;
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "probe_roundtrip: cudaSetDevice");
+  cudaError_t e = rtp::launch_probe(remote, local, c->probe_seq, iters, c->rank < peer ? 1 : 0,
+                                    c->timeout_ns, reinterpret_cast<long long*>(dev_out_ns),
+                                    nullptr, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "probe_roundtrip: launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int resident_ctas,
+                    rmsnorm_tp_plan_info* out) {
+  if (!out) return fail(RMSNORM_TP_ERR_INVALID, "plan: NULL out");
+  if (!valid_dtype(dtype)) return fail(RMSNORM_TP_ERR_INVALID, "plan: unknown dtype %d", dtype);
+  if (rows < 0 || hl < 1 || resident_ctas < 1)
+    return fail(RMSNORM_TP_ERR_INVALID, "plan: rows %lld, local_hidden %lld, resident %d",
+                (long long)rows, (long long)hl, resident_ctas);
+  const rtp::VariantDesc v = rtp::choose_variant(hl, dtype, aligned != 0);
+  const rtp::Plan p = rtp::plan_for(v, rows, resident_ctas);
+  out->variant = p.variant;
+  out->vec_per_lane = p.vec_per_lane;
+  out->team_warps = p.team_warps;
+  out->rows_per_tile = p.rows_per_tile;
+  out->block_threads = p.block_threads;
+  out->teams_per_cta = p.teams_per_cta;
+  out->tiles = p.tiles;
+  out->grid = p.grid;
+  out->reserved = 0;
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_plan_coverage(const rmsnorm_tp_plan_info* p, int64_t rows, int32_t* counts) {
+  if (!p || (!counts && rows > 0)) return fail(RMSNORM_TP_ERR_INVALID, "plan_coverage: NULL");
+  if (p->grid < 1 || p->teams_per_cta < 1 || p->rows_per_tile < 1)
+    return fail(RMSNORM_TP_ERR_INVALID, "plan_coverage: malformed plan");
+  for (int64_t i = 0; i < rows; ++i) counts[i] = 0;
+  // Same walk as the kernels: team g visits tiles g, g + T, g + 2T, ... (T = all teams).
+  const int64_t teams_total = (int64_t)p->grid * p->teams_per_cta;
+  const int64_t tiles = (rows + p->rows_per_tile - 1) / p->rows_per_tile;
+  for (int64_t g = 0; g < teams_total; ++g) {
+    for (int64_t it = 0;; ++it) {
+      const int64_t t = rtp::tile_of(g, it, teams_total);
+      if (t >= tiles) break;
+      for (int r = 0; r < p->rows_per_tile; ++r) {
+        const int64_t row = t * p->rows_per_tile + r;
+        if (row < rows) counts[row] += 1;
+      }
+    }
+  }
+  return RMSNORM_TP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// Internal interface between the C-ABI host code (comm.cpp) and the kernels
+// (kernels.cu). Not installed; the public interface is include/rmsnorm_tp_b200.h.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "rtp_common.h"
+
+namespace rtp {
+
+// Pointers of one rank's call.
+struct RankPtrs {
+  void* out;
+  const void* x;
+  const void* w;
+  DeviceState* state;        // null at TP = 1
+  unsigned int* host_flag;   // device alias of the host-mapped failure flag (may be null)
+};
+
+// Kernel parameters (passed by value, read through __grid_constant__).
+struct KArgs {
+  RankPtrs rp[kMaxTP];                 // [0] for a normal launch, [blockIdx.y] when emulated
+  unsigned long long* mbox[kMaxTP];    // mailbox base of every rank, as this process maps it
+  int64_t rows;
+  int64_t hl;                          // local hidden width (elements)
+  int64_t nmax;                        // num_max_rows: stride between source blocks of the mailbox
+  float hidden_f;                      // global hidden width (divisor of the sum of squares)
+  float eps;
+  int rank;                            // this rank (normal launch)
+  int tp;
+  int emulated;                        // 1: every rank in one launch, rank = blockIdx.y
+  int pad_;
+  unsigned long long timeout_ns;
+};
+
+enum Dtype { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+// Shape of a kernel variant (template parameters of the vectorised kernel).
+struct VariantDesc {
+  int id;              // -1 = generic
+  int vec_per_lane;
+  int team_warps;
+  int rows_per_tile;
+  int block_threads;
+};
+
+int elem_bytes(int dtype);
+VariantDesc choose_variant(int64_t hl, int dtype, bool aligned);
+Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
+
+// Launch the forward kernel. grid_y > 1 only for the emulated (all ranks on one
+// GPU, cooperative) launch. Returns a CUDA error; *plan_out (optional) gets the plan.
+cudaError_t launch_forward(const KArgs& a, int dtype, int device, int grid_y,
+                           cudaStream_t stream, Plan* plan_out);
+
+cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,
+                         unsigned long long seq, int iters, int initiator,
+                         unsigned long long timeout_ns, long long* out_ns,
+                         unsigned int* err_flag, cudaStream_t stream);
+
+}  // namespace rtp

@@ -1,0 +1,594 @@
+// Fused tensor-parallel RMSNorm kernels for B200 (sm_100a).
+//
+// One launch per forward call. For each row r of x [rows, hl] on rank k:
+//   1. load the row with 128-bit loads into registers (read once from HBM),
+//   2. s_k = sum(x^2) in fp32 (warp butterfly, then across the team's warps),
+//   3. push {s_k, tag} into slot [buf][k][r] of every peer's mailbox (one
+//      relaxed system-scope 64-bit store per peer over NVLink),
+//   4. poll slots [buf][q][r] of the local mailbox until each carries the tag
+//      (bounded by the global timer),
+//   5. S = s_0 + s_1 + ... + s_{tp-1} in rank order (bit-identical on every rank),
+//      y = (x * rsqrt(S / hidden + eps)) * w in fp32 from the registers, one
+//      rounding to the output type, 128-bit stores.
+// Reference: csrc/rmsnorm_tp.cu:48-178 does the same five phases with one CTA
+// per row, a second read of x for phase 5, a separate flag word per slot and an
+// unbounded `>=` poll; the math contract (S / hidden, rsqrtf, x*inv*w) follows
+// rmsnorm_tp.cu:156-170 and the AllReduce path bench_rmsnorm_tp.py:16-22.
+//
+// Rows map to "teams" of W warps. A team walks row tiles in a grid-stride loop
+// over a grid of at most one resident wave, so all CTAs of every rank are
+// resident together and the waits between GPUs always make progress.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "internal.h"
+#include "ptx.cuh"
+#include "rtp_common.h"
+
+namespace rtp {
+
+// ---------------------------------------------------------------------------
+// Element packing: 16 bytes = 4 fp32 or 8 bf16/fp16.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Pack;
+
+template <>
+struct Pack<float> {
+  static constexpr int kE = 4;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[4]) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[4]) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+};
+
+__device__ __forceinline__ void bf16x2_unpack(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xFFFF0000u);
+}
+__device__ __forceinline__ uint32_t bf16x2_pack(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Pack<__nv_bfloat16> {
+  static constexpr int kE = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
+    bf16x2_unpack(v.x, f[0], f[1]);
+    bf16x2_unpack(v.y, f[2], f[3]);
+    bf16x2_unpack(v.z, f[4], f[5]);
+    bf16x2_unpack(v.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+    return make_uint4(bf16x2_pack(f[0], f[1]), bf16x2_pack(f[2], f[3]), bf16x2_pack(f[4], f[5]),
+                      bf16x2_pack(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ void f16x2_unpack(uint32_t u, float& lo, float& hi) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  float2 f = __half22float2(h);
+  lo = f.x;
+  hi = f.y;
+}
+__device__ __forceinline__ uint32_t f16x2_pack(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Pack<__half> {
+  static constexpr int kE = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
+    f16x2_unpack(v.x, f[0], f[1]);
+    f16x2_unpack(v.y, f[2], f[3]);
+    f16x2_unpack(v.z, f[4], f[5]);
+    f16x2_unpack(v.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+    return make_uint4(f16x2_pack(f[0], f[1]), f16x2_pack(f[2], f[3]), f16x2_pack(f[4], f[5]),
+                      f16x2_pack(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
+};
+
+// Butterfly sum: every lane ends with the bit-identical total (IEEE addition is
+// commutative, and each step adds the same two operands on both partner lanes).
+__device__ __forceinline__ float warp_allreduce_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float sumsq16(const uint4& v) {
+  float f[Pack<T>::kE];
+  Pack<T>::unpack(v, f);
+  float a = 0.f, b = 0.f;
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; e += 2) {
+    a = fmaf(f[e], f[e], a);
+    b = fmaf(f[e + 1], f[e + 1], b);
+  }
+  return a + b;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 normalize16(const uint4& xv, const uint4& wv, float inv) {
+  float xf[Pack<T>::kE], wf[Pack<T>::kE];
+  Pack<T>::unpack(xv, xf);
+  Pack<T>::unpack(wv, wf);
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; ++e) xf[e] = (xf[e] * inv) * wf[e];
+  return Pack<T>::pack(xf);
+}
+
+__device__ __forceinline__ float quiet_nan() { return __uint_as_float(0x7FC00000u); }
+
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange of the partial sums of up to kRows rows, by one warp.
+// Lane L serves row r = L / tp and rank q = L % tp: it pushes the row's local
+// partial into rank q's mailbox and waits for rank q's partial in the local
+// one. Every lane returns S[i] = sum over ranks in rank order.
+// Returns false (warp-uniform) if any wait gave up; the failure is recorded in
+// the rank's DeviceState and mirrored to the host-mapped flag.
+// ---------------------------------------------------------------------------
+template <int kRows>
+__device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, const RankPtrs& rp,
+                                                  uint32_t buf, uint32_t tag,
+                                                  unsigned long long call, int64_t row0,
+                                                  int nrows, const float (&ss)[kRows],
+                                                  float (&S)[kRows]) {
+  const int lane = threadIdx.x & 31;
+  const int tp = a.tp;
+  const int r = lane / tp;
+  const int q = lane - r * tp;
+  const bool remote = (r < nrows) && (q != rank);
+  float mine = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRows; ++i)
+    if (i == r) mine = ss[i];
+
+  if (remote) {
+    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, tp, a.nmax, row0 + r);
+    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
+  }
+  float val = mine;
+  uint32_t fail = kStatusOk;
+  if (remote) {
+    const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, tp, a.nmax, row0 + r);
+    unsigned long long w = ptx::ld_relaxed_sys_u64(src);
+    if (slot_tag(w) != tag) {
+      const unsigned long long t0 = ptx::globaltimer();
+      for (;;) {
+        w = ptx::ld_relaxed_sys_u64(src);
+        if (slot_tag(w) == tag) break;
+        if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
+          fail = kStatusAborted;
+          break;
+        }
+        if (ptx::globaltimer() - t0 > a.timeout_ns) {
+          fail = kStatusTimeout;
+          break;
+        }
+      }
+    }
+    if (fail == kStatusTimeout) {
+      DeviceState* st = rp.state;
+      if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {
+        st->err_src = (unsigned)q;
+        st->err_row = (long long)(row0 + r);
+        st->err_expected = tag;
+        st->err_seen = slot_tag(w);
+        st->err_call = call;
+        if (rp.host_flag != nullptr) {
+          *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusTimeout;
+          __threadfence_system();
+        }
+      }
+      atomicExch(&st->abort, 1u);
+    }
+    val = slot_value(w);
+  }
+  const bool any_fail = __any_sync(0xFFFFFFFFu, fail != kStatusOk);
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    float s = 0.f;
+    for (int p = 0; p < tp; ++p) s += __shfl_sync(0xFFFFFFFFu, val, i * tp + p);
+    S[i] = s;
+  }
+  return !any_fail;
+}
+
+// Last CTA of the launch advances the rank's generation counter.
+__device__ __forceinline__ void finish_launch(DeviceState* st, unsigned long long call) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&st->done, 1u);
+    if (prev == gridDim.x - 1) {
+      st->done = 0u;
+      st->call = call + 1ull;
+      __threadfence();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Vectorised kernel: each lane keeps kVec 16-byte vectors of each of the team's
+// kRows rows in registers between the load and the store (x is read once).
+// Column vector c of a row belongs to lane (c % 32) of warp ((c / 32) % kW) at
+// register j = c / (32 * kW): each warp instruction touches 512 contiguous bytes.
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kRows, int kBlock>
+__global__ void __launch_bounds__(kBlock)
+    tp_rmsnorm_vec_kernel(const __grid_constant__ KArgs a) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  static_assert(kRows * kMaxTP <= 32, "one warp serves every (row, rank) pair of a tile");
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const int64_t V = a.hl / Pack<T>::kE;
+  const uint4* __restrict__ xg = reinterpret_cast<const uint4*>(rp.x);
+  const uint4* __restrict__ wg = reinterpret_cast<const uint4*>(rp.w);
+  uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
+  const bool exchange = a.tp > 1;
+
+  __shared__ unsigned long long s_call;
+  __shared__ float s_part[kTeams][2][kW][kRows];
+  __shared__ float s_sum[kTeams][2][kRows];
+  __shared__ int s_ok[kTeams][2];
+
+  unsigned long long call = 0ull;
+  uint32_t buf = 0u, tag = 0u;
+  if (exchange) {
+    if (threadIdx.x == 0) s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
+    __syncthreads();
+    call = s_call;
+    buf = buffer_of(call);
+    tag = tag_of(call);
+  }
+
+  const int64_t tiles = (a.rows + kRows - 1) / kRows;
+  const int64_t teams_total = (int64_t)gridDim.x * kTeams;
+  const int64_t team_global = (int64_t)blockIdx.x * kTeams + team;
+  int it = 0;
+  for (int64_t t = team_global; t < tiles; t += teams_total, ++it) {
+    const int64_t row0 = t * kRows;
+    const int nrows = (int)min((int64_t)kRows, a.rows - row0);
+    uint4 xv[kRows][kVec];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
+        if (r < nrows && c < V)
+          xv[r][j] = ptx::ld_stream_v4(xg + (row0 + r) * V + c);
+        else
+          xv[r][j] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    float ss[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) s += sumsq16<T>(xv[r][j]);
+      ss[r] = warp_allreduce_sum(s);
+    }
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) s_part[team][it & 1][wit][r] = ss[r];
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) s += s_part[team][it & 1][w][r];
+        ss[r] = s;
+      }
+    }
+    float S[kRows];
+    bool ok = true;
+    if (exchange) {
+      if (kW == 1 || wit == 0)
+        ok = exchange_partials<kRows>(a, rank, rp, buf, tag, call, row0, nrows, ss, S);
+      if constexpr (kW > 1) {
+        if (wit == 0 && lane == 0) {
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) s_sum[team][it & 1][r] = S[r];
+          s_ok[team][it & 1] = ok ? 1 : 0;
+        }
+        ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][it & 1][r];
+        ok = s_ok[team][it & 1] != 0;
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) S[r] = ss[r];
+    }
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (r < nrows) {
+        const float var = S[r] / a.hidden_f;
+        const float inv = ok ? rsqrtf(var + a.eps) : quiet_nan();
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
+          if (c < V) {
+            const uint4 wv = ptx::ld_cached_v4(wg + c);
+            ptx::st_v4(yg + (row0 + r) * V + c, normalize16<T>(xv[r][j], wv, inv));
+          }
+        }
+      }
+    }
+  }
+  if (exchange) finish_launch(rp.state, call);
+}
+
+// ---------------------------------------------------------------------------
+// Generic kernel: any width and alignment. One CTA per row at a time, scalar
+// loads, x read twice (the second read normally hits L2). Same exchange.
+// ---------------------------------------------------------------------------
+template <typename T, int kBlock>
+__global__ void __launch_bounds__(kBlock)
+    tp_rmsnorm_generic_kernel(const __grid_constant__ KArgs a) {
+  constexpr int kWarps = kBlock / 32;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const T* __restrict__ xg = reinterpret_cast<const T*>(rp.x);
+  const T* __restrict__ wg = reinterpret_cast<const T*>(rp.w);
+  T* __restrict__ yg = reinterpret_cast<T*>(rp.out);
+  const bool exchange = a.tp > 1;
+  const int64_t hl = a.hl;
+
+  __shared__ unsigned long long s_call;
+  __shared__ float s_part[kWarps];
+  __shared__ float s_sum;
+  __shared__ int s_ok;
+
+  unsigned long long call = 0ull;
+  uint32_t buf = 0u, tag = 0u;
+  if (exchange) {
+    if (threadIdx.x == 0) s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
+    __syncthreads();
+    call = s_call;
+    buf = buffer_of(call);
+    tag = tag_of(call);
+  }
+
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const T* xr = xg + row * hl;
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < hl; i += kBlock) {
+      const float v = Pack<T>::to_f(xr[i]);
+      s = fmaf(v, v, s);
+    }
+    s = warp_allreduce_sum(s);
+    if (lane == 0) s_part[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += s_part[w];
+      float ss[1] = {t};
+      float S[1] = {t};
+      bool ok = true;
+      if (exchange) ok = exchange_partials<1>(a, rank, rp, buf, tag, call, row, 1, ss, S);
+      if (lane == 0) {
+        s_sum = S[0];
+        s_ok = ok ? 1 : 0;
+      }
+    }
+    __syncthreads();
+    const float var = s_sum / a.hidden_f;
+    const float inv = s_ok ? rsqrtf(var + a.eps) : quiet_nan();
+    T* yr = yg + row * hl;
+    for (int64_t i = threadIdx.x; i < hl; i += kBlock) {
+      const float v = Pack<T>::to_f(xr[i]);
+      const float w = Pack<T>::to_f(wg[i]);
+      yr[i] = Pack<T>::from_f((v * inv) * w);
+    }
+    __syncthreads();  // s_part / s_sum are reused by the next row
+  }
+  if (exchange) finish_launch(rp.state, call);
+}
+
+// ---------------------------------------------------------------------------
+// One-hop latency probe: a single thread bounces a counter between two GPUs.
+// ---------------------------------------------------------------------------
+__global__ void probe_roundtrip_kernel(unsigned long long* remote_slot,
+                                       const unsigned long long* local_slot,
+                                       unsigned long long seq, int iters, int initiator,
+                                       unsigned long long timeout_ns, long long* out_ns,
+                                       unsigned int* err_flag) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const unsigned long long start = ptx::globaltimer();
+  bool failed = false;
+  for (int i = 1; i <= iters && !failed; ++i) {
+    const unsigned long long v = (seq << 32) | (unsigned long long)i;
+    if (initiator) ptx::st_relaxed_sys_u64(remote_slot, v);
+    const unsigned long long t0 = ptx::globaltimer();
+    while (ptx::ld_relaxed_sys_u64(local_slot) != v) {
+      if (ptx::globaltimer() - t0 > timeout_ns) {
+        failed = true;
+        break;
+      }
+    }
+    if (!initiator && !failed) ptx::st_relaxed_sys_u64(remote_slot, v);
+  }
+  const unsigned long long stop = ptx::globaltimer();
+  if (failed) {
+    if (err_flag) *err_flag = 1u;
+    if (out_ns) *out_ns = -1;
+  } else if (out_ns) {
+    *out_ns = (long long)((stop - start) / (unsigned long long)(iters > 0 ? iters : 1));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: variant table, plan, occupancy cache, launch.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct VariantShape {
+  int vec, w, rows, block;
+};
+// Selected by the number of 16-byte vectors per row, V: the first entry whose
+// capacity 32 * w * vec >= V.
+constexpr VariantShape kShapes[] = {
+    {1, 1, 4, 256},   // V <= 32     (bf16 hl <= 256,   fp32 hl <= 128)
+    {2, 1, 2, 256},   // V <= 64     (bf16 hl <= 512,   fp32 hl <= 256)
+    {4, 1, 2, 256},   // V <= 128    (bf16 hl <= 1024,  fp32 hl <= 512)
+    {8, 1, 1, 256},   // V <= 256    (bf16 hl <= 2048,  fp32 hl <= 1024)
+    {8, 2, 1, 256},   // V <= 512    (bf16 hl <= 4096,  fp32 hl <= 2048)
+    {8, 4, 1, 256},   // V <= 1024   (bf16 hl <= 8192,  fp32 hl <= 4096)
+    {8, 8, 1, 256},   // V <= 2048   (bf16 hl <= 16384, fp32 hl <= 8192)
+    {8, 16, 1, 512},  // V <= 4096   (bf16 hl <= 32768, fp32 hl <= 16384)
+};
+constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
+constexpr int kGenericBlock = 256;
+
+using KernelFn = void (*)(const KArgs);
+
+template <typename T>
+struct KernelTable {
+  static constexpr KernelFn vec[kNumShapes] = {
+      tp_rmsnorm_vec_kernel<T, 1, 1, 4, 256>, tp_rmsnorm_vec_kernel<T, 2, 1, 2, 256>,
+      tp_rmsnorm_vec_kernel<T, 4, 1, 2, 256>, tp_rmsnorm_vec_kernel<T, 8, 1, 1, 256>,
+      tp_rmsnorm_vec_kernel<T, 8, 2, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 4, 1, 256>,
+      tp_rmsnorm_vec_kernel<T, 8, 8, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 16, 1, 512>,
+  };
+  static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
+};
+
+KernelFn kernel_for(int dtype, int variant) {
+  switch (dtype) {
+    case kF32:
+      return variant < 0 ? KernelTable<float>::generic : KernelTable<float>::vec[variant];
+    case kBF16:
+      return variant < 0 ? KernelTable<__nv_bfloat16>::generic
+                         : KernelTable<__nv_bfloat16>::vec[variant];
+    default:
+      return variant < 0 ? KernelTable<__half>::generic : KernelTable<__half>::vec[variant];
+  }
+}
+
+constexpr int kMaxDevices = 64;
+// resident CTAs per device/dtype/variant (+1 slot for generic); 0 = not yet computed
+std::atomic<int> g_resident[kMaxDevices][3][kNumShapes + 1];
+
+int resident_ctas(int device, int dtype, int variant, int block, cudaError_t* err) {
+  *err = cudaSuccess;
+  const int slot = variant < 0 ? kNumShapes : variant;
+  if (device >= 0 && device < kMaxDevices) {
+    const int cached = g_resident[device][dtype][slot].load(std::memory_order_relaxed);
+    if (cached > 0) return cached;
+  }
+  int per_sm = 0, sms = 0;
+  *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &per_sm, reinterpret_cast<const void*>(kernel_for(dtype, variant)), block, 0);
+  if (*err != cudaSuccess) return 0;
+  *err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (*err != cudaSuccess) return 0;
+  const int total = per_sm * sms;
+  if (device >= 0 && device < kMaxDevices && total > 0)
+    g_resident[device][dtype][slot].store(total, std::memory_order_relaxed);
+  return total;
+}
+
+}  // namespace
+
+int elem_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
+
+VariantDesc choose_variant(int64_t hl, int dtype, bool aligned) {
+  const int eb = elem_bytes(dtype);
+  const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
+  if (vec_ok) {
+    const int64_t V = hl * eb / 16;
+    for (int i = 0; i < kNumShapes; ++i) {
+      const int64_t cap = 32ll * kShapes[i].w * kShapes[i].vec;
+      if (V <= cap) return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block};
+    }
+  }
+  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock};
+}
+
+Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
+  Plan p{};
+  p.variant = v.id;
+  p.vec_per_lane = v.vec_per_lane;
+  p.team_warps = v.team_warps;
+  p.rows_per_tile = v.rows_per_tile;
+  p.block_threads = v.block_threads;
+  p.teams_per_cta = v.block_threads / 32 / v.team_warps;
+  p.tiles = rows > 0 ? (rows + v.rows_per_tile - 1) / v.rows_per_tile : 0;
+  const int64_t need = (p.tiles + p.teams_per_cta - 1) / p.teams_per_cta;
+  int64_t grid = need < (int64_t)resident_ctas ? need : (int64_t)resident_ctas;
+  if (grid < 1) grid = 1;
+  p.grid = (int)grid;
+  return p;
+}
+
+cudaError_t launch_forward(const KArgs& a, int dtype, int device, int grid_y,
+                           cudaStream_t stream, Plan* plan_out) {
+  const int nranks = a.emulated ? grid_y : 1;
+  bool aligned = true;
+  for (int r = 0; r < nranks; ++r) {
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(a.rp[r].x) |
+                           reinterpret_cast<uintptr_t>(a.rp[r].out) |
+                           reinterpret_cast<uintptr_t>(a.rp[r].w);
+    if (bits & 15u) aligned = false;
+  }
+  const VariantDesc v = choose_variant(a.hl, dtype, aligned);
+  cudaError_t err = cudaSuccess;
+  int resident = resident_ctas(device, dtype, v.id, v.block_threads, &err);
+  if (err != cudaSuccess) return err;
+  if (grid_y > 1) resident /= grid_y;
+  if (resident < 1) return cudaErrorCooperativeLaunchTooLarge;
+  const Plan p = plan_for(v, a.rows, resident);
+  if (plan_out) *plan_out = p;
+  const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
+  void* args[] = {const_cast<KArgs*>(&a)};
+  const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
+  const dim3 block((unsigned)p.block_threads);
+  if (grid_y > 1) return cudaLaunchCooperativeKernel(fn, grid, block, args, 0, stream);
+  return cudaLaunchKernel(fn, grid, block, args, 0, stream);
+}
+
+cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,
+                         unsigned long long seq, int iters, int initiator,
+                         unsigned long long timeout_ns, long long* out_ns,
+                         unsigned int* err_flag, cudaStream_t stream) {
+  probe_roundtrip_kernel<<<1, 32, 0, stream>>>(remote_slot, local_slot, seq, iters, initiator,
+                                               timeout_ns, out_ns, err_flag);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace rtp

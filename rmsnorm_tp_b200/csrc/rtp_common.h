@@ -1,0 +1,132 @@
+// Shared host/device definitions of the fused tensor-parallel RMSNorm.
+//
+// Everything here is plain arithmetic that both the CUDA kernels and the host
+// C-ABI use, so the host unit tests exercise exactly the code the device runs:
+//   * the per-rank device state (generation counter, completion counter, error
+//     record),
+//   * the generation -> (mailbox buffer, tag) mapping that replaces the
+//     reference's `int generation` kernel argument and `>=` poll
+//     (reference csrc/rmsnorm_tp.cu:61, :114, :128),
+//   * the packed 64-bit mailbox word {partial sum, tag},
+//   * the mailbox slot layout (reference csrc/bindings.cpp:26-33 keeps
+//     float sums[tp][rows] + int gen[tp][rows]; here one u64 per slot, two
+//     generation buffers, rows strided by num_max_rows),
+//   * the row -> team mapping of the launch plan.
+#pragma once
+
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__CUDACC__)
+#define RTP_HD __host__ __device__ __forceinline__
+#else
+#define RTP_HD static inline
+#endif
+
+namespace rtp {
+
+constexpr int kMaxTP = 8;              // reference common.hpp:9 (MAX_TP_SIZE)
+constexpr int kHandleBytes = 128;      // reference common.hpp:10 (HANDLE_SIZE)
+constexpr uint32_t kHandleMagic = 0x42505452u;  // "RTPB"
+constexpr uint32_t kHandleVersion = 1u;
+
+// Device-side failure codes recorded in DeviceState::err_code and mirrored
+// into the host-mapped flag word.
+enum DeviceStatus : uint32_t {
+  kStatusOk = 0,
+  kStatusTimeout = 1,   // a peer's partial sum did not arrive within the limit
+  kStatusAborted = 2,   // gave up because another CTA on this GPU timed out
+};
+
+// Per-rank state in local device memory (never mapped to peers).
+struct alignas(64) DeviceState {
+  unsigned long long call;      // launches completed so far = generation of the next launch
+  unsigned int done;            // CTAs of the running launch that have finished
+  unsigned int abort;           // set once any CTA gave up; the rest give up fast
+  unsigned int err_code;        // first failure (DeviceStatus), set with atomicCAS
+  unsigned int err_src;         // source rank whose partial never arrived
+  long long err_row;            // row that timed out
+  unsigned int err_expected;    // tag that was awaited
+  unsigned int err_seen;        // tag found in the slot when the wait ended
+  unsigned long long err_call;  // generation of the failing launch
+  unsigned long long reserved[3];
+};
+
+// ---------------------------------------------------------------------------
+// Generation arithmetic.
+//
+// Call number `g` (a 64-bit count of launches, identical on every rank because
+// every rank launches the same sequence) selects
+//   buffer(g) = g & 1                 -- double buffer: a rank that has finished
+//                                        call g may already push call g+1 while a
+//                                        slow peer still reads call g's slots;
+//                                        it cannot reach call g+2 before that
+//                                        peer has pushed g+1, i.e. finished g.
+//   tag(g)    = 1 + g mod (2^32 - 1)  -- never 0 (a zeroed mailbox never matches)
+//                                        and tag(g) != tag(g+2) at every g, across
+//                                        the 32-bit wrap included.
+// The poll tests the tag for EQUALITY, so a stale slot from call g-2 (same
+// buffer) is never taken for call g, unlike the reference's `< generation`
+// test (rmsnorm_tp.cu:128), which also accepts newer generations.
+// ---------------------------------------------------------------------------
+RTP_HD uint32_t tag_of(uint64_t g) { return (uint32_t)(g % 0xFFFFFFFFull) + 1u; }
+RTP_HD uint32_t buffer_of(uint64_t g) { return (uint32_t)(g & 1ull); }
+
+RTP_HD uint32_t f32_bits(float v) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_uint(v);
+#else
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  return u;
+#endif
+}
+RTP_HD float bits_f32(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+  return __uint_as_float(u);
+#else
+  float v;
+  memcpy(&v, &u, 4);
+  return v;
+#endif
+}
+
+// One mailbox word: high 32 bits = tag, low 32 bits = fp32 partial sum of squares.
+// A naturally aligned 64-bit store is single-copy atomic, so a reader that sees
+// the tag also sees the value: no separate flag and no release/acquire pair.
+RTP_HD uint64_t pack_slot(float partial, uint32_t tag) {
+  return ((uint64_t)tag << 32) | (uint64_t)f32_bits(partial);
+}
+RTP_HD uint32_t slot_tag(uint64_t w) { return (uint32_t)(w >> 32); }
+RTP_HD float slot_value(uint64_t w) { return bits_f32((uint32_t)(w & 0xFFFFFFFFull)); }
+
+// Mailbox of one rank: u64 slot[2 buffers][tp source ranks][num_max_rows].
+RTP_HD uint64_t slot_index(uint32_t buf, int src, int tp, int64_t nmax, int64_t row) {
+  return ((uint64_t)buf * (uint64_t)tp + (uint64_t)src) * (uint64_t)nmax + (uint64_t)row;
+}
+RTP_HD uint64_t mailbox_slots(int tp, int64_t nmax) { return 2ull * (uint64_t)tp * (uint64_t)nmax; }
+
+// ---------------------------------------------------------------------------
+// Launch plan: which kernel variant handles a (rows, local_hidden, dtype) call
+// and how rows map to "teams" (a team = team_warps warps sharing one row).
+// Teams walk row tiles of rows_per_tile rows in a grid-stride loop; the grid is
+// never larger than one resident wave, so every CTA of every rank is resident
+// at once and the cross-GPU waits always make progress.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int variant;          // index in the variant table, -1 = generic (any alignment / width)
+  int vec_per_lane;     // 16-byte vectors of one row held per lane
+  int team_warps;       // warps that share one row
+  int rows_per_tile;    // rows a team handles per step
+  int block_threads;
+  int teams_per_cta;
+  int64_t tiles;        // ceil(rows / rows_per_tile)
+  int grid;             // CTAs (x); <= resident capacity
+};
+
+// First row of the tile a team handles at step `it`; rows [first, first + rows_per_tile)
+RTP_HD int64_t tile_of(int64_t team_global, int64_t it, int64_t teams_total) {
+  return team_global + it * teams_total;
+}
+
+}  // namespace rtp

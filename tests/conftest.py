@@ -1,0 +1,47 @@
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); run with -m gpu")
+
+
+def load_golden():
+    """{case: {"meta": dict, "x": [..], "w": [..], "y": [..]}} from tests/golden/golden.npz."""
+    cases = {}
+    with np.load(GOLDEN) as z:
+        names = sorted({k.split("/")[0] for k in z.files})
+        for n in names:
+            meta = json.loads(bytes(z[f"{n}/meta"]).decode())
+            tp = meta["tp"]
+            cases[n] = {
+                "meta": meta,
+                "x": [z[f"{n}/x{r}"] for r in range(tp)],
+                "w": [z[f"{n}/w{r}"] for r in range(tp)],
+                "y": [z[f"{n}/y{r}"] for r in range(tp)],
+            }
+    return cases
+
+
+@pytest.fixture(scope="session")
+def golden():
+    return load_golden()
+
+
+@pytest.fixture(autouse=True)
+def _require_cuda_for_gpu_tests(request):
+    # A GPU test must never pass by skipping on a box without CUDA.
+    if request.node.get_closest_marker("gpu") is not None:
+        import torch
+
+        assert torch.cuda.is_available(), "GPU test run without a CUDA device"

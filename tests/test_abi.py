@@ -1,0 +1,75 @@
+"""The C-ABI library loads without a GPU and exports exactly what
+include/rmsnorm_tp_b200.h declares; argument checks run before any CUDA call."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from rmsnorm_tp_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "rmsnorm_tp_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b((?:rmsnorm)_\w+)\s*\(", text)))
+
+
+def test_header_declares_functions():
+    names = declared_functions()
+    assert "rmsnorm_tp_forward" in names and "rmsnorm_tp_create" in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_the_header():
+    assert sorted(_lib.SIGNATURES) == declared_functions()
+
+
+def test_abi_version():
+    assert _lib.LIB.rmsnorm_tp_abi_version() == 100
+
+
+@pytest.mark.parametrize("rank,tp,nmax", [(2, 2, 16), (-1, 2, 16), (0, 0, 16), (0, 9, 16), (0, 2, 0)])
+def test_create_rejects_bad_arguments_before_touching_cuda(rank, tp, nmax):
+    out = ctypes.c_void_p()
+    rc = _lib.LIB.rmsnorm_tp_create(rank, tp, nmax, 0, ctypes.byref(out))
+    assert rc == _lib.ERR_INVALID
+    assert out.value is None
+    assert _lib.last_error().startswith("create:")
+
+
+def test_null_communicator_is_an_error_not_a_crash():
+    L = _lib.LIB
+    assert L.rmsnorm_tp_forward(None, None, None, None, 1, 8, 8, 0, 1e-6, None) == _lib.ERR_INVALID
+    assert L.rmsnorm_tp_finalize(None) == _lib.ERR_INVALID
+    assert L.rmsnorm_tp_destroy(None) == _lib.OK
+    assert L.rmsnorm_tp_open_peer(None, 1, b"x" * 128, 128) == _lib.ERR_INVALID
+    assert L.rmsnorm_tp_set_timeout(None, 5) == _lib.ERR_INVALID
+    code = ctypes.c_uint32()
+    assert L.rmsnorm_tp_poll_error(None, ctypes.byref(code)) == _lib.ERR_INVALID
+
+
+def test_local_forward_validates_shape_without_gpu():
+    L = _lib.LIB
+    assert L.rmsnorm_local_forward(None, None, None, 4, 8, 7, 1e-6, None) == _lib.ERR_INVALID  # dtype
+    assert L.rmsnorm_local_forward(None, None, None, -1, 8, 0, 1e-6, None) == _lib.ERR_INVALID  # rows
+    assert L.rmsnorm_local_forward(None, None, None, 4, 0, 0, 1e-6, None) == _lib.ERR_INVALID  # width
+    assert L.rmsnorm_local_forward(None, None, None, 4, 8, 0, 1e-6, None) == _lib.ERR_INVALID  # NULL
+    assert L.rmsnorm_local_forward(None, None, None, 0, 8, 0, 1e-6, None) == _lib.OK  # no rows: no launch
+
+
+def test_check_maps_codes_to_exceptions():
+    with pytest.raises(_lib.RMSNormTPDeviceError):
+        _lib.check(_lib.ERR_DEVICE, "x")
+    with pytest.raises(_lib.RMSNormTPError) as e:
+        _lib.check(_lib.ERR_INVALID, "x")
+    assert e.value.code == _lib.ERR_INVALID and isinstance(e.value, RuntimeError)

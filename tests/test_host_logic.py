@@ -1,0 +1,101 @@
+"""Host-side logic without a GPU: generation arithmetic, launch plan and
+row -> team coverage, the Python surface's contract checks, handle format,
+and the C++ protocol test of the shared header."""
+import os
+import subprocess
+
+import pytest
+import torch
+
+import rmsnorm_tp_b200 as rtp
+from conftest import ROOT
+from rmsnorm_tp_b200 import FusedTPRMSNorm, IpcHandle
+
+
+def test_tags_never_zero_and_change_every_two_calls():
+    for g0 in (0, 2**32 - 5, 2**32 - 1 - 5, 2 * (2**32 - 1) - 5, 2**40):
+        for g in range(g0, g0 + 12):
+            assert rtp.tag_of(g) != 0
+            assert rtp.tag_of(g) != rtp.tag_of(g + 2)
+            assert rtp.buffer_of(g) == g & 1
+    assert rtp.tag_of(2**32 - 2) == 2**32 - 1 and rtp.tag_of(2**32 - 1) == 1
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384, 32768, 65536])
+def test_plan_variant_capacity(dtype, hl):
+    es = torch.tensor([], dtype=dtype).element_size()
+    p = rtp.plan(100, hl, dtype)
+    if (hl * es) % 16 or hl * es // 16 > 4096:
+        assert p["variant"] == -1
+    else:
+        V = hl * es // 16
+        assert p["variant"] >= 0
+        assert 32 * p["team_warps"] * p["vec_per_lane"] >= V            # whole row in registers
+        assert p["rows_per_tile"] * 8 <= 32                               # one lane per (row, rank)
+    assert p["block_threads"] % (32 * p["team_warps"]) == 0
+
+
+def test_unaligned_pointers_use_generic_kernel():
+    assert rtp.plan(10, 1024, torch.bfloat16, aligned=False)["variant"] == -1
+
+
+@pytest.mark.parametrize("rows", [0, 1, 2, 3, 7, 255, 256, 1000, 4097, 65536])
+@pytest.mark.parametrize("hl", [64, 1024, 4096, 37])
+@pytest.mark.parametrize("resident", [1, 7, 296, 1184])
+def test_every_row_is_visited_exactly_once(rows, hl, resident):
+    p = rtp.plan(rows, hl, torch.bfloat16, resident_ctas=resident)
+    assert p["grid"] <= max(1, resident)
+    counts = rtp.plan_coverage(p, rows)
+    assert len(counts) == rows and all(c == 1 for c in counts)
+
+
+def test_grid_never_exceeds_one_resident_wave():
+    p = rtp.plan(65536, 1024, torch.bfloat16, resident_ctas=296)
+    assert p["grid"] == 296 and p["tiles"] == 65536 // p["rows_per_tile"]
+    p = rtp.plan(3, 1024, torch.bfloat16, resident_ctas=296)
+    assert p["grid"] == 1
+
+
+def test_tp1_module_keeps_reference_attributes():
+    m = FusedTPRMSNorm(hidden_dim=4096, eps=1e-5)
+    assert (m.tp_size, m.rank, m.eps, m.hidden_dim, m.num_max_rows) == (1, 0, 1e-5, 4096, 65536)
+    assert m.comm_buf is None
+    m.destroy()
+
+
+def test_forward_contract_checks_raise_assertion_error():
+    m = FusedTPRMSNorm(hidden_dim=64)
+    x = torch.randn(4, 64)
+    w = torch.randn(64)
+    with pytest.raises(AssertionError):                  # not contiguous
+        m.forward(x.t(), w)
+    with pytest.raises(AssertionError):                  # unsupported dtype
+        m.forward(x.double(), w.double())
+    with pytest.raises(AssertionError):                  # mismatched dtypes
+        m.forward(x, w.half())
+    with pytest.raises(AssertionError):                  # weight shape
+        m.forward(x, torch.randn(63))
+    with pytest.raises(AssertionError):                  # CPU tensors: no CPU fallback
+        m.forward(x, w)
+
+
+def test_ipc_handle_bytes():
+    with pytest.raises(RuntimeError, match="Invalid handle size"):
+        IpcHandle().from_bytes(b"\0" * 127)
+    raw = bytearray(128)
+    raw[88:96] = (123456).to_bytes(8, "little")
+    h = IpcHandle().from_bytes(bytes(raw))
+    assert h.to_bytes() == bytes(raw) and h.alloc_size == 123456
+
+
+def test_protocol_host_program(tmp_path):
+    """Compile and run tests/cpp/test_protocol.cpp against the kernels' header."""
+    exe = tmp_path / "test_protocol"
+    src = os.path.join(ROOT, "tests", "cpp", "test_protocol.cpp")
+    inc = os.path.join(ROOT, "rmsnorm_tp_b200", "csrc")
+    subprocess.run(["g++", "-O2", "-std=c++17", "-pthread", "-Wall", "-I", inc, src, "-o", str(exe)],
+                   check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "ALL PASS" in res.stdout
