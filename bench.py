@@ -243,25 +243,58 @@ def make_rotating_sets(rows, hl, dtype, seed, min_bytes):
     return xs, w, outs
 
 
-def time_steps(fn, steps, per_launch_events=True):
-    """CUDA-event timing on the current stream: total ms and mean ms between
-    per-step event pairs (the kernel's own duration when a step is one launch)."""
+def time_steps(fn, steps):
+    """CUDA-event time (ms) of `steps` calls of fn(i) on the current stream."""
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(steps)] if per_launch_events else []
     start.record()
     for i in range(steps):
-        if per_launch_events:
-            evs[i][0].record()
         fn(i)
-        if per_launch_events:
-            evs[i][1].record()
     end.record()
     torch.cuda.synchronize()
-    total = start.elapsed_time(end)
-    per = (sum(a.elapsed_time(b) for a, b in evs) / steps) if evs else total / steps
-    return total, per
+    return start.elapsed_time(end)
+
+
+def time_graph(fn, n_capture, steps, world):
+    """Capture n_capture calls of fn(i) in a CUDA graph, replay it until about
+    `steps` calls ran, and return the CUDA-event time per call (ms, max over
+    ranks). Every replayed call is a full launch of the kernel."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(n_capture):
+            fn(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    g.replay()                       # warm replay
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    reps = max(1, round(steps / n_capture))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    per = max_over_ranks([e0.elapsed_time(e1) / (reps * n_capture)], world)[0]
+    del g
+    return per, reps * n_capture
+
+
+def plan_name(rtp, rows, hl, tp):
+    p = rtp.plan(rows, hl, torch.bfloat16, tp=tp)
+    v = p["variant"]
+    if v >= 100:
+        return (f"tp_rmsnorm_bulk_kernel<bf16,{p['teams_per_cta']} warps,{p['vec_per_lane']} stages>"
+                f" {p['rows_per_tile']} rows/stage")
+    if v >= 0:
+        return (f"tp_rmsnorm_vec_kernel<bf16,{p['vec_per_lane']},{p['team_warps']},"
+                f"{p['rows_per_tile']},{p['block_threads']}>")
+    return "tp_rmsnorm_generic_kernel<bf16,256>"
 
 
 def run_our_arm(args):
@@ -293,55 +326,28 @@ def run_our_arm(args):
     def step(i):
         module.forward(xs[i % nsets], wt, out=outs[i % nsets])
 
-    # ---- device-timed region (the `value`)
-    if sampler:
-        sampler.start()
+    # ---- timed region: the forward kernel replayed from a CUDA graph (no host
+    # launch cost), K calls over the rotating sets; clocks sampled meanwhile
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
-    total_ms, kernel_ms = time_steps(step, args.steps)
+    if sampler:
+        sampler.start()
+    # the graph holds exactly K calls and is timed over one replay (after one warm replay)
+    graph_ms, graph_calls = time_graph(step, args.steps, args.steps, world)
+    clocks = sampler.stop() if sampler else None
+    bytes_rank = algorithmic_bytes(rows, hl, elem)
+    value = tp * bytes_rank / (graph_ms * 1e-3) / 1e9
+
+    # ---- the same calls launched one by one from Python (host launch cost included)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
-    total_ms, kernel_ms = max_over_ranks([total_ms, kernel_ms], world)
-    ms_per_step = total_ms / args.steps
-    bytes_rank = algorithmic_bytes(rows, hl, elem)
-    value = tp * bytes_rank / (ms_per_step * 1e-3) / 1e9
-
-    # ---- the same steps replayed from a CUDA graph (no host launch cost)
-    graph_ms = None
-    try:
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        g = torch.cuda.CUDAGraph()
-        n_cap = nsets * max(1, 64 // nsets)
-        with torch.cuda.graph(g, stream=s):
-            for i in range(n_cap):
-                step(i)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        reps = max(1, args.steps // n_cap)
-        g.replay()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            g.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        graph_ms = max_over_ranks([e0.elapsed_time(e1) / (reps * n_cap)], world)[0]
-        del g
-    except Exception as exc:  # reported, not fatal
-        graph_ms = None
-        if rank == 0:
-            print(f"# graph replay skipped: {exc}", file=sys.stderr)
+    eager_ms = max_over_ranks([time_steps(step, args.steps)], world)[0] / args.steps
+    if world > 1:
+        dist.barrier()
 
     # ---- end to end through the public API with pinned host buffers
     x_host = xs[0].cpu().pin_memory()
@@ -359,8 +365,7 @@ def run_our_arm(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    e2e_total, _ = time_steps(e2e_step, e2e_steps, per_launch_events=False)
-    e2e_total = max_over_ranks([e2e_total], world)[0]
+    e2e_total = max_over_ranks([time_steps(e2e_step, e2e_steps)], world)[0]
     e2e_ms = e2e_total / e2e_steps
     e2e_value = tp * bytes_rank / (e2e_ms * 1e-3) / 1e9
 
@@ -377,7 +382,7 @@ def run_our_arm(args):
                "sample": f"{n} full calls of {rows}x{hl} bf16 (TP=1), torch CPU, {cores} threads"}
 
     peak, peak_kind = measured_peak_hbm()
-    achieved = bytes_rank / (kernel_ms * 1e-3) / 1e9
+    achieved = bytes_rank / (graph_ms * 1e-3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(tpath):
@@ -391,28 +396,28 @@ def run_our_arm(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "steps": graph_calls, "warmup": args.warmup, "ms_per_step": round(graph_ms, 6),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": w["name"], "hidden": w["hidden"], "rows": rows, "tp": tp,
                        "local_hidden": hl, "eps": w["eps"], "parallelism": f"tp{tp}",
+                       "launch": "CUDA graph of forward() calls, one kernel each",
                        "l2": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
                              f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB L2)"},
-            "us_per_call": round(ms_per_step * 1e3, 3),
-            "kernel_us": round(kernel_ms * 1e3, 3),
-            "graph_us_per_call": round(graph_ms * 1e3, 3) if graph_ms else None,
-            "graph_value": round(tp * bytes_rank / (graph_ms * 1e-3) / 1e9, 2) if graph_ms else None,
+            "us_per_call": round(graph_ms * 1e3, 3),
+            "eager_us_per_call": round(eager_ms * 1e3, 3),
+            "eager_value": round(tp * bytes_rank / (eager_ms * 1e-3) / 1e9, 2),
+            "kernel": plan_name(rtp, rows, hl, tp),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_kind": peak_kind,
-                         "kernel": "tp_rmsnorm_vec_kernel" if tp > 0 else None,
-                         "bytes_per_launch": bytes_rank},
+                         "peak_kind": peak_kind, "bytes_per_launch": bytes_rank,
+                         "per_launch_us": round(graph_ms * 1e3, 3)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
                     "ms_per_step": round(e2e_ms, 4), "path": "FusedTPRMSNorm.forward"},
             "cpu_baseline": cpu,
-            "gpu_launches": args.steps,
+            "gpu_launches": graph_calls,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -462,41 +467,20 @@ def run_sweeps(args, module, group, world, rank, dev):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        total, per = time_steps(step, steps)
-        eager_us, kern_us = [v * 1e3 for v in max_over_ranks([total / steps, per], world)]
+        eager_us = max_over_ranks([time_steps(step, steps)], world)[0] * 1e3 / steps
         graph_us = None
         try:
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            g = torch.cuda.CUDAGraph()
-            ncap = max(n, 100)
-            with torch.cuda.graph(g, stream=s):
-                for i in range(ncap):
-                    step(i)
-            torch.cuda.synchronize()
-            if world > 1:
-                dist.barrier()
-            g.replay()
-            torch.cuda.synchronize()
-            reps = max(1, steps // ncap)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            if world > 1:
-                dist.barrier()
-            e0.record()
-            for _ in range(reps):
-                g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            graph_us = max_over_ranks([e0.elapsed_time(e1) * 1e3 / (reps * ncap)], world)[0]
-            del g
+            graph_ms, _ = time_graph(step, max(n, min(100, steps)), steps, world)
+            graph_us = graph_ms * 1e3
         except Exception as exc:
             if rank == 0:
                 print(f"# graph skipped: {exc}", file=sys.stderr)
         b = algorithmic_bytes(rows, hl, elem)
         return {"rows": rows, "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
-                "eager_us_per_call": round(eager_us, 3), "kernel_us": round(kern_us, 3),
+                "family": rtp.get_kernel_family(),
+                "eager_us_per_call": round(eager_us, 3),
                 "graph_us_per_call": round(graph_us, 3) if graph_us else None,
-                "kernel_GBps_per_rank": round(b / (kern_us * 1e-6) / 1e9, 1),
+                "eager_GBps_per_rank": round(b / (eager_us * 1e-6) / 1e9, 1),
                 "graph_GBps_per_rank": round(b / (graph_us * 1e-6) / 1e9, 1) if graph_us else None,
                 "bytes_per_rank": b, "rotating_sets": n}
 

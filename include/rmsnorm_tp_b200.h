@@ -55,7 +55,8 @@ enum rmsnorm_tp_error {
 enum rmsnorm_tp_device_status {
   RMSNORM_TP_STATUS_OK = 0,
   RMSNORM_TP_STATUS_TIMEOUT = 1,  /* a wait for a peer's partial sum ran out */
-  RMSNORM_TP_STATUS_ABORTED = 2   /* gave up because another CTA timed out */
+  RMSNORM_TP_STATUS_ABORTED = 2,  /* gave up because another CTA timed out */
+  RMSNORM_TP_STATUS_LOAD_TIMEOUT = 3  /* a bulk copy into shared memory never completed */
 };
 
 typedef struct rmsnorm_tp_comm rmsnorm_tp_comm;
@@ -179,8 +180,17 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp,
 int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
                                void* stream, int64_t* dev_out_ns);
 
-/* The launch plan the forward call would use (pure host arithmetic; no GPU). */
-int rmsnorm_tp_plan(int64_t rows, int64_t local_hidden, int dtype, int aligned,
+/* Kernel family used by every later launch of this process:
+ * 0 = automatic (bulk-copy kernels where eligible), 1 = register kernels only,
+ * 2 = bulk-copy kernels where eligible (same as 0 today). For tests and
+ * benchmarks that compare the two implementations. */
+int rmsnorm_tp_set_kernel_family(int family);
+int rmsnorm_tp_get_kernel_family(void);
+
+/* The launch plan the forward call would use (pure host arithmetic; no GPU).
+ * variant: -1 generic, 0..7 register kernels, >= 100 bulk-copy kernels
+ * (vec_per_lane then = stages per warp, rows_per_tile = rows per stage). */
+int rmsnorm_tp_plan(int64_t rows, int64_t local_hidden, int dtype, int aligned, int tp,
                     int resident_ctas, rmsnorm_tp_plan_info* out);
 
 /* Count, for every row, how many teams of `plan` visit it (coverage check of

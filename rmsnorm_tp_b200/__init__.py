@@ -18,6 +18,8 @@ from .api import (
     local_rmsnorm,
     plan,
     plan_coverage,
+    set_kernel_family,
+    get_kernel_family,
     tag_of,
 )
 
@@ -33,6 +35,8 @@ __all__ = [
     "plan",
     "plan_coverage",
     "tag_of",
+    "set_kernel_family",
+    "get_kernel_family",
     "buffer_of",
     "dtype_code",
 ]

@@ -18,7 +18,9 @@ F32, BF16, F16 = 0, 1, 2
 # enum rmsnorm_tp_error
 OK, ERR_INVALID, ERR_CUDA, ERR_STATE, ERR_ROWS, ERR_DEVICE, ERR_HANDLE = range(7)
 # enum rmsnorm_tp_device_status
-STATUS_OK, STATUS_TIMEOUT, STATUS_ABORTED = 0, 1, 2
+STATUS_OK, STATUS_TIMEOUT, STATUS_ABORTED, STATUS_LOAD_TIMEOUT = 0, 1, 2, 3
+# kernel families (rmsnorm_tp_set_kernel_family)
+FAMILY_AUTO, FAMILY_REGISTER, FAMILY_BULK = 0, 1, 2
 
 MAX_TP = 8
 HANDLE_BYTES = 128
@@ -91,7 +93,9 @@ SIGNATURES = {
         ],
     ),
     "rmsnorm_tp_probe_roundtrip": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p]),
-    "rmsnorm_tp_plan": (_i32, [_i64, _i64, _i32, _i32, _i32, ctypes.POINTER(PlanInfo)]),
+    "rmsnorm_tp_plan": (_i32, [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(PlanInfo)]),
+    "rmsnorm_tp_set_kernel_family": (_i32, [_i32]),
+    "rmsnorm_tp_get_kernel_family": (_i32, []),
     "rmsnorm_tp_plan_coverage": (_i32, [ctypes.POINTER(PlanInfo), _i64, ctypes.POINTER(ctypes.c_int32)]),
     "rmsnorm_tp_tag_of": (_u32, [_u64]),
     "rmsnorm_tp_buffer_of": (_u32, [_u64]),
@@ -116,7 +120,7 @@ def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"rmsnorm_tp_b200: native library {LIB_PATH} is missing; build it with "
-            "`python -m rmsnorm_tp_b200.build` (needs nvcc). There is no CPU fallback."
+            "`python rmsnorm_tp_b200/build.py` (needs nvcc). There is no CPU fallback."
         )
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

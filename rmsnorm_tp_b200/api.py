@@ -388,12 +388,12 @@ class EmulatedTPGroup:
             b.destroy()
 
 
-def plan(rows: int, local_hidden: int, dtype: torch.dtype, aligned: bool = True,
+def plan(rows: int, local_hidden: int, dtype: torch.dtype, aligned: bool = True, tp: int = 1,
          resident_ctas: int = 148 * 2) -> dict:
     """Launch plan the forward call would use (host arithmetic only)."""
     info = _lib.PlanInfo()
-    check(LIB.rmsnorm_tp_plan(rows, local_hidden, dtype_code(dtype), int(aligned), resident_ctas,
-                              ctypes.byref(info)), "rmsnorm_tp_plan")
+    check(LIB.rmsnorm_tp_plan(rows, local_hidden, dtype_code(dtype), int(aligned), tp,
+                              resident_ctas, ctypes.byref(info)), "rmsnorm_tp_plan")
     return {name: getattr(info, name) for name, _ in info._fields_}
 
 
@@ -403,6 +403,16 @@ def plan_coverage(plan_dict: dict, rows: int):
     counts = (ctypes.c_int32 * max(rows, 1))()
     check(LIB.rmsnorm_tp_plan_coverage(ctypes.byref(info), rows, counts), "rmsnorm_tp_plan_coverage")
     return list(counts)[:rows]
+
+
+def set_kernel_family(family: str) -> None:
+    """Process-wide kernel family: "auto", "register" or "bulk" (tests, benchmarks)."""
+    code = {"auto": _lib.FAMILY_AUTO, "register": _lib.FAMILY_REGISTER, "bulk": _lib.FAMILY_BULK}[family]
+    check(LIB.rmsnorm_tp_set_kernel_family(code), "rmsnorm_tp_set_kernel_family")
+
+
+def get_kernel_family() -> str:
+    return {0: "auto", 1: "register", 2: "bulk"}[LIB.rmsnorm_tp_get_kernel_family()]
 
 
 def tag_of(generation: int) -> int:

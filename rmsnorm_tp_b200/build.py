@@ -5,8 +5,10 @@ kernels and their launcher, comm.cpp the extern "C" entry points declared in
 include/rmsnorm_tp_b200.h. The CUDA runtime is linked statically, so the
 library loads (and its symbols can be listed) on a machine without a GPU.
 
-    python -m rmsnorm_tp_b200.build          # build if sources are newer
-    python -m rmsnorm_tp_b200.build --force  # always rebuild
+    python rmsnorm_tp_b200/build.py          # build if sources are newer
+    python rmsnorm_tp_b200/build.py --force  # always rebuild
+
+(Run it as a file: importing the package loads the library it builds.)
 """
 from __future__ import annotations
 

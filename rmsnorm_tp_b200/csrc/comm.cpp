@@ -507,14 +507,23 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* c, int peer, int iters, void* st
   return RMSNORM_TP_OK;
 }
 
-int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int resident_ctas,
+int rmsnorm_tp_set_kernel_family(int family) {
+  if (family < rtp::kFamilyAuto || family > rtp::kFamilyBulk)
+    return fail(RMSNORM_TP_ERR_INVALID, "set_kernel_family: unknown family %d", family);
+  rtp::set_family(family);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_get_kernel_family(void) { return rtp::get_family(); }
+
+int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int tp, int resident_ctas,
                     rmsnorm_tp_plan_info* out) {
   if (!out) return fail(RMSNORM_TP_ERR_INVALID, "plan: NULL out");
   if (!valid_dtype(dtype)) return fail(RMSNORM_TP_ERR_INVALID, "plan: unknown dtype %d", dtype);
-  if (rows < 0 || hl < 1 || resident_ctas < 1)
-    return fail(RMSNORM_TP_ERR_INVALID, "plan: rows %lld, local_hidden %lld, resident %d",
-                (long long)rows, (long long)hl, resident_ctas);
-  const rtp::VariantDesc v = rtp::choose_variant(hl, dtype, aligned != 0);
+  if (rows < 0 || hl < 1 || resident_ctas < 1 || tp < 1 || tp > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "plan: rows %lld, local_hidden %lld, tp %d, resident %d",
+                (long long)rows, (long long)hl, tp, resident_ctas);
+  const rtp::VariantDesc v = rtp::choose_variant(hl, dtype, aligned != 0, tp, rows);
   const rtp::Plan p = rtp::plan_for(v, rows, resident_ctas);
   out->variant = p.variant;
   out->vec_per_lane = p.vec_per_lane;

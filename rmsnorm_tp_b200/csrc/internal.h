@@ -31,23 +31,35 @@ struct KArgs {
   int rank;                            // this rank (normal launch)
   int tp;
   int emulated;                        // 1: every rank in one launch, rank = blockIdx.y
+  int tile_rows;                       // bulk kernels: rows per shared-memory stage
+  unsigned int stage_bytes;            // bulk kernels: bytes per stage (multiple of 128)
   int pad_;
   unsigned long long timeout_ns;
 };
 
 enum Dtype { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
+// Kernel family selection (process-wide): automatic, or one family forced.
+enum Family { kFamilyAuto = 0, kFamilyRegister = 1, kFamilyBulk = 2 };
+void set_family(int family);
+int get_family();
+
 // Shape of a kernel variant (template parameters of the vectorised kernel).
 struct VariantDesc {
-  int id;              // -1 = generic
-  int vec_per_lane;
-  int team_warps;
+  int id;              // -1 = generic, 0..kNumShapes-1 register kernels, >= kBulkBase bulk kernels
+  int vec_per_lane;    // register kernels: 16-byte vectors per lane; bulk: stages per warp
+  int team_warps;      // warps sharing one row (bulk: 1)
   int rows_per_tile;
   int block_threads;
+  unsigned int stage_bytes;   // bulk kernels only
+  unsigned int smem_bytes;    // dynamic shared memory of the launch
 };
 
+constexpr int kBulkBase = 100;
+
 int elem_bytes(int dtype);
-VariantDesc choose_variant(int64_t hl, int dtype, bool aligned);
+VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp = 1, int64_t rows = 0,
+                           int family = kFamilyAuto);
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
 
 // Launch the forward kernel. grid_y > 1 only for the emulated (all ranks on one

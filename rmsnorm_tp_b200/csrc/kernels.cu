@@ -141,37 +141,28 @@ __device__ __forceinline__ uint4 normalize16(const uint4& xv, const uint4& wv, f
 __device__ __forceinline__ float quiet_nan() { return __uint_as_float(0x7FC00000u); }
 
 // ---------------------------------------------------------------------------
-// Cross-GPU exchange of the partial sums of up to kRows rows, by one warp.
-// Lane L serves row r = L / tp and rank q = L % tp: it pushes the row's local
-// partial into rank q's mailbox and waits for rank q's partial in the local
-// one. Every lane returns S[i] = sum over ranks in rank order.
-// Returns false (warp-uniform) if any wait gave up; the failure is recorded in
-// the rank's DeviceState and mirrored to the host-mapped flag.
+// Cross-GPU exchange, one lane's share: push this rank's partial of `row` into
+// rank q's mailbox slot [buf][rank][row], then wait (bounded by the global
+// timer) until slot [buf][q][row] of the local mailbox carries `tag`, and
+// return rank q's partial. Lanes with q == rank or !active return `mine`.
+// A timeout is recorded in the rank's DeviceState (first failure wins) and
+// mirrored to the host-mapped flag; it also raises `abort`, which makes every
+// other wait of this launch give up at once.
 // ---------------------------------------------------------------------------
-template <int kRows>
-__device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, const RankPtrs& rp,
-                                                  uint32_t buf, uint32_t tag,
-                                                  unsigned long long call, int64_t row0,
-                                                  int nrows, const float (&ss)[kRows],
-                                                  float (&S)[kRows]) {
-  const int lane = threadIdx.x & 31;
+__device__ __forceinline__ float push_poll(const KArgs& a, int rank, const RankPtrs& rp,
+                                           uint32_t buf, uint32_t tag, unsigned long long call,
+                                           int64_t row, int q, bool active, float mine,
+                                           bool& failed) {
   const int tp = a.tp;
-  const int r = lane / tp;
-  const int q = lane - r * tp;
-  const bool remote = (r < nrows) && (q != rank);
-  float mine = 0.f;
-#pragma unroll
-  for (int i = 0; i < kRows; ++i)
-    if (i == r) mine = ss[i];
-
+  const bool remote = active && (q != rank);
   if (remote) {
-    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, tp, a.nmax, row0 + r);
+    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, tp, a.nmax, row);
     ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
   }
   float val = mine;
   uint32_t fail = kStatusOk;
   if (remote) {
-    const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, tp, a.nmax, row0 + r);
+    const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, tp, a.nmax, row);
     unsigned long long w = ptx::ld_relaxed_sys_u64(src);
     if (slot_tag(w) != tag) {
       const unsigned long long t0 = ptx::globaltimer();
@@ -192,7 +183,7 @@ __device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, cons
       DeviceState* st = rp.state;
       if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {
         st->err_src = (unsigned)q;
-        st->err_row = (long long)(row0 + r);
+        st->err_row = (long long)row;
         st->err_expected = tag;
         st->err_seen = slot_tag(w);
         st->err_call = call;
@@ -205,7 +196,31 @@ __device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, cons
     }
     val = slot_value(w);
   }
-  const bool any_fail = __any_sync(0xFFFFFFFFu, fail != kStatusOk);
+  failed = (fail != kStatusOk);
+  return val;
+}
+
+// Exchange of the partial sums of up to kRows rows by one warp (register
+// kernels). Lane L serves row r = L / tp and rank q = L % tp; every lane
+// returns S[i] = sum over ranks, in rank order, of row i's partials. Returns
+// false (warp-uniform) if any wait gave up.
+template <int kRows>
+__device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, const RankPtrs& rp,
+                                                  uint32_t buf, uint32_t tag,
+                                                  unsigned long long call, int64_t row0,
+                                                  int nrows, const float (&ss)[kRows],
+                                                  float (&S)[kRows]) {
+  const int lane = threadIdx.x & 31;
+  const int tp = a.tp;
+  const int r = lane / tp;
+  const int q = lane - r * tp;
+  float mine = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRows; ++i)
+    if (i == r) mine = ss[i];
+  bool failed = false;
+  const float val = push_poll(a, rank, rp, buf, tag, call, row0 + r, q, r < nrows, mine, failed);
+  const bool any_fail = __any_sync(0xFFFFFFFFu, failed);
 #pragma unroll
   for (int i = 0; i < kRows; ++i) {
     float s = 0.f;
@@ -421,6 +436,170 @@ __global__ void __launch_bounds__(kBlock)
 }
 
 // ---------------------------------------------------------------------------
+// Bulk-copy kernel (the default for aligned rows of up to 16 KB).
+//
+// Every warp owns a ring of kStages shared-memory stages. A stage holds one
+// tile of tile_rows consecutive rows -- one contiguous span of x -- fetched by a
+// single cp.async.bulk (TMA) copy that signals an mbarrier with its byte
+// count. Lane 0 keeps kStages - 1 tiles in flight ahead of the one the warp
+// works on, so the bytes in flight per SM are set by shared memory (up to
+// ~200 KB), not by registers, and the exchange wait of one tile overlaps the
+// loads of the next ones. The weight row is staged once per CTA in shared
+// memory. x is read from HBM once (then twice from shared memory: sum of
+// squares, normalisation); y is written with 128-bit stores.
+// Tiles go to warps round-robin (tile t -> warp t mod all warps), the same
+// on every rank, over a grid of at most one resident wave.
+// ---------------------------------------------------------------------------
+constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  unsigned long long limit_ns) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (;;) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (ptx::globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
+template <typename T, int kWarps, int kStages>
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    tp_rmsnorm_bulk_kernel(const __grid_constant__ KArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) unsigned long long s_bar[kWarps][kStages];
+  __shared__ float s_part[kWarps][32];
+  __shared__ float s_sum[kWarps][32];
+  __shared__ unsigned long long s_call;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const int V = (int)(a.hl / Pack<T>::kE);                  // 16-byte vectors per row
+  const uint32_t row_bytes = (uint32_t)a.hl * (uint32_t)sizeof(T);
+  const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
+  const int tile_rows = a.tile_rows;
+  const uint32_t stage_bytes = a.stage_bytes;
+  const bool exchange = a.tp > 1;
+
+  unsigned char* ring = smem + w_bytes + (size_t)warp * kStages * stage_bytes;
+  const uint32_t ring_addr = ptx::smem_addr(ring);
+  const uint32_t bar0 = ptx::smem_addr(&s_bar[warp][0]);
+  const int64_t tiles = (a.rows + tile_rows - 1) / tile_rows;
+  const int64_t nw = (int64_t)gridDim.x * kWarps;
+  const int64_t wgid = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t my_tiles = wgid < tiles ? (tiles - 1 - wgid) / nw + 1 : 0;
+  const unsigned char* xg = reinterpret_cast<const unsigned char*>(rp.x);
+
+  auto issue = [&](int64_t kk, int st) {   // lane 0: fetch the warp's kk-th tile into stage st
+    const int64_t row0 = (wgid + kk * nw) * tile_rows;
+    const int nr = (int)min((int64_t)tile_rows, a.rows - row0);
+    const uint32_t bytes = (uint32_t)nr * row_bytes;
+    const uint32_t bar = bar0 + 8u * (uint32_t)st;
+    ptx::mbar_arrive_expect_tx(bar, bytes);
+    ptx::bulk_load(ring_addr + (uint32_t)st * stage_bytes, xg + row0 * (int64_t)row_bytes, bytes, bar);
+  };
+
+  if (lane == 0) {
+#pragma unroll
+    for (int st = 0; st < kStages; ++st) ptx::mbar_init(bar0 + 8u * st, 1u);
+    ptx::fence_mbar_init();
+    for (int st = 0; st < kStages && st < my_tiles; ++st) issue(st, st);
+  }
+  // weight row -> shared memory while the first tiles are in flight
+  const uint4* wg = reinterpret_cast<const uint4*>(rp.w);
+  uint4* wsm = reinterpret_cast<uint4*>(smem);
+  for (int v = threadIdx.x; v < V; v += kWarps * 32) wsm[v] = ptx::ld_cached_v4(wg + v);
+  if (exchange && threadIdx.x == 0)
+    s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
+  __syncthreads();
+
+  unsigned long long call = 0ull;
+  uint32_t buf = 0u, tag = 0u;
+  if (exchange) {
+    call = s_call;
+    buf = buffer_of(call);
+    tag = tag_of(call);
+  }
+  uint4* yg = reinterpret_cast<uint4*>(rp.out);
+
+  int64_t k = 0;
+  bool load_ok = true;
+  for (; k < my_tiles; ++k) {
+    const int st = (int)(k % kStages);
+    if (!mbar_wait_bounded(bar0 + 8u * st, (uint32_t)((k / kStages) & 1), kLoadTimeoutNs)) {
+      load_ok = false;
+      break;
+    }
+    const int64_t row0 = (wgid + k * nw) * tile_rows;
+    const int nr = (int)min((int64_t)tile_rows, a.rows - row0);
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + (size_t)st * stage_bytes);
+
+    for (int r = 0; r < nr; ++r) {
+      const uint4* xr = xs + r * V;
+      float acc0 = 0.f, acc1 = 0.f;
+      int v = lane;
+      for (; v + 32 < V; v += 64) {
+        acc0 += sumsq16<T>(xr[v]);
+        acc1 += sumsq16<T>(xr[v + 32]);
+      }
+      if (v < V) acc0 += sumsq16<T>(xr[v]);
+      const float ss = warp_allreduce_sum(acc0 + acc1);
+      if (lane == 0) s_part[warp][r] = ss;
+    }
+    __syncwarp();
+    bool ok = true;
+    if (exchange) {
+      const int tp = a.tp;
+      const int r = lane / tp;
+      const int q = lane - r * tp;
+      const bool active = r < nr;
+      bool failed = false;
+      const float val = push_poll(a, rank, rp, buf, tag, call, row0 + r, q, active,
+                                  active ? s_part[warp][r] : 0.f, failed);
+      ok = !__any_sync(0xFFFFFFFFu, failed);
+      float S = 0.f;
+      for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, r * tp + p);
+      if (active && q == 0) s_sum[warp][r] = S;
+    } else if (lane < nr) {
+      s_sum[warp][lane] = s_part[warp][lane];
+    }
+    __syncwarp();
+    for (int r = 0; r < nr; ++r) {
+      const float inv = ok ? rsqrtf(s_sum[warp][r] / a.hidden_f + a.eps) : quiet_nan();
+      const uint4* xr = xs + r * V;
+      uint4* yr = yg + (row0 + r) * (int64_t)V;
+      for (int v = lane; v < V; v += 32) ptx::st_v4(yr + v, normalize16<T>(xr[v], wsm[v], inv));
+    }
+    __syncwarp();
+    if (lane == 0 && k + kStages < my_tiles) {
+      ptx::fence_proxy_async_smem();   // our reads of stage st before the copy that refills it
+      issue(k + kStages, st);
+    }
+  }
+  if (!load_ok) {
+    // A copy never landed: record it, then wait (bounded) for the copies still
+    // in flight so none of them lands in shared memory this CTA no longer owns.
+    if (lane == 0 && rp.state != nullptr) {
+      if (atomicCAS(&rp.state->err_code, 0u, (unsigned)kStatusLoadTimeout) == 0u) {
+        rp.state->err_call = call;
+        if (rp.host_flag != nullptr) {
+          *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusLoadTimeout;
+          __threadfence_system();
+        }
+      }
+      atomicExch(&rp.state->abort, 1u);
+    }
+    const int64_t end = min(my_tiles, k + kStages);
+    for (int64_t kk = k; kk < end; ++kk)
+      mbar_wait_bounded(bar0 + 8u * (uint32_t)(kk % kStages), (uint32_t)((kk / kStages) & 1),
+                        kLoadTimeoutNs);
+  }
+  if (exchange) finish_launch(rp.state, call);
+}
+
+// ---------------------------------------------------------------------------
 // One-hop latency probe: a single thread bounces a counter between two GPUs.
 // ---------------------------------------------------------------------------
 __global__ void probe_roundtrip_kernel(unsigned long long* remote_slot,
@@ -460,8 +639,8 @@ namespace {
 struct VariantShape {
   int vec, w, rows, block;
 };
-// Selected by the number of 16-byte vectors per row, V: the first entry whose
-// capacity 32 * w * vec >= V.
+// Register kernels, selected by the number of 16-byte vectors per row, V: the
+// first entry whose capacity 32 * w * vec >= V.
 constexpr VariantShape kShapes[] = {
     {1, 1, 4, 256},   // V <= 32     (bf16 hl <= 256,   fp32 hl <= 128)
     {2, 1, 2, 256},   // V <= 64     (bf16 hl <= 512,   fp32 hl <= 256)
@@ -475,6 +654,14 @@ constexpr VariantShape kShapes[] = {
 constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 constexpr int kGenericBlock = 256;
 
+// Bulk kernels: warps per CTA (3 stages each).
+constexpr int kBulkStages = 3;
+constexpr int kBulkWarps[] = {4, 8, 16};
+constexpr int kNumBulk = sizeof(kBulkWarps) / sizeof(kBulkWarps[0]);
+constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
+constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
+constexpr int kSlots = kNumShapes + 1 + kNumBulk;     // register, generic, bulk
+
 using KernelFn = void (*)(const KArgs);
 
 template <typename T>
@@ -485,59 +672,109 @@ struct KernelTable {
       tp_rmsnorm_vec_kernel<T, 8, 2, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 4, 1, 256>,
       tp_rmsnorm_vec_kernel<T, 8, 8, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 16, 1, 512>,
   };
+  static constexpr KernelFn bulk[kNumBulk] = {
+      tp_rmsnorm_bulk_kernel<T, 4, kBulkStages>,
+      tp_rmsnorm_bulk_kernel<T, 8, kBulkStages>,
+      tp_rmsnorm_bulk_kernel<T, 16, kBulkStages>,
+  };
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
+  static KernelFn get(int variant) {
+    if (variant < 0) return generic;
+    if (variant >= kBulkBase) return bulk[variant - kBulkBase];
+    return vec[variant];
+  }
 };
 
 KernelFn kernel_for(int dtype, int variant) {
   switch (dtype) {
     case kF32:
-      return variant < 0 ? KernelTable<float>::generic : KernelTable<float>::vec[variant];
+      return KernelTable<float>::get(variant);
     case kBF16:
-      return variant < 0 ? KernelTable<__nv_bfloat16>::generic
-                         : KernelTable<__nv_bfloat16>::vec[variant];
+      return KernelTable<__nv_bfloat16>::get(variant);
     default:
-      return variant < 0 ? KernelTable<__half>::generic : KernelTable<__half>::vec[variant];
+      return KernelTable<__half>::get(variant);
   }
 }
 
-constexpr int kMaxDevices = 64;
-// resident CTAs per device/dtype/variant (+1 slot for generic); 0 = not yet computed
-std::atomic<int> g_resident[kMaxDevices][3][kNumShapes + 1];
+int slot_of(int variant) {
+  if (variant < 0) return kNumShapes;
+  if (variant >= kBulkBase) return kNumShapes + 1 + (variant - kBulkBase);
+  return variant;
+}
 
-int resident_ctas(int device, int dtype, int variant, int block, cudaError_t* err) {
+std::atomic<int> g_family{kFamilyAuto};
+
+constexpr int kMaxDevices = 64;
+// Per device/dtype/variant: (dynamic smem bytes << 32) | resident CTAs of the
+// last occupancy query; 0 = none yet. Bulk kernels also get their max dynamic
+// shared memory raised once (bit 31 of g_attr_set).
+std::atomic<unsigned long long> g_resident[kMaxDevices][3][kSlots];
+std::atomic<unsigned int> g_attr_set[kMaxDevices][3][kSlots];
+
+int resident_ctas(int device, int dtype, const VariantDesc& v, cudaError_t* err) {
   *err = cudaSuccess;
-  const int slot = variant < 0 ? kNumShapes : variant;
-  if (device >= 0 && device < kMaxDevices) {
-    const int cached = g_resident[device][dtype][slot].load(std::memory_order_relaxed);
-    if (cached > 0) return cached;
+  const int slot = slot_of(v.id);
+  const bool cacheable = device >= 0 && device < kMaxDevices;
+  const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
+  if (cacheable) {
+    const unsigned long long c = g_resident[device][dtype][slot].load(std::memory_order_relaxed);
+    if (c != 0ull && (unsigned)(c >> 32) == v.smem_bytes) return (int)(c & 0xFFFFFFFFull);
+  }
+  if (v.smem_bytes > 48u * 1024u && (!cacheable || g_attr_set[device][dtype][slot].load() == 0u)) {
+    *err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kBulkSmemBudget);
+    if (*err != cudaSuccess) return 0;
+    if (cacheable) g_attr_set[device][dtype][slot].store(1u);
   }
   int per_sm = 0, sms = 0;
-  *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &per_sm, reinterpret_cast<const void*>(kernel_for(dtype, variant)), block, 0);
+  *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, v.block_threads,
+                                                       (size_t)v.smem_bytes);
   if (*err != cudaSuccess) return 0;
   *err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (*err != cudaSuccess) return 0;
   const int total = per_sm * sms;
-  if (device >= 0 && device < kMaxDevices && total > 0)
-    g_resident[device][dtype][slot].store(total, std::memory_order_relaxed);
+  if (cacheable && total > 0)
+    g_resident[device][dtype][slot].store(((unsigned long long)v.smem_bytes << 32) | (unsigned)total,
+                                          std::memory_order_relaxed);
   return total;
 }
 
 }  // namespace
 
+void set_family(int family) { g_family.store(family); }
+int get_family() { return g_family.load(); }
+
 int elem_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
 
-VariantDesc choose_variant(int64_t hl, int dtype, bool aligned) {
+VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family) {
+  (void)rows;
   const int eb = elem_bytes(dtype);
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
+  if (family == kFamilyAuto) family = get_family();
+  if (vec_ok && family != kFamilyRegister && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
+    const uint32_t row_bytes = (uint32_t)(hl * eb);
+    const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
+    const int max_rows = tp > 1 ? 32 / tp : 32;          // one lane per (row, rank) in the exchange
+    const uint32_t target = row_bytes <= 8192u ? 8192u : row_bytes;
+    int tile_rows = (int)(target / row_bytes);
+    if (tile_rows > max_rows) tile_rows = max_rows;
+    if (tile_rows < 1) tile_rows = 1;
+    const uint32_t stage = ((uint32_t)tile_rows * row_bytes + 127u) & ~127u;
+    for (int i = kNumBulk - 1; i >= 0; --i) {
+      const uint32_t smem = w_bytes + (uint32_t)kBulkWarps[i] * kBulkStages * stage;
+      if (smem <= kBulkSmemBudget)
+        return VariantDesc{kBulkBase + i, kBulkStages, 1, tile_rows, kBulkWarps[i] * 32, stage, smem};
+    }
+  }
   if (vec_ok) {
     const int64_t V = hl * eb / 16;
     for (int i = 0; i < kNumShapes; ++i) {
       const int64_t cap = 32ll * kShapes[i].w * kShapes[i].vec;
-      if (V <= cap) return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block};
+      if (V <= cap)
+        return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u};
     }
   }
-  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock};
+  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u};
 }
 
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
@@ -556,30 +793,33 @@ Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
   return p;
 }
 
-cudaError_t launch_forward(const KArgs& a, int dtype, int device, int grid_y,
+cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
                            cudaStream_t stream, Plan* plan_out) {
-  const int nranks = a.emulated ? grid_y : 1;
+  const int nranks = a_in.emulated ? grid_y : 1;
   bool aligned = true;
   for (int r = 0; r < nranks; ++r) {
-    const uintptr_t bits = reinterpret_cast<uintptr_t>(a.rp[r].x) |
-                           reinterpret_cast<uintptr_t>(a.rp[r].out) |
-                           reinterpret_cast<uintptr_t>(a.rp[r].w);
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(a_in.rp[r].x) |
+                           reinterpret_cast<uintptr_t>(a_in.rp[r].out) |
+                           reinterpret_cast<uintptr_t>(a_in.rp[r].w);
     if (bits & 15u) aligned = false;
   }
-  const VariantDesc v = choose_variant(a.hl, dtype, aligned);
+  const VariantDesc v = choose_variant(a_in.hl, dtype, aligned, a_in.tp, a_in.rows);
   cudaError_t err = cudaSuccess;
-  int resident = resident_ctas(device, dtype, v.id, v.block_threads, &err);
+  int resident = resident_ctas(device, dtype, v, &err);
   if (err != cudaSuccess) return err;
   if (grid_y > 1) resident /= grid_y;
   if (resident < 1) return cudaErrorCooperativeLaunchTooLarge;
-  const Plan p = plan_for(v, a.rows, resident);
+  const Plan p = plan_for(v, a_in.rows, resident);
   if (plan_out) *plan_out = p;
+  KArgs a = a_in;
+  a.tile_rows = v.rows_per_tile;
+  a.stage_bytes = v.stage_bytes;
   const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
-  void* args[] = {const_cast<KArgs*>(&a)};
+  void* args[] = {&a};
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
   const dim3 block((unsigned)p.block_threads);
-  if (grid_y > 1) return cudaLaunchCooperativeKernel(fn, grid, block, args, 0, stream);
-  return cudaLaunchKernel(fn, grid, block, args, 0, stream);
+  if (grid_y > 1) return cudaLaunchCooperativeKernel(fn, grid, block, args, v.smem_bytes, stream);
+  return cudaLaunchKernel(fn, grid, block, args, v.smem_bytes, stream);
 }
 
 cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,

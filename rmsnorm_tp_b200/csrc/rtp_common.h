@@ -36,6 +36,7 @@ enum DeviceStatus : uint32_t {
   kStatusOk = 0,
   kStatusTimeout = 1,   // a peer's partial sum did not arrive within the limit
   kStatusAborted = 2,   // gave up because another CTA on this GPU timed out
+  kStatusLoadTimeout = 3,  // a bulk copy into shared memory did not complete in time
 };
 
 // Per-rank state in local device memory (never mapped to peers).

@@ -45,3 +45,13 @@ def _require_cuda_for_gpu_tests(request):
         import torch
 
         assert torch.cuda.is_available(), "GPU test run without a CUDA device"
+
+
+@pytest.fixture(params=["bulk", "register"])
+def family(request):
+    """Run a test once per kernel family (bulk-copy and register kernels)."""
+    import rmsnorm_tp_b200 as rtp
+
+    rtp.set_kernel_family(request.param)
+    yield request.param
+    rtp.set_kernel_family("auto")

@@ -74,7 +74,7 @@ LOCAL_WIDTHS = [8, 37, 64, 96, 256, 384, 512, 1000, 1024, 2048, 3000, 4096, 8192
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 @pytest.mark.parametrize("hidden", LOCAL_WIDTHS)
 @pytest.mark.parametrize("rows", [1, 3, 64, 257])
-def test_local_kernel_sweep(dtype, hidden, rows):
+def test_local_kernel_sweep(family, dtype, hidden, rows):
     xs, ws = make_group(rows, hidden, 1, TORCH_DTYPES[dtype], 1000 + hidden + rows)
     x, w = xs[0].cuda(), ws[0].cuda()
     y = rtp.local_rmsnorm(x, w, 1e-6)
@@ -82,11 +82,11 @@ def test_local_kernel_sweep(dtype, hidden, rows):
     _assert_ok(check_against_oracle(dtype, [x], [w], 1e-6, [y]), f"{dtype} {hidden} {rows}")
 
 
-@pytest.mark.parametrize("tp", [2, 4, 8])
+@pytest.mark.parametrize("tp", [2, 3, 4, 8])
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 @pytest.mark.parametrize("hl", [37, 64, 512, 1024, 2048, 4096])
 @pytest.mark.parametrize("rows", [1, 7, 300])
-def test_emulated_group_sweep(tp, dtype, hl, rows):
+def test_emulated_group_sweep(family, tp, dtype, hl, rows):
     xs, ws = make_group(rows, hl * tp, tp, TORCH_DTYPES[dtype], 7 * hl + rows)
     xs = [x.cuda() for x in xs]
     ws = [w.cuda() for w in ws]
@@ -129,7 +129,7 @@ def test_unaligned_pointers_take_the_generic_kernel():
 @pytest.mark.parametrize("tp,rank", [(2, 0), (2, 1), (4, 2), (8, 5)])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 @pytest.mark.parametrize("hl,rows", [(1024, 1), (512, 77), (2048, 300), (4096, 5)])
-def test_forward_entry_point_with_host_written_peer_slots(tp, rank, dtype, hl, rows):
+def test_forward_entry_point_with_host_written_peer_slots(family, tp, rank, dtype, hl, rows):
     """rmsnorm_tp_forward at TP > 1 on one GPU. Before each call the host writes
     the other ranks' {partial, tag} words into this rank's mailbox, as their
     pushes would; the peers' mailboxes are device buffers that must receive
@@ -185,7 +185,7 @@ def _sampled_oracle_check(dtype, xs, ws, eps, outs, n=96, seed=0):
 
 
 @pytest.mark.parametrize("tp", [1, 2, 4, 8])
-def test_llama3_8b_config_full_size(tp):
+def test_llama3_8b_config_full_size(family, tp):
     cfg = BY_NAME["llama3_8b"]
     rows = cfg.rows[0]
     xs, ws = make_group(rows, cfg.hidden, tp, cfg.dtype, cfg.seed_base, device="cuda")
@@ -222,7 +222,7 @@ def test_rows_are_independent_permutation_equivariance():
         assert torch.equal(a[perm].view(torch.int16), b.view(torch.int16))
 
 
-def test_stress_pattern_zero_rows_and_outlier_channels():
+def test_stress_pattern_zero_rows_and_outlier_channels(family):
     cfg = BY_NAME["stress"]
     tp, rows = 8, 4096
     xs, ws = make_group(rows, cfg.hidden, tp, cfg.dtype, cfg.seed_base, stress=True, device="cuda")
@@ -244,7 +244,7 @@ def test_stress_pattern_zero_rows_and_outlier_channels():
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_prefill_config_full_size_tp8(dtype):
+def test_prefill_config_full_size_tp8(family, dtype):
     cfg = BY_NAME["prefill"]
     tp, rows = 8, 65536
     xs, ws = make_group(rows, cfg.hidden, tp, TORCH_DTYPES[dtype], cfg.seed_base, device="cuda")

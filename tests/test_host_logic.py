@@ -21,39 +21,76 @@ def test_tags_never_zero_and_change_every_two_calls():
     assert rtp.tag_of(2**32 - 2) == 2**32 - 1 and rtp.tag_of(2**32 - 1) == 1
 
 
+@pytest.fixture
+def register_family():
+    rtp.set_kernel_family("register")
+    yield
+    rtp.set_kernel_family("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384, 32768, 65536])
-def test_plan_variant_capacity(dtype, hl):
+def test_register_plan_capacity(register_family, dtype, hl):
     es = torch.tensor([], dtype=dtype).element_size()
     p = rtp.plan(100, hl, dtype)
     if (hl * es) % 16 or hl * es // 16 > 4096:
         assert p["variant"] == -1
     else:
         V = hl * es // 16
-        assert p["variant"] >= 0
+        assert 0 <= p["variant"] < 100
         assert 32 * p["team_warps"] * p["vec_per_lane"] >= V            # whole row in registers
         assert p["rows_per_tile"] * 8 <= 32                               # one lane per (row, rank)
     assert p["block_threads"] % (32 * p["team_warps"]) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("tp", [1, 2, 3, 4, 8])
+def test_bulk_plan_by_default(dtype, hl, tp):
+    es = torch.tensor([], dtype=dtype).element_size()
+    p = rtp.plan(1000, hl, dtype, tp=tp)
+    row = hl * es
+    if row % 16 or row > 16384:
+        assert p["variant"] < 100
+        return
+    assert p["variant"] >= 100 and p["team_warps"] == 1
+    assert p["teams_per_cta"] == p["block_threads"] // 32 in (4, 8, 16)
+    assert 1 <= p["rows_per_tile"] <= (32 // tp if tp > 1 else 32)       # one exchange round
+    stages = p["vec_per_lane"]
+    stage = -(-p["rows_per_tile"] * row // 128) * 128
+    smem = -(-row // 128) * 128 + p["teams_per_cta"] * stages * stage
+    assert smem <= 216 * 1024                                             # fits one CTA per SM
 
 
 def test_unaligned_pointers_use_generic_kernel():
     assert rtp.plan(10, 1024, torch.bfloat16, aligned=False)["variant"] == -1
 
 
+def test_kernel_family_switch():
+    assert rtp.get_kernel_family() == "auto"
+    rtp.set_kernel_family("register")
+    try:
+        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] < 100
+    finally:
+        rtp.set_kernel_family("auto")
+    assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 100
+
+
 @pytest.mark.parametrize("rows", [0, 1, 2, 3, 7, 255, 256, 1000, 4097, 65536])
 @pytest.mark.parametrize("hl", [64, 1024, 4096, 37])
-@pytest.mark.parametrize("resident", [1, 7, 296, 1184])
-def test_every_row_is_visited_exactly_once(rows, hl, resident):
-    p = rtp.plan(rows, hl, torch.bfloat16, resident_ctas=resident)
+@pytest.mark.parametrize("resident", [1, 7, 148, 1184])
+@pytest.mark.parametrize("tp", [1, 3, 8])
+def test_every_row_is_visited_exactly_once(rows, hl, resident, tp):
+    p = rtp.plan(rows, hl, torch.bfloat16, tp=tp, resident_ctas=resident)
     assert p["grid"] <= max(1, resident)
     counts = rtp.plan_coverage(p, rows)
     assert len(counts) == rows and all(c == 1 for c in counts)
 
 
 def test_grid_never_exceeds_one_resident_wave():
-    p = rtp.plan(65536, 1024, torch.bfloat16, resident_ctas=296)
-    assert p["grid"] == 296 and p["tiles"] == 65536 // p["rows_per_tile"]
-    p = rtp.plan(3, 1024, torch.bfloat16, resident_ctas=296)
+    p = rtp.plan(65536, 1024, torch.bfloat16, tp=8, resident_ctas=148)
+    assert p["grid"] == 148 and p["tiles"] == 65536 // p["rows_per_tile"]
+    p = rtp.plan(3, 1024, torch.bfloat16, tp=8, resident_ctas=148)
     assert p["grid"] == 1
 
 
