@@ -59,6 +59,11 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-path", choices=["cpu", "fused", "nccl"], default="cpu",
+                    help="reference arm: its CPU path (default), or, as GPU comparators for "
+                         "the sweeps, its fused kernel (oracle/_ref) or its NCCL path")
+    ap.add_argument("--family", choices=["auto", "register", "bulk"], default="auto",
+                    help="kernel family of our arm (comparisons)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound on the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -166,8 +171,32 @@ def cpu_reference_time(xs, ws, eps, seconds, max_calls=10**6, min_calls=3):
     return (time.perf_counter() - t0) / n, n
 
 
+def run_reference_gpu(args):
+    """--impl reference --ref-path fused|nccl: the reference's GPU paths on this box
+    (its fused kernel built from its sources into oracle/_ref/, or its NCCL AllReduce
+    path), per-point lines for the sweeps -- comparators, not the driver's arm."""
+    world, rank, local = dist_env()
+    group = setup_group(world, local)
+    dev = torch.device("cuda", local)
+    impl_cls = RefFusedImpl if args.ref_path == "fused" else RefNcclImpl
+    if impl_cls is RefFusedImpl and world < 2:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "ref_path": "fused",
+                              "unavailable": "the reference fused kernel needs tp >= 2"}))
+        return 0
+    if args.sweep == "none":
+        args.sweep = "all"
+    run_sweeps(args, impl_cls, group, world, rank, dev)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_reference_arm(args):
     """--impl reference: rank 0 times the reference's CPU path on all ranks' data."""
+    if args.ref_path != "cpu":
+        return run_reference_gpu(args)
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
@@ -300,6 +329,7 @@ def plan_name(rtp, rows, hl, tp):
 def run_our_arm(args):
     import rmsnorm_tp_b200 as rtp
 
+    rtp.set_kernel_family(args.family)
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
@@ -423,7 +453,7 @@ def run_our_arm(args):
         print(json.dumps(line), flush=True)
 
     if args.sweep != "none":
-        run_sweeps(args, module, group, world, rank, dev)
+        run_sweeps(args, OursImpl, group, world, rank, dev)
 
     module.destroy()
     if world > 1:
@@ -434,6 +464,7 @@ def run_our_arm(args):
 
 # --------------------------------------------------------------------------- sweeps
 def emit(args, rank, rec):
+    """Print one sweep point (rank 0) and append it to --out."""
     if rank != 0:
         return
     print(json.dumps(rec), flush=True)
@@ -442,15 +473,109 @@ def emit(args, rank, rec):
             f.write(json.dumps(rec) + "\n")
 
 
-def run_sweeps(args, module, group, world, rank, dev):
-    import rmsnorm_tp_b200 as rtp
+class OursImpl:
+    """This repository's fused TP RMSNorm through its public API."""
+
+    name = "ours"
+    graphable = True
+    dtypes = (torch.float32, torch.bfloat16, torch.float16)
+
+    def __init__(self, hidden, eps, group, nmax):
+        import rmsnorm_tp_b200 as rtp
+
+        self.m = rtp.FusedTPRMSNorm(hidden, eps=eps, tp_group=group, num_max_rows=nmax)
+        self.family = rtp.get_kernel_family()
+
+    def __call__(self, x, w, out):
+        self.m.forward(x, w, out=out)
+
+    def close(self):
+        self.m.destroy()
+
+
+class RefFusedImpl:
+    """The reference's own fused kernel (csrc/rmsnorm_tp.cu, compiled unmodified into
+    oracle/_ref/ by oracle/build_ref.py), driven through its pybind11 module exactly as
+    its rmsnorm_tp/__init__.py does. fp32 only; its generation is a kernel argument,
+    so it is timed with eager launches only (a captured graph would freeze it)."""
+
+    name = "reference_fused"
+    graphable = False
+    dtypes = (torch.float32,)
+
+    def __init__(self, hidden, eps, group, nmax):
+        ref_dir = os.path.join(ROOT, "oracle", "_ref")
+        if ref_dir not in sys.path:
+            sys.path.insert(0, ref_dir)
+        import rmsnorm_tp_cpp as _C  # noqa: N814  (the reference's extension module)
+
+        self._C = _C
+        self.eps = eps
+        self.tp = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.buf = _C.CommBuffer(self.rank, self.tp, 65536)       # __init__.py:65-68
+        self.buf.allocate()
+        handles = [None] * self.tp
+        dist.all_gather_object(handles, self.buf.get_ipc_handle().to_bytes(), group=group)
+        for i in range(self.tp):                                  # __init__.py:79-83
+            if i != self.rank:
+                h = _C.IpcHandle()
+                h.from_bytes(handles[i])
+                self.buf.open_remote_handle(i, h)
+        self.buf.finalize_setup()
+        dist.barrier(group=group)
+        self.gen = 0
+
+    def __call__(self, x, w, out):                                # __init__.py:87-131
+        assert x.is_contiguous() and x.dtype == torch.float32
+        self.gen += 1
+        rows, hl = x.shape
+        self._C.launch_fused_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(),
+                                     self.buf.sums_ptrs_gpu(), self.buf.gen_ptrs_gpu(), self.rank,
+                                     self.tp, hl, hl * self.tp, rows, self.eps, self.gen,
+                                     torch.cuda.current_stream().cuda_stream)
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier()
+        self.buf.destroy()
+
+
+class RefNcclImpl:
+    """The reference's AllReduce path (bench_rmsnorm_tp.py:16-22: torch ops around an
+    NCCL all_reduce of the [rows, 1] fp32 variance), eager, as the reference times it.
+    Its output is a fresh tensor (fp32 for bf16/fp16 inputs), not `out`."""
+
+    name = "reference_nccl"
+    graphable = False
+    dtypes = (torch.float32, torch.bfloat16, torch.float16)
+
+    def __init__(self, hidden, eps, group, nmax):
+        from oracle import torch_port  # the reference arm only
+
+        self.fn = torch_port.allreduce_path_dist
+        self.fn_group = torch_port.allreduce_path_group
+        self.eps = eps
+        self.group = group
+
+    def __call__(self, x, w, out):
+        if self.group is None:                      # TP = 1: no all_reduce (bench_rmsnorm_tp.py:19)
+            self.fn_group([x], [w], self.eps)
+        else:
+            self.fn(x, w, self.eps, self.group)
+
+    def close(self):
+        pass
+
+
+def run_sweeps(args, impl_cls, group, world, rank, dev):
     from rmsnorm_tp_b200.workloads import BY_NAME, make_slice
 
     tp = world
     kinds = ["decode", "prefill", "llama"] if args.sweep == "all" else [args.sweep]
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
 
-    def measure(mod, rows, hl, dtype, seed, steps, rotate=True):
+    def measure(impl, rows, hl, dtype, seed, steps, rotate=True):
         elem = torch.tensor([], dtype=dtype).element_size()
         if rotate:
             xs, wt, outs = make_rotating_sets(rows, hl, dtype, seed, 3 * l2)
@@ -460,25 +585,31 @@ def run_sweeps(args, module, group, world, rank, dev):
         n = len(xs)
 
         def step(i):
-            mod.forward(xs[i % n], wt, out=outs[i % n])
+            impl(xs[i % n], wt, outs[i % n])
 
         for i in range(10):
             step(i)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        eager_us = max_over_ranks([time_steps(step, steps)], world)[0] * 1e3 / steps
+        t0 = time.perf_counter()
+        eager_ms = time_steps(step, steps)
+        wall_us = (time.perf_counter() - t0) * 1e6 / steps
+        eager_us = max_over_ranks([eager_ms], world)[0] * 1e3 / steps
         graph_us = None
-        try:
-            graph_ms, _ = time_graph(step, max(n, min(100, steps)), steps, world)
-            graph_us = graph_ms * 1e3
-        except Exception as exc:
-            if rank == 0:
-                print(f"# graph skipped: {exc}", file=sys.stderr)
+        if impl.graphable:
+            try:
+                graph_ms, _ = time_graph(step, max(n, min(100, steps)), steps, world)
+                graph_us = graph_ms * 1e3
+            except Exception as exc:
+                if rank == 0:
+                    print(f"# graph skipped: {exc}", file=sys.stderr)
+        if world > 1:
+            dist.barrier()
         b = algorithmic_bytes(rows, hl, elem)
-        return {"rows": rows, "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
-                "family": rtp.get_kernel_family(),
-                "eager_us_per_call": round(eager_us, 3),
+        return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
+                "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
+                "eager_us_per_call": round(eager_us, 3), "host_wall_us_per_call": round(wall_us, 3),
                 "graph_us_per_call": round(graph_us, 3) if graph_us else None,
                 "eager_GBps_per_rank": round(b / (eager_us * 1e-6) / 1e9, 1),
                 "graph_GBps_per_rank": round(b / (graph_us * 1e-6) / 1e9, 1) if graph_us else None,
@@ -487,35 +618,44 @@ def run_sweeps(args, module, group, world, rank, dev):
     if "decode" in kinds:
         cfg = BY_NAME["decode_llama70b"]
         hl = cfg.hidden // tp
-        mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=256)
-        for rows in cfg.rows:
-            rec = measure(mod, rows, hl, cfg.dtype, cfg.seed_base + rank, 10000, rotate=False)
-            rec.update(sweep="decode", hidden=cfg.hidden)
-            emit(args, rank, rec)
-        if tp > 1 and mod.comm_buf is not None:
-            ns = probe_roundtrip(mod, rank, tp)
+        impl = impl_cls(cfg.hidden, cfg.eps, group, 256)
+        for dtype in (cfg.dtype, torch.float32):
+            if dtype not in impl.dtypes:
+                continue
+            for rows in cfg.rows:
+                rec = measure(impl, rows, hl, dtype, cfg.seed_base + rank, 10000, rotate=False)
+                rec.update(sweep="decode", hidden=cfg.hidden)
+                emit(args, rank, rec)
+        if tp > 1 and isinstance(impl, OursImpl):
+            ns = probe_roundtrip(impl.m, rank, tp)
             emit(args, rank, {"sweep": "decode", "probe": "one-hop store->poll round trip",
                               "roundtrip_ns_rank0_rank1": ns, "one_hop_ns": ns / 2 if ns else None})
-        mod.destroy()
+        impl.close()
     if "prefill" in kinds and tp > 1:
         cfg = BY_NAME["prefill"]
         hl = cfg.hidden // tp
-        mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=65536)
-        for dtype in (torch.bfloat16, torch.float16):
+        impl = impl_cls(cfg.hidden, cfg.eps, group, 65536)
+        for dtype in (torch.bfloat16, torch.float16, torch.float32):
+            if dtype not in impl.dtypes:
+                continue
             for rows in cfg.rows:
-                rec = measure(mod, rows, hl, dtype, cfg.seed_base + rank, 200)
+                rec = measure(impl, rows, hl, dtype, cfg.seed_base + rank, 200)
                 rec.update(sweep="prefill", hidden=cfg.hidden)
                 emit(args, rank, rec)
-        mod.destroy()
+        impl.close()
     if "llama" in kinds:
         cfg = BY_NAME["llama3_8b"]
         hl = cfg.hidden // tp
-        for rows in (1, 16, 128, 1024, 4096, 16384, 65536):
-            mod = rtp.FusedTPRMSNorm(cfg.hidden, eps=cfg.eps, tp_group=group, num_max_rows=rows)
-            rec = measure(mod, rows, hl, cfg.dtype, cfg.seed_base + rank, 1000 if rows <= 1024 else 200)
-            rec.update(sweep="llama", hidden=cfg.hidden)
-            emit(args, rank, rec)
-            mod.destroy()
+        impl = impl_cls(cfg.hidden, cfg.eps, group, 65536)
+        for dtype in (cfg.dtype, torch.float32):
+            if dtype not in impl.dtypes:
+                continue
+            for rows in (1, 16, 128, 1024, 4096, 16384, 65536):
+                rec = measure(impl, rows, hl, dtype, cfg.seed_base + rank,
+                              1000 if rows <= 1024 else 200)
+                rec.update(sweep="llama", hidden=cfg.hidden)
+                emit(args, rank, rec)
+        impl.close()
 
 
 def probe_roundtrip(mod, rank, tp, iters=2000):

@@ -30,7 +30,7 @@ def _lonely_rank(timeout_s, nmax=64):
 
 
 @pytest.mark.parametrize("hl,dtype", [(512, torch.bfloat16), (37, torch.float32)])
-def test_missing_peer_times_out_then_reset_recovers(hl, dtype):
+def test_missing_peer_times_out_then_reset_recovers(family, hl, dtype):
     rows = 8
     buf, stand_in = _lonely_rank(0.05)
     try:
@@ -77,7 +77,7 @@ def test_missing_peer_times_out_then_reset_recovers(hl, dtype):
         buf.destroy()
 
 
-def test_ranks_that_disagree_on_the_generation_time_out_bounded():
+def test_ranks_that_disagree_on_the_generation_time_out_bounded(family):
     """Two emulated ranks whose generation counters differ (as after a rank
     skipped a call) push and await different tags; every wait ends at the
     timeout with an error status, inside the cooperative launch too."""

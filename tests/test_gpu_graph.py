@@ -14,7 +14,7 @@ from rmsnorm_tp_b200.workloads import make_group
 pytestmark = pytest.mark.gpu
 
 
-def test_graph_replays_advance_the_generation_on_the_entry_point():
+def test_graph_replays_advance_the_generation_on_the_entry_point(family):
     tp, rank, hl, rows, nmax = 4, 1, 1024, 16, 64
     buf = rtp.TPCommBuffer(rank, tp, nmax)
     buf.allocate()
@@ -64,7 +64,7 @@ def test_graph_replays_advance_the_generation_on_the_entry_point():
         buf.destroy()
 
 
-def test_graph_of_local_kernel():
+def test_graph_of_local_kernel(family):
     xs, ws = make_group(300, 4096, 1, torch.bfloat16, 9, device="cuda")
     x, w = xs[0], ws[0]
     out = torch.empty_like(x)
