@@ -489,6 +489,29 @@ class OursImpl:
     def __call__(self, x, w, out):
         self.m.forward(x, w, out=out)
 
+    def profile(self, step, calls=8):
+        """In-kernel counters over single launches: kernel span (first CTA start to
+        last CTA end), share of peer polls that had to wait, mean wait."""
+        import rmsnorm_tp_b200 as rtp
+
+        if self.m.comm_buf is None:
+            return None
+        spans, slow, fast, wait_ns = [], 0, 0, 0
+        for i in range(calls):
+            c = rtp.profile_counters()
+            self.m.comm_buf.set_profile(c)
+            torch.cuda.synchronize()
+            dist.barrier()
+            step(i)
+            torch.cuda.synchronize()
+            self.m.comm_buf.set_profile(None)
+            v = c.cpu().tolist()
+            spans.append((v[4] - v[3]) / 1e3)
+            slow, fast, wait_ns = slow + v[1], fast + v[2], wait_ns + v[0]
+        return {"kernel_span_us_median": round(statistics.median(spans), 3),
+                "slow_poll_share": round(slow / max(1, slow + fast), 4),
+                "mean_wait_us": round(wait_ns / max(1, slow) / 1e3, 3)}
+
     def close(self):
         self.m.destroy()
 
@@ -606,8 +629,10 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
                     print(f"# graph skipped: {exc}", file=sys.stderr)
         if world > 1:
             dist.barrier()
+        prof = impl.profile(step) if hasattr(impl, "profile") else None
         b = algorithmic_bytes(rows, hl, elem)
         return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
+                "profile": prof,
                 "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
                 "eager_us_per_call": round(eager_us, 3), "host_wall_us_per_call": round(wall_us, 3),
                 "graph_us_per_call": round(graph_us, 3) if graph_us else None,

@@ -146,6 +146,14 @@ int rmsnorm_local_forward(void* out, const void* x, const void* weight,
  * 10 s, or RMSNORM_TP_TIMEOUT_MS from the environment at create time). */
 int rmsnorm_tp_set_timeout(rmsnorm_tp_comm* comm, uint64_t timeout_ns);
 
+/* Optional in-kernel counters for later launches of this communicator (NULL
+ * turns them off): dev_counters points to 5 uint64 in device memory that the
+ * kernels add to -- [0] ns spent waiting for peers' partial sums (summed over
+ * waiting lanes), [1] waits that found the slot not yet written, [2] waits
+ * satisfied by the first poll, [3] earliest CTA start and [4] latest CTA end
+ * on the GPU global timer (initialise [3] to UINT64_MAX, the rest to 0). */
+int rmsnorm_tp_set_profile(rmsnorm_tp_comm* comm, uint64_t* dev_counters);
+
 /* Non-blocking: nonzero in *code once a launch has recorded a device failure
  * (reads host-mapped memory the kernel writes; no CUDA call). */
 int rmsnorm_tp_poll_error(const rmsnorm_tp_comm* comm, uint32_t* code);

@@ -18,6 +18,7 @@ from .api import (
     local_rmsnorm,
     plan,
     plan_coverage,
+    profile_counters,
     set_kernel_family,
     get_kernel_family,
     tag_of,
@@ -34,6 +35,7 @@ __all__ = [
     "RMSNormTPDeviceError",
     "plan",
     "plan_coverage",
+    "profile_counters",
     "tag_of",
     "set_kernel_family",
     "get_kernel_family",

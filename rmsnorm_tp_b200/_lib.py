@@ -81,6 +81,7 @@ SIGNATURES = {
         [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, ctypes.c_float, _c_void_p],
     ),
     "rmsnorm_tp_set_timeout": (_i32, [_c_void_p, _u64]),
+    "rmsnorm_tp_set_profile": (_i32, [_c_void_p, _c_void_p]),
     "rmsnorm_tp_poll_error": (_i32, [_c_void_p, ctypes.POINTER(_u32)]),
     "rmsnorm_tp_status": (_i32, [_c_void_p, ctypes.POINTER(StatusInfo)]),
     "rmsnorm_tp_reset": (_i32, [_c_void_p, _u64]),

@@ -188,6 +188,11 @@ class TPCommBuffer:
     def set_timeout(self, seconds: float) -> None:
         check(LIB.rmsnorm_tp_set_timeout(self._comm, int(seconds * 1e9)), "rmsnorm_tp_set_timeout")
 
+    def set_profile(self, counters: Optional[torch.Tensor]) -> None:
+        """Point later launches at 5 int64 device counters (see profile_counters), or None."""
+        ptr = None if counters is None else ctypes.c_void_p(counters.data_ptr())
+        check(LIB.rmsnorm_tp_set_profile(self._comm, ptr), "rmsnorm_tp_set_profile")
+
     def poll_error(self) -> int:
         code = ctypes.c_uint32()
         check(LIB.rmsnorm_tp_poll_error(self._comm, ctypes.byref(code)), "rmsnorm_tp_poll_error")
@@ -386,6 +391,14 @@ class EmulatedTPGroup:
     def destroy(self) -> None:
         for b in self.bufs:
             b.destroy()
+
+
+def profile_counters(device=None) -> torch.Tensor:
+    """Fresh in-kernel counters for TPCommBuffer.set_profile: int64[5] =
+    [wait ns, slow waits, fast waits, earliest CTA start, latest CTA end]."""
+    t = torch.zeros(5, dtype=torch.int64, device=device or "cuda")
+    t[3] = -1   # UINT64_MAX for the atomicMin of the start time
+    return t
 
 
 def plan(rows: int, local_hidden: int, dtype: torch.dtype, aligned: bool = True, tp: int = 1,

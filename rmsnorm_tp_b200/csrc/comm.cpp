@@ -114,6 +114,7 @@ struct rmsnorm_tp_comm {
   bool finalized = false;
   unsigned long long probe_seq = 0;
   unsigned char uuid[16] = {};
+  unsigned long long* prof = nullptr;      // optional device counters (5 x u64)
 };
 
 static void release(rmsnorm_tp_comm* c) {
@@ -350,6 +351,7 @@ int rmsnorm_tp_forward(rmsnorm_tp_comm* c, void* out, const void* x, const void*
   a.tp = c->tp;
   a.emulated = 0;
   a.timeout_ns = c->timeout_ns;
+  a.prof = c->prof;
   int cur = -1;
   cudaGetDevice(&cur);
   cudaError_t e;
@@ -427,11 +429,20 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* con
   a.tp = tp;
   a.emulated = 1;
   a.timeout_ns = comms[0]->timeout_ns;
+  a.prof = comms[0]->prof;
   DeviceGuard guard(comms[0]->device);
   if (guard.err != cudaSuccess) return cuda_fail(guard.err, "forward_emulated: cudaSetDevice");
   cudaError_t e = rtp::launch_forward(a, dtype, comms[0]->device, tp,
                                       reinterpret_cast<cudaStream_t>(stream), nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "forward_emulated: cooperative launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_set_profile(rmsnorm_tp_comm* c, uint64_t* dev_counters) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "set_profile: NULL communicator");
+  if (reinterpret_cast<uintptr_t>(dev_counters) & 7u)
+    return fail(RMSNORM_TP_ERR_INVALID, "set_profile: counters not 8-byte aligned");
+  c->prof = reinterpret_cast<unsigned long long*>(dev_counters);
   return RMSNORM_TP_OK;
 }
 

@@ -35,6 +35,7 @@ struct KArgs {
   unsigned int stage_bytes;            // bulk kernels: bytes per stage (multiple of 128)
   int pad_;
   unsigned long long timeout_ns;
+  unsigned long long* prof;            // optional wait/timing counters (5 x u64), or null
 };
 
 enum Dtype { kF32 = 0, kBF16 = 1, kF16 = 2 };

@@ -141,93 +141,103 @@ __device__ __forceinline__ uint4 normalize16(const uint4& xv, const uint4& wv, f
 __device__ __forceinline__ float quiet_nan() { return __uint_as_float(0x7FC00000u); }
 
 // ---------------------------------------------------------------------------
-// Cross-GPU exchange, one lane's share: push this rank's partial of `row` into
-// rank q's mailbox slot [buf][rank][row], then wait (bounded by the global
-// timer) until slot [buf][q][row] of the local mailbox carries `tag`, and
-// return rank q's partial. Lanes with q == rank or !active return `mine`.
-// A timeout is recorded in the rank's DeviceState (first failure wins) and
-// mirrored to the host-mapped flag; it also raises `abort`, which makes every
-// other wait of this launch give up at once.
+// Cross-GPU exchange, one lane's share, in two steps.
+//
+// push_slot: store this rank's partial of `row` into rank q's mailbox slot
+// [buf][rank][row] (one relaxed system-scope 64-bit store over NVLink).
+// poll_slot: wait, bounded by the global timer, until slot [buf][q][row] of the
+// local mailbox carries `tag`, and return rank q's partial. Lanes with
+// q == rank or !active return `mine`. A timeout is recorded in the rank's
+// DeviceState (first failure wins) and mirrored to the host-mapped flag; it
+// also raises `abort`, which makes every other wait of this launch give up.
 // ---------------------------------------------------------------------------
+struct WaitStats {          // optional per-lane counters (KArgs::prof)
+  unsigned long long ns = 0;
+  unsigned int slow = 0;    // waits that found the slot not yet written
+  unsigned int fast = 0;    // waits satisfied by the first poll
+};
+
+__device__ __forceinline__ void push_slot(const KArgs& a, int rank, uint32_t buf, uint32_t tag,
+                                          int64_t row, int q, bool active, float mine) {
+  if (active && q != rank) {
+    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, a.tp, a.nmax, row);
+    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
+  }
+}
+
+__device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankPtrs& rp,
+                                           uint32_t buf, uint32_t tag, unsigned long long call,
+                                           int64_t row, int q, bool active, float mine,
+                                           bool& failed, WaitStats& ws) {
+  failed = false;
+  if (!active || q == rank) return mine;
+  const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, a.tp, a.nmax, row);
+  unsigned long long w = ptx::ld_relaxed_sys_u64(src);
+  if (slot_tag(w) == tag) {
+    ws.fast += 1;
+    return slot_value(w);
+  }
+  uint32_t fail = kStatusOk;
+  const unsigned long long t0 = ptx::globaltimer();
+  unsigned long long now = t0;
+  for (;;) {
+    w = ptx::ld_relaxed_sys_u64(src);
+    if (slot_tag(w) == tag) break;
+    if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
+      fail = kStatusAborted;
+      break;
+    }
+    now = ptx::globaltimer();
+    if (now - t0 > a.timeout_ns) {
+      fail = kStatusTimeout;
+      break;
+    }
+  }
+  ws.slow += 1;
+  ws.ns += ptx::globaltimer() - t0;
+  if (fail == kStatusTimeout) {
+    DeviceState* st = rp.state;
+    if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {
+      st->err_src = (unsigned)q;
+      st->err_row = (long long)row;
+      st->err_expected = tag;
+      st->err_seen = slot_tag(w);
+      st->err_call = call;
+      if (rp.host_flag != nullptr) {
+        *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusTimeout;
+        __threadfence_system();
+      }
+    }
+    atomicExch(&st->abort, 1u);
+  }
+  failed = (fail != kStatusOk);
+  return slot_value(w);
+}
+
 __device__ __forceinline__ float push_poll(const KArgs& a, int rank, const RankPtrs& rp,
                                            uint32_t buf, uint32_t tag, unsigned long long call,
                                            int64_t row, int q, bool active, float mine,
-                                           bool& failed) {
-  const int tp = a.tp;
-  const bool remote = active && (q != rank);
-  if (remote) {
-    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, tp, a.nmax, row);
-    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
-  }
-  float val = mine;
-  uint32_t fail = kStatusOk;
-  if (remote) {
-    const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, tp, a.nmax, row);
-    unsigned long long w = ptx::ld_relaxed_sys_u64(src);
-    if (slot_tag(w) != tag) {
-      const unsigned long long t0 = ptx::globaltimer();
-      for (;;) {
-        w = ptx::ld_relaxed_sys_u64(src);
-        if (slot_tag(w) == tag) break;
-        if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
-          fail = kStatusAborted;
-          break;
-        }
-        if (ptx::globaltimer() - t0 > a.timeout_ns) {
-          fail = kStatusTimeout;
-          break;
-        }
-      }
-    }
-    if (fail == kStatusTimeout) {
-      DeviceState* st = rp.state;
-      if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {
-        st->err_src = (unsigned)q;
-        st->err_row = (long long)row;
-        st->err_expected = tag;
-        st->err_seen = slot_tag(w);
-        st->err_call = call;
-        if (rp.host_flag != nullptr) {
-          *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusTimeout;
-          __threadfence_system();
-        }
-      }
-      atomicExch(&st->abort, 1u);
-    }
-    val = slot_value(w);
-  }
-  failed = (fail != kStatusOk);
-  return val;
+                                           bool& failed, WaitStats& ws) {
+  push_slot(a, rank, buf, tag, row, q, active, mine);
+  return poll_slot(a, rank, rp, buf, tag, call, row, q, active, mine, failed, ws);
 }
 
-// Exchange of the partial sums of up to kRows rows by one warp (register
-// kernels). Lane L serves row r = L / tp and rank q = L % tp; every lane
-// returns S[i] = sum over ranks, in rank order, of row i's partials. Returns
-// false (warp-uniform) if any wait gave up.
-template <int kRows>
-__device__ __forceinline__ bool exchange_partials(const KArgs& a, int rank, const RankPtrs& rp,
-                                                  uint32_t buf, uint32_t tag,
-                                                  unsigned long long call, int64_t row0,
-                                                  int nrows, const float (&ss)[kRows],
-                                                  float (&S)[kRows]) {
-  const int lane = threadIdx.x & 31;
-  const int tp = a.tp;
-  const int r = lane / tp;
-  const int q = lane - r * tp;
-  float mine = 0.f;
-#pragma unroll
-  for (int i = 0; i < kRows; ++i)
-    if (i == r) mine = ss[i];
-  bool failed = false;
-  const float val = push_poll(a, rank, rp, buf, tag, call, row0 + r, q, r < nrows, mine, failed);
-  const bool any_fail = __any_sync(0xFFFFFFFFu, failed);
-#pragma unroll
-  for (int i = 0; i < kRows; ++i) {
-    float s = 0.f;
-    for (int p = 0; p < tp; ++p) s += __shfl_sync(0xFFFFFFFFu, val, i * tp + p);
-    S[i] = s;
+// Adds the lanes' wait counters and the CTA's start/end times to KArgs::prof:
+// [0] wait ns summed over lanes, [1] slow waits, [2] fast waits,
+// [3] earliest CTA start, [4] latest CTA end (global timer, ns).
+__device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
+                                            unsigned long long t_start) {
+  if (a.prof == nullptr) return;
+  if (ws.slow) {
+    atomicAdd(a.prof + 0, ws.ns);
+    atomicAdd(a.prof + 1, (unsigned long long)ws.slow);
   }
-  return !any_fail;
+  if (ws.fast) atomicAdd(a.prof + 2, (unsigned long long)ws.fast);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicMin(a.prof + 3, t_start);
+    atomicMax(a.prof + 4, ptx::globaltimer());
+  }
 }
 
 // Last CTA of the launch advances the rank's generation counter.
@@ -244,11 +254,20 @@ __device__ __forceinline__ void finish_launch(DeviceState* st, unsigned long lon
   }
 }
 
+__device__ __forceinline__ unsigned long long read_generation(const DeviceState* st) {
+  return *reinterpret_cast<const volatile unsigned long long*>(&st->call);
+}
+
 // ---------------------------------------------------------------------------
-// Vectorised kernel: each lane keeps kVec 16-byte vectors of each of the team's
-// kRows rows in registers between the load and the store (x is read once).
-// Column vector c of a row belongs to lane (c % 32) of warp ((c / 32) % kW) at
-// register j = c / (32 * kW): each warp instruction touches 512 contiguous bytes.
+// Register kernel: a team of kW warps holds kRows rows in registers between
+// the load and the store (x is read once), kVec 16-byte vectors per lane and
+// row. Column vector c of a row belongs to lane c % 32 of warp (c / 32) % kW,
+// register j = c / (32 kW): each warp instruction touches 512 contiguous bytes.
+//
+// Software pipeline of depth 2 per team: the loads of tile t+1 are issued
+// before the wait for tile t's remote partials, and tile t+1's partial is
+// pushed right after tile t is stored, so one tile's NVLink round trip
+// overlaps the next tile's HBM latency instead of adding to it.
 // ---------------------------------------------------------------------------
 template <typename T, int kVec, int kW, int kRows, int kBlock>
 __global__ void __launch_bounds__(kBlock)
@@ -256,6 +275,7 @@ __global__ void __launch_bounds__(kBlock)
   constexpr int kTeams = kBlock / 32 / kW;
   static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
   static_assert(kRows * kMaxTP <= 32, "one warp serves every (row, rank) pair of a tile");
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int team = warp / kW;
@@ -268,42 +288,42 @@ __global__ void __launch_bounds__(kBlock)
   const uint4* __restrict__ wg = reinterpret_cast<const uint4*>(rp.w);
   uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
   const bool exchange = a.tp > 1;
+  const int tp = a.tp;
+  const int lr = exchange ? lane / tp : 0;      // exchange lane -> (row, rank)
+  const int lq = exchange ? lane - lr * tp : 0;
 
-  __shared__ unsigned long long s_call;
   __shared__ float s_part[kTeams][2][kW][kRows];
   __shared__ float s_sum[kTeams][2][kRows];
   __shared__ int s_ok[kTeams][2];
 
+  const int64_t tiles = (a.rows + kRows - 1) / kRows;
+  const int64_t stride = (int64_t)gridDim.x * kTeams;
+  int64_t t = (int64_t)blockIdx.x * kTeams + team;
+
   unsigned long long call = 0ull;
   uint32_t buf = 0u, tag = 0u;
-  if (exchange) {
-    if (threadIdx.x == 0) s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
-    __syncthreads();
-    call = s_call;
-    buf = buffer_of(call);
-    tag = tag_of(call);
-  }
+  WaitStats ws;
 
-  const int64_t tiles = (a.rows + kRows - 1) / kRows;
-  const int64_t teams_total = (int64_t)gridDim.x * kTeams;
-  const int64_t team_global = (int64_t)blockIdx.x * kTeams + team;
-  int it = 0;
-  for (int64_t t = team_global; t < tiles; t += teams_total, ++it) {
-    const int64_t row0 = t * kRows;
-    const int nrows = (int)min((int64_t)kRows, a.rows - row0);
-    uint4 xv[kRows][kVec];
+  auto nrows_of = [&](int64_t tt) { return (int)min((int64_t)kRows, a.rows - tt * kRows); };
+
+  auto load = [&](int64_t tt, uint4 (&xv)[kRows][kVec]) {
+    const int64_t row0 = tt * kRows;
+    const int nr = nrows_of(tt);
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
         const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
-        if (r < nrows && c < V)
+        if (r < nr && c < V)
           xv[r][j] = ptx::ld_stream_v4(xg + (row0 + r) * V + c);
         else
           xv[r][j] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    float ss[kRows];
+  };
+
+  // Team-wide fp32 sum of squares of each row (all lanes of all team warps get it).
+  auto reduce = [&](const uint4 (&xv)[kRows][kVec], float (&ss)[kRows], int parity) {
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       float s = 0.f;
@@ -314,42 +334,73 @@ __global__ void __launch_bounds__(kBlock)
     if constexpr (kW > 1) {
       if (lane == 0) {
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) s_part[team][it & 1][wit][r] = ss[r];
+        for (int r = 0; r < kRows; ++r) s_part[team][parity][wit][r] = ss[r];
       }
       ptx::team_bar(1 + team, kW * 32);
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < kW; ++w) s += s_part[team][it & 1][w][r];
+        for (int w = 0; w < kW; ++w) s += s_part[team][parity][w][r];
         ss[r] = s;
       }
     }
-    float S[kRows];
+  };
+
+  auto mine_of = [&](const float (&ss)[kRows]) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (i == lr) m = ss[i];
+    return m;
+  };
+
+  auto push = [&](int64_t tt, const float (&ss)[kRows]) {
+    if (kW == 1 || wit == 0)
+      push_slot(a, rank, buf, tag, tt * kRows + lr, lq, lr < nrows_of(tt), mine_of(ss));
+  };
+
+  // Group sums S of tile tt's rows (rank order); returns false if a wait gave up.
+  auto gather = [&](int64_t tt, const float (&ss)[kRows], float (&S)[kRows], int parity) {
     bool ok = true;
-    if (exchange) {
-      if (kW == 1 || wit == 0)
-        ok = exchange_partials<kRows>(a, rank, rp, buf, tag, call, row0, nrows, ss, S);
-      if constexpr (kW > 1) {
-        if (wit == 0 && lane == 0) {
-#pragma unroll
-          for (int r = 0; r < kRows; ++r) s_sum[team][it & 1][r] = S[r];
-          s_ok[team][it & 1] = ok ? 1 : 0;
-        }
-        ptx::team_bar(1 + team, kW * 32);
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][it & 1][r];
-        ok = s_ok[team][it & 1] != 0;
-      }
-    } else {
+    if (!exchange) {
 #pragma unroll
       for (int r = 0; r < kRows; ++r) S[r] = ss[r];
+      return ok;
     }
+    if (kW == 1 || wit == 0) {
+      bool failed = false;
+      const float val = poll_slot(a, rank, rp, buf, tag, call, tt * kRows + lr, lq,
+                                  lr < nrows_of(tt), mine_of(ss), failed, ws);
+      ok = !__any_sync(0xFFFFFFFFu, failed);
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        float s = 0.f;
+        for (int p = 0; p < tp; ++p) s += __shfl_sync(0xFFFFFFFFu, val, i * tp + p);
+        S[i] = s;
+      }
+    }
+    if constexpr (kW > 1) {
+      if (wit == 0 && lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) s_sum[team][parity][r] = S[r];
+        s_ok[team][parity] = ok ? 1 : 0;
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][parity][r];
+      ok = s_ok[team][parity] != 0;
+    }
+    return ok;
+  };
+
+  auto store = [&](int64_t tt, const uint4 (&xv)[kRows][kVec], const float (&S)[kRows], bool ok) {
+    const int64_t row0 = tt * kRows;
+    const int nr = nrows_of(tt);
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
-      if (r < nrows) {
-        const float var = S[r] / a.hidden_f;
-        const float inv = ok ? rsqrtf(var + a.eps) : quiet_nan();
+      if (r < nr) {
+        const float inv = ok ? rsqrtf(S[r] / a.hidden_f + a.eps) : quiet_nan();
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
           const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
@@ -360,8 +411,46 @@ __global__ void __launch_bounds__(kBlock)
         }
       }
     }
+  };
+
+  // One pipeline step: prefetch tile tt + stride into `nxt`, finish tile tt from
+  // `cur`, then reduce and push the prefetched tile. Returns false at the end.
+  auto step = [&](int64_t tt, uint4 (&cur)[kRows][kVec], float (&ss_cur)[kRows],
+                  uint4 (&nxt)[kRows][kVec], float (&ss_nxt)[kRows], int it) {
+    const int64_t tn = tt + stride;
+    const bool has_next = tn < tiles;
+    if (has_next) load(tn, nxt);
+    float S[kRows];
+    const bool ok = gather(tt, ss_cur, S, it & 1);
+    store(tt, cur, S, ok);
+    if (!has_next) return false;
+    reduce(nxt, ss_nxt, (it + 1) & 1);
+    if (exchange) push(tn, ss_nxt);
+    return true;
+  };
+
+  if (t < tiles) {
+    uint4 xa[kRows][kVec], xb[kRows][kVec];
+    float ssa[kRows], ssb[kRows];
+    load(t, xa);
+    if (exchange) {   // read after the first loads are in flight: its latency overlaps theirs
+      call = read_generation(rp.state);
+      buf = buffer_of(call);
+      tag = tag_of(call);
+    }
+    reduce(xa, ssa, 0);
+    if (exchange) push(t, ssa);
+    for (int it = 0;; it += 2) {
+      if (!step(t, xa, ssa, xb, ssb, it)) break;
+      t += stride;
+      if (!step(t, xb, ssb, xa, ssa, it + 1)) break;
+      t += stride;
+    }
+  } else if (exchange) {
+    call = read_generation(rp.state);
   }
   if (exchange) finish_launch(rp.state, call);
+  flush_stats(a, ws, t_start);
 }
 
 // ---------------------------------------------------------------------------
@@ -372,6 +461,8 @@ template <typename T, int kBlock>
 __global__ void __launch_bounds__(kBlock)
     tp_rmsnorm_generic_kernel(const __grid_constant__ KArgs a) {
   constexpr int kWarps = kBlock / 32;
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  WaitStats ws;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int ri = a.emulated ? (int)blockIdx.y : 0;
@@ -415,7 +506,15 @@ __global__ void __launch_bounds__(kBlock)
       float ss[1] = {t};
       float S[1] = {t};
       bool ok = true;
-      if (exchange) ok = exchange_partials<1>(a, rank, rp, buf, tag, call, row, 1, ss, S);
+      if (exchange) {
+        bool failed = false;
+        const int q = lane;   // tp <= 8 lanes serve the row's ranks
+        const float val = push_poll(a, rank, rp, buf, tag, call, row, q, q < a.tp, ss[0], failed, ws);
+        ok = !__any_sync(0xFFFFFFFFu, failed);
+        float tot = 0.f;
+        for (int p = 0; p < a.tp; ++p) tot += __shfl_sync(0xFFFFFFFFu, val, p);
+        S[0] = tot;
+      }
       if (lane == 0) {
         s_sum = S[0];
         s_ok = ok ? 1 : 0;
@@ -433,6 +532,7 @@ __global__ void __launch_bounds__(kBlock)
     __syncthreads();  // s_part / s_sum are reused by the next row
   }
   if (exchange) finish_launch(rp.state, call);
+  flush_stats(a, ws, t_start);
 }
 
 // ---------------------------------------------------------------------------
@@ -471,6 +571,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   __shared__ float s_sum[kWarps][32];
   __shared__ unsigned long long s_call;
 
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  WaitStats ws;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int ri = a.emulated ? (int)blockIdx.y : 0;
@@ -557,7 +659,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const bool active = r < nr;
       bool failed = false;
       const float val = push_poll(a, rank, rp, buf, tag, call, row0 + r, q, active,
-                                  active ? s_part[warp][r] : 0.f, failed);
+                                  active ? s_part[warp][r] : 0.f, failed, ws);
       ok = !__any_sync(0xFFFFFFFFu, failed);
       float S = 0.f;
       for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, r * tp + p);
@@ -597,6 +699,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
                         kLoadTimeoutNs);
   }
   if (exchange) finish_launch(rp.state, call);
+  flush_stats(a, ws, t_start);
 }
 
 // ---------------------------------------------------------------------------
