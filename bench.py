@@ -69,6 +69,11 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", choices=["none", "decode", "prefill", "llama", "all"], default="none")
     ap.add_argument("--out", default=None, help="JSON-lines file for sweep points")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="override the workload's row count (profiling a single case)")
+    ap.add_argument("--hidden", type=int, default=None, help="override the workload's hidden size")
+    ap.add_argument("--dtype", choices=["bf16", "f16", "f32"], default=None,
+                    help="override the workload's dtype")
     return ap.parse_args(argv)
 
 
@@ -314,8 +319,8 @@ def time_graph(fn, n_capture, steps, world):
     return per, reps * n_capture
 
 
-def plan_name(rtp, rows, hl, tp):
-    p = rtp.plan(rows, hl, torch.bfloat16, tp=tp)
+def plan_name(rtp, rows, hl, tp, dtype=torch.bfloat16):
+    p = rtp.plan(rows, hl, dtype, tp=tp)
     v = p["variant"]
     if v >= 100:
         return (f"tp_rmsnorm_bulk_kernel<bf16,{p['teams_per_cta']} warps,{p['vec_per_lane']} stages>"
@@ -335,11 +340,17 @@ def run_our_arm(args):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     group = setup_group(world, local)
     dev = torch.device("cuda", local)
-    w = WORKLOAD
+    w = dict(WORKLOAD)
+    if args.rows or args.hidden or args.dtype:
+        w["name"] = "custom"
+        w["rows"] = args.rows or w["rows"]
+        w["hidden"] = args.hidden or w["hidden"]
+        w["dtype"] = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
+                      None: w["dtype"]}[args.dtype]
     tp = world
     hl = w["hidden"] // tp
     rows = w["rows"]
-    elem = 2
+    elem = torch.tensor([], dtype=w["dtype"]).element_size()
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     module = rtp.FusedTPRMSNorm(w["hidden"], eps=w["eps"], tp_group=group, num_max_rows=rows)
     xs, wt, outs = make_rotating_sets(rows, hl, w["dtype"], w["seed_base"] + rank, 3 * l2)
@@ -427,7 +438,8 @@ def run_our_arm(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": graph_calls, "warmup": args.warmup, "ms_per_step": round(graph_ms, 6),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[w["dtype"]],
             "data": "synthetic",
             "config": {"workload": w["name"], "hidden": w["hidden"], "rows": rows, "tp": tp,
                        "local_hidden": hl, "eps": w["eps"], "parallelism": f"tp{tp}",
@@ -437,7 +449,7 @@ def run_our_arm(args):
             "us_per_call": round(graph_ms * 1e3, 3),
             "eager_us_per_call": round(eager_ms * 1e3, 3),
             "eager_value": round(tp * bytes_rank / (eager_ms * 1e-3) / 1e9, 2),
-            "kernel": plan_name(rtp, rows, hl, tp),
+            "kernel": plan_name(rtp, rows, hl, tp, w["dtype"]),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_kind": peak_kind, "bytes_per_launch": bytes_rank,

@@ -260,17 +260,22 @@ __device__ __forceinline__ unsigned long long read_generation(const DeviceState*
 
 // ---------------------------------------------------------------------------
 // Register kernel: a team of kW warps holds kRows rows in registers between
-// the load and the store (x is read once), kVec 16-byte vectors per lane and
-// row. Column vector c of a row belongs to lane c % 32 of warp (c / 32) % kW,
-// register j = c / (32 kW): each warp instruction touches 512 contiguous bytes.
+// the load and the store (x is read from HBM once), kVec 16-byte vectors per
+// lane and row. Column vector c of a row belongs to lane c % 32 of warp
+// (c / 32) % kW, register j = c / (32 kW): each warp instruction touches 512
+// contiguous bytes.
 //
-// Software pipeline of depth 2 per team: the loads of tile t+1 are issued
-// before the wait for tile t's remote partials, and tile t+1's partial is
-// pushed right after tile t is stored, so one tile's NVLink round trip
-// overlaps the next tile's HBM latency instead of adding to it.
+// Three-buffer software pipeline per team. Buffers rotate through the roles
+//   A: tile t    -- partial pushed one step ago; poll the peers' partials, store y
+//   B: tile t+s  -- loads issued one step ago; reduce, push the partial
+//   C: tile t+2s -- loads issued now
+// and one step runs C-load, B-reduce-push, A-poll-store. Each tile's HBM
+// latency is covered by the rest of the step it was issued in, and each tile's
+// NVLink round trip (push -> peer's push visible) by a full step of other work,
+// so neither latency adds up tile after tile.
 // ---------------------------------------------------------------------------
-template <typename T, int kVec, int kW, int kRows, int kBlock>
-__global__ void __launch_bounds__(kBlock)
+template <typename T, int kVec, int kW, int kRows, int kBlock, int kMinBlocks>
+__global__ void __launch_bounds__(kBlock, kMinBlocks)
     tp_rmsnorm_vec_kernel(const __grid_constant__ KArgs a) {
   constexpr int kTeams = kBlock / 32 / kW;
   static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
@@ -292,9 +297,9 @@ __global__ void __launch_bounds__(kBlock)
   const int lr = exchange ? lane / tp : 0;      // exchange lane -> (row, rank)
   const int lq = exchange ? lane - lr * tp : 0;
 
-  __shared__ float s_part[kTeams][2][kW][kRows];
-  __shared__ float s_sum[kTeams][2][kRows];
-  __shared__ int s_ok[kTeams][2];
+  __shared__ float s_part[kTeams][3][kW][kRows];
+  __shared__ float s_sum[kTeams][3][kRows];
+  __shared__ int s_ok[kTeams][3];
 
   const int64_t tiles = (a.rows + kRows - 1) / kRows;
   const int64_t stride = (int64_t)gridDim.x * kTeams;
@@ -311,19 +316,20 @@ __global__ void __launch_bounds__(kBlock)
     const int nr = nrows_of(tt);
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
+      const uint4* xr = xg + (row0 + r) * V;
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
-        const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
+        const int c = (j * kW + wit) * 32 + lane;
         if (r < nr && c < V)
-          xv[r][j] = ptx::ld_stream_v4(xg + (row0 + r) * V + c);
+          xv[r][j] = ptx::ld_stream_v4(xr + c);
         else
           xv[r][j] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
   };
 
-  // Team-wide fp32 sum of squares of each row (all lanes of all team warps get it).
-  auto reduce = [&](const uint4 (&xv)[kRows][kVec], float (&ss)[kRows], int parity) {
+  // Team-wide fp32 sum of squares of each row (every lane of the team gets it).
+  auto reduce = [&](const uint4 (&xv)[kRows][kVec], float (&ss)[kRows], int slot) {
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       float s = 0.f;
@@ -334,14 +340,14 @@ __global__ void __launch_bounds__(kBlock)
     if constexpr (kW > 1) {
       if (lane == 0) {
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) s_part[team][parity][wit][r] = ss[r];
+        for (int r = 0; r < kRows; ++r) s_part[team][slot][wit][r] = ss[r];
       }
       ptx::team_bar(1 + team, kW * 32);
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < kW; ++w) s += s_part[team][parity][w][r];
+        for (int w = 0; w < kW; ++w) s += s_part[team][slot][w][r];
         ss[r] = s;
       }
     }
@@ -360,8 +366,8 @@ __global__ void __launch_bounds__(kBlock)
       push_slot(a, rank, buf, tag, tt * kRows + lr, lq, lr < nrows_of(tt), mine_of(ss));
   };
 
-  // Group sums S of tile tt's rows (rank order); returns false if a wait gave up.
-  auto gather = [&](int64_t tt, const float (&ss)[kRows], float (&S)[kRows], int parity) {
+  // Group sums S of tile tt's rows (rank order); false if a wait gave up.
+  auto gather = [&](int64_t tt, const float (&ss)[kRows], float (&S)[kRows], int slot) {
     bool ok = true;
     if (!exchange) {
 #pragma unroll
@@ -383,13 +389,13 @@ __global__ void __launch_bounds__(kBlock)
     if constexpr (kW > 1) {
       if (wit == 0 && lane == 0) {
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) s_sum[team][parity][r] = S[r];
-        s_ok[team][parity] = ok ? 1 : 0;
+        for (int r = 0; r < kRows; ++r) s_sum[team][slot][r] = S[r];
+        s_ok[team][slot] = ok ? 1 : 0;
       }
       ptx::team_bar(1 + team, kW * 32);
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][parity][r];
-      ok = s_ok[team][parity] != 0;
+      for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][slot][r];
+      ok = s_ok[team][slot] != 0;
     }
     return ok;
   };
@@ -401,49 +407,51 @@ __global__ void __launch_bounds__(kBlock)
     for (int r = 0; r < kRows; ++r) {
       if (r < nr) {
         const float inv = ok ? rsqrtf(S[r] / a.hidden_f + a.eps) : quiet_nan();
+        uint4* yr = yg + (row0 + r) * V;
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
-          const int64_t c = (int64_t)(j * kW + wit) * 32 + lane;
-          if (c < V) {
-            const uint4 wv = ptx::ld_cached_v4(wg + c);
-            ptx::st_v4(yg + (row0 + r) * V + c, normalize16<T>(xv[r][j], wv, inv));
-          }
+          const int c = (j * kW + wit) * 32 + lane;
+          if (c < V) ptx::st_v4(yr + c, normalize16<T>(xv[r][j], ptx::ld_cached_v4(wg + c), inv));
         }
       }
     }
   };
 
-  // One pipeline step: prefetch tile tt + stride into `nxt`, finish tile tt from
-  // `cur`, then reduce and push the prefetched tile. Returns false at the end.
-  auto step = [&](int64_t tt, uint4 (&cur)[kRows][kVec], float (&ss_cur)[kRows],
-                  uint4 (&nxt)[kRows][kVec], float (&ss_nxt)[kRows], int it) {
-    const int64_t tn = tt + stride;
-    const bool has_next = tn < tiles;
-    if (has_next) load(tn, nxt);
+  // One step with buffer roles (A, B, C) = tiles (tt, tt + stride, tt + 2 stride);
+  // returns false once tile tt was the team's last.
+  auto step = [&](int64_t tt, uint4 (&xa)[kRows][kVec], float (&ssa)[kRows], int sa,
+                  uint4 (&xb)[kRows][kVec], float (&ssb)[kRows], int sb,
+                  uint4 (&xc)[kRows][kVec]) {
+    const int64_t t1 = tt + stride, t2 = tt + 2 * stride;
+    if (t2 < tiles) load(t2, xc);
+    if (t1 < tiles) {
+      reduce(xb, ssb, sb);
+      if (exchange) push(t1, ssb);
+    }
     float S[kRows];
-    const bool ok = gather(tt, ss_cur, S, it & 1);
-    store(tt, cur, S, ok);
-    if (!has_next) return false;
-    reduce(nxt, ss_nxt, (it + 1) & 1);
-    if (exchange) push(tn, ss_nxt);
-    return true;
+    const bool ok = gather(tt, ssa, S, sa);
+    store(tt, xa, S, ok);
+    return t1 < tiles;
   };
 
   if (t < tiles) {
-    uint4 xa[kRows][kVec], xb[kRows][kVec];
-    float ssa[kRows], ssb[kRows];
-    load(t, xa);
+    uint4 x0[kRows][kVec], x1[kRows][kVec], x2[kRows][kVec];
+    float ss0[kRows], ss1[kRows], ss2[kRows];
+    load(t, x0);
+    if (t + stride < tiles) load(t + stride, x1);
     if (exchange) {   // read after the first loads are in flight: its latency overlaps theirs
       call = read_generation(rp.state);
       buf = buffer_of(call);
       tag = tag_of(call);
     }
-    reduce(xa, ssa, 0);
-    if (exchange) push(t, ssa);
-    for (int it = 0;; it += 2) {
-      if (!step(t, xa, ssa, xb, ssb, it)) break;
+    reduce(x0, ss0, 0);
+    if (exchange) push(t, ss0);
+    for (;;) {
+      if (!step(t, x0, ss0, 0, x1, ss1, 1, x2)) break;
       t += stride;
-      if (!step(t, xb, ssb, xa, ssa, it + 1)) break;
+      if (!step(t, x1, ss1, 1, x2, ss2, 2, x0)) break;
+      t += stride;
+      if (!step(t, x2, ss2, 2, x0, ss0, 0, x1)) break;
       t += stride;
     }
   } else if (exchange) {
@@ -747,12 +755,11 @@ struct VariantShape {
 constexpr VariantShape kShapes[] = {
     {1, 1, 4, 256},   // V <= 32     (bf16 hl <= 256,   fp32 hl <= 128)
     {2, 1, 2, 256},   // V <= 64     (bf16 hl <= 512,   fp32 hl <= 256)
-    {4, 1, 2, 256},   // V <= 128    (bf16 hl <= 1024,  fp32 hl <= 512)
-    {8, 1, 1, 256},   // V <= 256    (bf16 hl <= 2048,  fp32 hl <= 1024)
-    {8, 2, 1, 256},   // V <= 512    (bf16 hl <= 4096,  fp32 hl <= 2048)
-    {8, 4, 1, 256},   // V <= 1024   (bf16 hl <= 8192,  fp32 hl <= 4096)
-    {8, 8, 1, 256},   // V <= 2048   (bf16 hl <= 16384, fp32 hl <= 8192)
-    {8, 16, 1, 512},  // V <= 4096   (bf16 hl <= 32768, fp32 hl <= 16384)
+    {4, 1, 1, 256},   // V <= 128    (bf16 hl <= 1024,  fp32 hl <= 512)
+    {4, 2, 1, 256},   // V <= 256    (bf16 hl <= 2048,  fp32 hl <= 1024)
+    {4, 4, 1, 256},   // V <= 512    (bf16 hl <= 4096,  fp32 hl <= 2048)
+    {4, 8, 1, 256},   // V <= 1024   (bf16 hl <= 8192,  fp32 hl <= 4096)
+    {4, 16, 1, 512},  // V <= 2048   (bf16 hl <= 16384, fp32 hl <= 8192)
 };
 constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 constexpr int kGenericBlock = 256;
@@ -770,10 +777,10 @@ using KernelFn = void (*)(const KArgs);
 template <typename T>
 struct KernelTable {
   static constexpr KernelFn vec[kNumShapes] = {
-      tp_rmsnorm_vec_kernel<T, 1, 1, 4, 256>, tp_rmsnorm_vec_kernel<T, 2, 1, 2, 256>,
-      tp_rmsnorm_vec_kernel<T, 4, 1, 2, 256>, tp_rmsnorm_vec_kernel<T, 8, 1, 1, 256>,
-      tp_rmsnorm_vec_kernel<T, 8, 2, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 4, 1, 256>,
-      tp_rmsnorm_vec_kernel<T, 8, 8, 1, 256>, tp_rmsnorm_vec_kernel<T, 8, 16, 1, 512>,
+      tp_rmsnorm_vec_kernel<T, 1, 1, 4, 256, 3>, tp_rmsnorm_vec_kernel<T, 2, 1, 2, 256, 3>,
+      tp_rmsnorm_vec_kernel<T, 4, 1, 1, 256, 3>, tp_rmsnorm_vec_kernel<T, 4, 2, 1, 256, 3>,
+      tp_rmsnorm_vec_kernel<T, 4, 4, 1, 256, 3>, tp_rmsnorm_vec_kernel<T, 4, 8, 1, 256, 3>,
+      tp_rmsnorm_vec_kernel<T, 4, 16, 1, 512, 1>,
   };
   static constexpr KernelFn bulk[kNumBulk] = {
       tp_rmsnorm_bulk_kernel<T, 4, kBulkStages>,

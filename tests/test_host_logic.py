@@ -33,13 +33,14 @@ def register_family():
 def test_register_plan_capacity(register_family, dtype, hl):
     es = torch.tensor([], dtype=dtype).element_size()
     p = rtp.plan(100, hl, dtype)
-    if (hl * es) % 16 or hl * es // 16 > 4096:
+    if (hl * es) % 16 or hl * es // 16 > 2048:
         assert p["variant"] == -1
     else:
         V = hl * es // 16
         assert 0 <= p["variant"] < 100
         assert 32 * p["team_warps"] * p["vec_per_lane"] >= V            # whole row in registers
         assert p["rows_per_tile"] * 8 <= 32                               # one lane per (row, rank)
+        assert p["vec_per_lane"] * p["rows_per_tile"] <= 4                # 3 tiles in flight fit
     assert p["block_threads"] % (32 * p["team_warps"]) == 0
 
 
