@@ -549,14 +549,18 @@ __global__ void __launch_bounds__(kBlock)
 // Every warp owns a ring of kStages shared-memory stages. A stage holds one
 // tile of tile_rows consecutive rows -- one contiguous span of x -- fetched by a
 // single cp.async.bulk (TMA) copy that signals an mbarrier with its byte
-// count. Lane 0 keeps kStages - 1 tiles in flight ahead of the one the warp
-// works on, so the bytes in flight per SM are set by shared memory (up to
-// ~200 KB), not by registers, and the exchange wait of one tile overlaps the
-// loads of the next ones. The weight row is staged once per CTA in shared
-// memory. x is read from HBM once (then twice from shared memory: sum of
-// squares, normalisation); y is written with 128-bit stores.
-// Tiles go to warps round-robin (tile t -> warp t mod all warps), the same
-// on every rank, over a grid of at most one resident wave.
+// count, so the bytes in flight per SM are set by shared memory (~200 KB),
+// not by registers. The weight row is staged once per CTA. x is read from HBM
+// once (then from shared memory for the sum of squares and the normalisation);
+// y is written with 128-bit stores.
+//
+// Per warp, tile k goes through: wait for its copy -> reduce -> push the
+// partials -> [lag] -> poll the peers' partials -> normalise, store -> refill
+// its stage with tile k + kStages. With TP > 1 the poll of tile k is done
+// after tile k+1 has been reduced and pushed (lag of one tile), so the NVLink
+// round trip overlaps a tile of work; each copy is issued kStages-1 tiles
+// before it is needed. Tiles go to warps round-robin (tile t -> warp
+// t mod all warps), the same on every rank, over at most one resident wave.
 // ---------------------------------------------------------------------------
 constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
 
@@ -575,7 +579,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     tp_rmsnorm_bulk_kernel(const __grid_constant__ KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long s_bar[kWarps][kStages];
-  __shared__ float s_part[kWarps][32];
+  __shared__ float s_part[kWarps][2][32];
   __shared__ float s_sum[kWarps][32];
   __shared__ unsigned long long s_call;
 
@@ -592,6 +596,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int tile_rows = a.tile_rows;
   const uint32_t stage_bytes = a.stage_bytes;
   const bool exchange = a.tp > 1;
+  const int tp = a.tp;
+  const int lr = exchange ? lane / tp : 0;      // exchange lane -> (row, rank)
+  const int lq = exchange ? lane - lr * tp : 0;
 
   unsigned char* ring = smem + w_bytes + (size_t)warp * kStages * stage_bytes;
   const uint32_t ring_addr = ptx::smem_addr(ring);
@@ -602,27 +609,30 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int64_t my_tiles = wgid < tiles ? (tiles - 1 - wgid) / nw + 1 : 0;
   const unsigned char* xg = reinterpret_cast<const unsigned char*>(rp.x);
 
-  auto issue = [&](int64_t kk, int st) {   // lane 0: fetch the warp's kk-th tile into stage st
-    const int64_t row0 = (wgid + kk * nw) * tile_rows;
-    const int nr = (int)min((int64_t)tile_rows, a.rows - row0);
-    const uint32_t bytes = (uint32_t)nr * row_bytes;
+  auto row0_of = [&](int64_t kk) { return (wgid + kk * nw) * tile_rows; };
+  auto nrows_of = [&](int64_t kk) { return (int)min((int64_t)tile_rows, a.rows - row0_of(kk)); };
+
+  auto issue = [&](int64_t kk) {   // lane 0: fetch the warp's kk-th tile into stage kk % kStages
+    const int st = (int)(kk % kStages);
+    const uint32_t bytes = (uint32_t)nrows_of(kk) * row_bytes;
     const uint32_t bar = bar0 + 8u * (uint32_t)st;
     ptx::mbar_arrive_expect_tx(bar, bytes);
-    ptx::bulk_load(ring_addr + (uint32_t)st * stage_bytes, xg + row0 * (int64_t)row_bytes, bytes, bar);
+    ptx::bulk_load(ring_addr + (uint32_t)st * stage_bytes, xg + row0_of(kk) * (int64_t)row_bytes,
+                   bytes, bar);
   };
 
+  int64_t issued = my_tiles < kStages ? my_tiles : kStages;
   if (lane == 0) {
 #pragma unroll
     for (int st = 0; st < kStages; ++st) ptx::mbar_init(bar0 + 8u * st, 1u);
     ptx::fence_mbar_init();
-    for (int st = 0; st < kStages && st < my_tiles; ++st) issue(st, st);
+    for (int64_t kk = 0; kk < issued; ++kk) issue(kk);
   }
   // weight row -> shared memory while the first tiles are in flight
   const uint4* wg = reinterpret_cast<const uint4*>(rp.w);
   uint4* wsm = reinterpret_cast<uint4*>(smem);
   for (int v = threadIdx.x; v < V; v += kWarps * 32) wsm[v] = ptx::ld_cached_v4(wg + v);
-  if (exchange && threadIdx.x == 0)
-    s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
+  if (exchange && threadIdx.x == 0) s_call = read_generation(rp.state);
   __syncthreads();
 
   unsigned long long call = 0ull;
@@ -633,61 +643,90 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     tag = tag_of(call);
   }
   uint4* yg = reinterpret_cast<uint4*>(rp.out);
+  auto stage_ptr = [&](int64_t kk) {
+    return reinterpret_cast<const uint4*>(ring + (size_t)(kk % kStages) * stage_bytes);
+  };
 
-  int64_t k = 0;
-  bool load_ok = true;
-  for (; k < my_tiles; ++k) {
-    const int st = (int)(k % kStages);
-    if (!mbar_wait_bounded(bar0 + 8u * st, (uint32_t)((k / kStages) & 1), kLoadTimeoutNs)) {
-      load_ok = false;
-      break;
-    }
-    const int64_t row0 = (wgid + k * nw) * tile_rows;
-    const int nr = (int)min((int64_t)tile_rows, a.rows - row0);
-    const uint4* xs = reinterpret_cast<const uint4*>(ring + (size_t)st * stage_bytes);
-
+  // sum of squares of every row of tile kk -> s_part[warp][kk & 1][r]
+  auto reduce = [&](int64_t kk) {
+    const uint4* xs = stage_ptr(kk);
+    const int nr = nrows_of(kk);
     for (int r = 0; r < nr; ++r) {
       const uint4* xr = xs + r * V;
-      float acc0 = 0.f, acc1 = 0.f;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
       int v = lane;
-      for (; v + 32 < V; v += 64) {
-        acc0 += sumsq16<T>(xr[v]);
-        acc1 += sumsq16<T>(xr[v + 32]);
+      for (; v + 96 < V; v += 128) {
+        a0 += sumsq16<T>(xr[v]);
+        a1 += sumsq16<T>(xr[v + 32]);
+        a2 += sumsq16<T>(xr[v + 64]);
+        a3 += sumsq16<T>(xr[v + 96]);
       }
-      if (v < V) acc0 += sumsq16<T>(xr[v]);
-      const float ss = warp_allreduce_sum(acc0 + acc1);
-      if (lane == 0) s_part[warp][r] = ss;
+      for (; v < V; v += 32) a0 += sumsq16<T>(xr[v]);
+      const float ss = warp_allreduce_sum((a0 + a1) + (a2 + a3));
+      if (lane == 0) s_part[warp][kk & 1][r] = ss;
     }
     __syncwarp();
+  };
+
+  auto push = [&](int64_t kk) {
+    const bool active = lr < nrows_of(kk);
+    push_slot(a, rank, buf, tag, row0_of(kk) + lr, lq, active,
+              active ? s_part[warp][kk & 1][lr] : 0.f);
+  };
+
+  // poll tile kk's remote partials, normalise and store it, refill its stage
+  auto finish = [&](int64_t kk) {
+    const int64_t row0 = row0_of(kk);
+    const int nr = nrows_of(kk);
     bool ok = true;
     if (exchange) {
-      const int tp = a.tp;
-      const int r = lane / tp;
-      const int q = lane - r * tp;
-      const bool active = r < nr;
+      const bool active = lr < nr;
       bool failed = false;
-      const float val = push_poll(a, rank, rp, buf, tag, call, row0 + r, q, active,
-                                  active ? s_part[warp][r] : 0.f, failed, ws);
+      const float val = poll_slot(a, rank, rp, buf, tag, call, row0 + lr, lq, active,
+                                  active ? s_part[warp][kk & 1][lr] : 0.f, failed, ws);
       ok = !__any_sync(0xFFFFFFFFu, failed);
       float S = 0.f;
-      for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, r * tp + p);
-      if (active && q == 0) s_sum[warp][r] = S;
+      for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, lr * tp + p);
+      if (active && lq == 0) s_sum[warp][lr] = S;
     } else if (lane < nr) {
-      s_sum[warp][lane] = s_part[warp][lane];
+      s_sum[warp][lane] = s_part[warp][kk & 1][lane];
     }
     __syncwarp();
+    const uint4* xs = stage_ptr(kk);
     for (int r = 0; r < nr; ++r) {
       const float inv = ok ? rsqrtf(s_sum[warp][r] / a.hidden_f + a.eps) : quiet_nan();
       const uint4* xr = xs + r * V;
       uint4* yr = yg + (row0 + r) * (int64_t)V;
+#pragma unroll 4
       for (int v = lane; v < V; v += 32) ptx::st_v4(yr + v, normalize16<T>(xr[v], wsm[v], inv));
     }
     __syncwarp();
-    if (lane == 0 && k + kStages < my_tiles) {
-      ptx::fence_proxy_async_smem();   // our reads of stage st before the copy that refills it
-      issue(k + kStages, st);
+    if (lane == 0 && kk + kStages < my_tiles) {
+      ptx::fence_proxy_async_smem();   // our reads of the stage before the copy that refills it
+      issue(kk + kStages);
+    }
+    if (kk + kStages < my_tiles && kk + kStages + 1 > issued) issued = kk + kStages + 1;
+  };
+
+  int64_t k = 0;
+  int64_t pending = -1;          // reduced and pushed, not yet finished (TP > 1)
+  bool load_ok = true;
+  for (; k < my_tiles; ++k) {
+    if (!mbar_wait_bounded(bar0 + 8u * (uint32_t)(k % kStages), (uint32_t)((k / kStages) & 1),
+                           kLoadTimeoutNs)) {
+      load_ok = false;
+      break;
+    }
+    reduce(k);
+    if (exchange) {
+      push(k);
+      if (pending >= 0) finish(pending);
+      pending = k;
+    } else {
+      finish(k);
     }
   }
+  if (load_ok && pending >= 0) finish(pending);
   if (!load_ok) {
     // A copy never landed: record it, then wait (bounded) for the copies still
     // in flight so none of them lands in shared memory this CTA no longer owns.
@@ -701,8 +740,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       }
       atomicExch(&rp.state->abort, 1u);
     }
-    const int64_t end = min(my_tiles, k + kStages);
-    for (int64_t kk = k; kk < end; ++kk)
+    for (int64_t kk = k; kk < issued; ++kk)
       mbar_wait_bounded(bar0 + 8u * (uint32_t)(kk % kStages), (uint32_t)((kk / kStages) & 1),
                         kLoadTimeoutNs);
   }
