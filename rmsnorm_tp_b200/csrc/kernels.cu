@@ -558,8 +558,9 @@ __global__ void __launch_bounds__(kBlock)
 // partials -> [lag] -> poll the peers' partials -> normalise, store -> refill
 // its stage with tile k + kStages. With TP > 1 the poll of tile k is done
 // after tile k+1 has been reduced and pushed (lag of one tile), so the NVLink
-// round trip overlaps a tile of work; each copy is issued kStages-1 tiles
-// before it is needed. Tiles go to warps round-robin (tile t -> warp
+// round trip overlaps a tile of work (the same one-tile lag is kept at TP = 1,
+// where it measured faster); each copy is issued kStages-1 tiles before it is
+// needed. Tiles go to warps round-robin (tile t -> warp
 // t mod all warps), the same on every rank, over at most one resident wave.
 // ---------------------------------------------------------------------------
 constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
@@ -709,7 +710,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   };
 
   int64_t k = 0;
-  int64_t pending = -1;          // reduced and pushed, not yet finished (TP > 1)
+  int64_t pending = -1;          // reduced (and pushed), not yet finished
   bool load_ok = true;
   for (; k < my_tiles; ++k) {
     if (!mbar_wait_bounded(bar0 + 8u * (uint32_t)(k % kStages), (uint32_t)((k / kStages) & 1),
@@ -718,13 +719,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       break;
     }
     reduce(k);
-    if (exchange) {
-      push(k);
-      if (pending >= 0) finish(pending);
-      pending = k;
-    } else {
-      finish(k);
-    }
+    if (exchange) push(k);
+    // finish the previous tile only now: its NVLink round trip (TP > 1) and
+    // the next copies overlap this tile's reduction
+    if (pending >= 0) finish(pending);
+    pending = k;
   }
   if (load_ok && pending >= 0) finish(pending);
   if (!load_ok) {
@@ -808,6 +807,7 @@ constexpr int kBulkWarps[] = {4, 8, 16};
 constexpr int kNumBulk = sizeof(kBulkWarps) / sizeof(kBulkWarps[0]);
 constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
+constexpr uint64_t kBulkMinCallBytes = 24ull << 20;   // auto: bulk kernels from 24 MiB of x
 constexpr int kSlots = kNumShapes + 1 + kNumBulk;     // register, generic, bulk
 
 using KernelFn = void (*)(const KArgs);
@@ -815,9 +815,9 @@ using KernelFn = void (*)(const KArgs);
 template <typename T>
 struct KernelTable {
   static constexpr KernelFn vec[kNumShapes] = {
-      tp_rmsnorm_vec_kernel<T, 1, 1, 4, 256, 3>, tp_rmsnorm_vec_kernel<T, 2, 1, 2, 256, 3>,
-      tp_rmsnorm_vec_kernel<T, 4, 1, 1, 256, 3>, tp_rmsnorm_vec_kernel<T, 4, 2, 1, 256, 3>,
-      tp_rmsnorm_vec_kernel<T, 4, 4, 1, 256, 3>, tp_rmsnorm_vec_kernel<T, 4, 8, 1, 256, 3>,
+      tp_rmsnorm_vec_kernel<T, 1, 1, 4, 256, 2>, tp_rmsnorm_vec_kernel<T, 2, 1, 2, 256, 2>,
+      tp_rmsnorm_vec_kernel<T, 4, 1, 1, 256, 2>, tp_rmsnorm_vec_kernel<T, 4, 2, 1, 256, 2>,
+      tp_rmsnorm_vec_kernel<T, 4, 4, 1, 256, 2>, tp_rmsnorm_vec_kernel<T, 4, 8, 1, 256, 2>,
       tp_rmsnorm_vec_kernel<T, 4, 16, 1, 512, 1>,
   };
   static constexpr KernelFn bulk[kNumBulk] = {
@@ -895,11 +895,15 @@ int get_family() { return g_family.load(); }
 int elem_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
 
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family) {
-  (void)rows;
   const int eb = elem_bytes(dtype);
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
   if (family == kFamilyAuto) family = get_family();
-  if (vec_ok && family != kFamilyRegister && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
+  // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank), register
+  // kernels below that, where their lower fixed cost wins (measured crossover
+  // between 16 and 64 MiB of x per rank on B200)
+  const bool large = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb >= kBulkMinCallBytes;
+  const bool want_bulk = family == kFamilyBulk || (family == kFamilyAuto && large);
+  if (vec_ok && want_bulk && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
     const uint32_t row_bytes = (uint32_t)(hl * eb);
     const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
     const int max_rows = tp > 1 ? 32 / tp : 32;          // one lane per (row, rank) in the exchange

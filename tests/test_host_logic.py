@@ -47,9 +47,10 @@ def test_register_plan_capacity(register_family, dtype, hl):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384])
 @pytest.mark.parametrize("tp", [1, 2, 3, 4, 8])
-def test_bulk_plan_by_default(dtype, hl, tp):
+def test_bulk_plan_for_large_calls(dtype, hl, tp):
     es = torch.tensor([], dtype=dtype).element_size()
-    p = rtp.plan(1000, hl, dtype, tp=tp)
+    rows = -(-(24 << 20) // (hl * es))          # >= 24 MiB of x: the automatic choice is bulk
+    p = rtp.plan(rows, hl, dtype, tp=tp)
     row = hl * es
     if row % 16 or row > 16384:
         assert p["variant"] < 100
@@ -69,12 +70,15 @@ def test_unaligned_pointers_use_generic_kernel():
 
 def test_kernel_family_switch():
     assert rtp.get_kernel_family() == "auto"
+    assert rtp.plan(10, 1024, torch.bfloat16)["variant"] < 100           # small call: register
+    assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 100       # large call: bulk
     rtp.set_kernel_family("register")
     try:
-        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] < 100
+        assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] < 100
+        rtp.set_kernel_family("bulk")
+        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 100
     finally:
         rtp.set_kernel_family("auto")
-    assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 100
 
 
 @pytest.mark.parametrize("rows", [0, 1, 2, 3, 7, 255, 256, 1000, 4097, 65536])
