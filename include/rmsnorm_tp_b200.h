@@ -181,6 +181,24 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp,
                                 int64_t local_hidden, int dtype, float eps,
                                 void* stream);
 
+/* No counterpart in the reference. The fused TP RMSNorm of a whole TP group
+ * whose `tp` slices all sit on the current GPU (outs/xs/weights[r] = rank r's
+ * tensors, same shapes as rmsnorm_tp_forward_emulated), without allocating
+ * any device memory: for callers that may not call cudaMalloc, such as serving
+ * runtimes that fix their memory pool at start-up and plugin hosts that hand a
+ * kernel only its inputs and outputs. The mailboxes and per-rank state live in
+ * a static device array of RMSNORM_TP_STATIC_SCRATCH_BYTES that every GPU
+ * loading the library holds until exit; calls needing more than
+ * 16 * tp^2 * rows + 256 * tp bytes of it are rejected (RMSNORM_TP_ERR_ROWS).
+ * Each call clears the part it uses on `stream` before its launch; calls that
+ * overlap on the GPU share the array and race, so serialise them. The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture. */
+#define RMSNORM_TP_STATIC_SCRATCH_BYTES (4u << 20)
+int rmsnorm_tp_forward_group_static(int tp, void* const* outs, const void* const* xs,
+                                    const void* const* weights, int64_t rows,
+                                    int64_t local_hidden, int dtype, float eps, void* stream);
+
 /* One-hop NVLink latency probe between this rank and `peer`: `iters` round
  * trips of a store into the peer's mailbox and a poll of the local one. Both
  * ranks call it at the same time; the lower rank starts. Writes the average

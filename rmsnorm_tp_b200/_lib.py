@@ -93,6 +93,13 @@ SIGNATURES = {
             ctypes.POINTER(_c_void_p), _i64, _i64, _i32, ctypes.c_float, _c_void_p,
         ],
     ),
+    "rmsnorm_tp_forward_group_static": (
+        _i32,
+        [
+            _i32, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+            _i64, _i64, _i32, ctypes.c_float, _c_void_p,
+        ],
+    ),
     "rmsnorm_tp_probe_roundtrip": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p]),
     "rmsnorm_tp_plan": (_i32, [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(PlanInfo)]),
     "rmsnorm_tp_set_kernel_family": (_i32, [_i32]),

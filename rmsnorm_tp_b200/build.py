@@ -25,7 +25,8 @@ OUT_DIR = os.path.join(PKG_DIR, "_C")
 LIB_NAME = "librmsnorm_tp_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
-SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "comm.cpp")]
+SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "comm.cpp"),
+           os.path.join(CSRC, "noalloc.cu")]
 HEADERS = [
     os.path.join(CSRC, "rtp_common.h"),
     os.path.join(CSRC, "internal.h"),

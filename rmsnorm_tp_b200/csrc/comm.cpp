@@ -43,6 +43,15 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+int rtp::record_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(RMSNORM_TP_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }

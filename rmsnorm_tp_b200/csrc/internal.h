@@ -59,6 +59,10 @@ struct VariantDesc {
 constexpr int kBulkBase = 100;
 
 int elem_bytes(int dtype);
+
+// Records `msg` as the calling thread's last error (rmsnorm_tp_last_error) and
+// returns `code`.
+int record_error(int code, const char* msg);
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp = 1, int64_t rows = 0,
                            int family = kFamilyAuto);
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
