@@ -33,7 +33,7 @@ struct KArgs {
   int emulated;                        // 1: every rank in one launch, rank = blockIdx.y
   int tile_rows;                       // bulk kernels: rows per shared-memory stage
   unsigned int stage_bytes;            // bulk kernels: bytes per stage (multiple of 128)
-  int pad_;
+  int lag;                             // bulk kernels: tiles reduced before the oldest is finished
   unsigned long long timeout_ns;
   unsigned long long* prof;            // optional wait/timing counters (5 x u64), or null
 };
@@ -54,6 +54,7 @@ struct VariantDesc {
   int block_threads;
   unsigned int stage_bytes;   // bulk kernels only
   unsigned int smem_bytes;    // dynamic shared memory of the launch
+  int lag;                    // bulk kernels: exchange lag in tiles
 };
 
 constexpr int kBulkBase = 100;

@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -556,11 +557,12 @@ __global__ void __launch_bounds__(kBlock)
 //
 // Per warp, tile k goes through: wait for its copy -> reduce -> push the
 // partials -> [lag] -> poll the peers' partials -> normalise, store -> refill
-// its stage with tile k + kStages. With TP > 1 the poll of tile k is done
-// after tile k+1 has been reduced and pushed (lag of one tile), so the NVLink
-// round trip overlaps a tile of work (the same one-tile lag is kept at TP = 1,
-// where it measured faster); each copy is issued kStages-1 tiles before it is
-// needed. Tiles go to warps round-robin (tile t -> warp
+// its stage with tile k + kStages. The poll of tile k waits until `lag` more
+// tiles have been reduced and pushed, so the NVLink round trip -- and the
+// progress skew between ranks, which grows with the number of peers --
+// overlaps that much work; each copy is issued kStages - lag - 1 tiles before
+// it is needed. (A lag of one tile is kept at TP = 1 too, where it measured
+// faster than none.) Tiles go to warps round-robin (tile t -> warp
 // t mod all warps), the same on every rank, over at most one resident wave.
 // ---------------------------------------------------------------------------
 constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
@@ -580,7 +582,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     tp_rmsnorm_bulk_kernel(const __grid_constant__ KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long s_bar[kWarps][kStages];
-  __shared__ float s_part[kWarps][2][32];
+  __shared__ float s_part[kWarps][kStages][32];   // partials of the tile in each stage
   __shared__ float s_sum[kWarps][32];
   __shared__ unsigned long long s_call;
 
@@ -591,6 +593,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int ri = a.emulated ? (int)blockIdx.y : 0;
   const int rank = a.emulated ? (int)blockIdx.y : a.rank;
   const RankPtrs& rp = a.rp[ri];
+  // tiles reduced (and pushed) but not yet finished: up to `lag`; copies are
+  // issued kStages - lag - 1 tiles ahead of use
+  const int lag = a.lag < 1 ? 1 : (a.lag > kStages - 2 ? kStages - 2 : a.lag);
   const int V = (int)(a.hl / Pack<T>::kE);                  // 16-byte vectors per row
   const uint32_t row_bytes = (uint32_t)a.hl * (uint32_t)sizeof(T);
   const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       }
       for (; v < V; v += 32) a0 += sumsq16<T>(xr[v]);
       const float ss = warp_allreduce_sum((a0 + a1) + (a2 + a3));
-      if (lane == 0) s_part[warp][kk & 1][r] = ss;
+      if (lane == 0) s_part[warp][kk % kStages][r] = ss;
     }
     __syncwarp();
   };
@@ -672,7 +677,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   auto push = [&](int64_t kk) {
     const bool active = lr < nrows_of(kk);
     push_slot(a, rank, buf, tag, row0_of(kk) + lr, lq, active,
-              active ? s_part[warp][kk & 1][lr] : 0.f);
+              active ? s_part[warp][kk % kStages][lr] : 0.f);
   };
 
   // poll tile kk's remote partials, normalise and store it, refill its stage
@@ -684,13 +689,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const bool active = lr < nr;
       bool failed = false;
       const float val = poll_slot(a, rank, rp, buf, tag, call, row0 + lr, lq, active,
-                                  active ? s_part[warp][kk & 1][lr] : 0.f, failed, ws);
+                                  active ? s_part[warp][kk % kStages][lr] : 0.f, failed, ws);
       ok = !__any_sync(0xFFFFFFFFu, failed);
       float S = 0.f;
       for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, lr * tp + p);
       if (active && lq == 0) s_sum[warp][lr] = S;
     } else if (lane < nr) {
-      s_sum[warp][lane] = s_part[warp][kk & 1][lane];
+      s_sum[warp][lane] = s_part[warp][kk % kStages][lane];
     }
     __syncwarp();
     const uint4* xs = stage_ptr(kk);
@@ -710,7 +715,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   };
 
   int64_t k = 0;
-  int64_t pending = -1;          // reduced (and pushed), not yet finished
+  int64_t f = 0;                 // oldest tile not finished yet; tiles [f, k) are pending
   bool load_ok = true;
   for (; k < my_tiles; ++k) {
     if (!mbar_wait_bounded(bar0 + 8u * (uint32_t)(k % kStages), (uint32_t)((k / kStages) & 1),
@@ -720,12 +725,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
     reduce(k);
     if (exchange) push(k);
-    // finish the previous tile only now: its NVLink round trip (TP > 1) and
-    // the next copies overlap this tile's reduction
-    if (pending >= 0) finish(pending);
-    pending = k;
+    // finish tiles only `lag` tiles behind: their NVLink round trips (TP > 1)
+    // and the next copies overlap the reductions in between
+    while (k + 1 - f > lag) finish(f++);
   }
-  if (load_ok && pending >= 0) finish(pending);
+  if (load_ok)
+    while (f < my_tiles) finish(f++);
   if (!load_ok) {
     // A copy never landed: record it, then wait (bounded) for the copies still
     // in flight so none of them lands in shared memory this CTA no longer owns.
@@ -801,10 +806,13 @@ constexpr VariantShape kShapes[] = {
 constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 constexpr int kGenericBlock = 256;
 
-// Bulk kernels: warps per CTA (3 stages each).
-constexpr int kBulkStages = 3;
-constexpr int kBulkWarps[] = {4, 8, 16};
-constexpr int kNumBulk = sizeof(kBulkWarps) / sizeof(kBulkWarps[0]);
+// Bulk kernels: (warps per CTA, stages per warp).
+struct BulkShape {
+  int warps, stages;
+};
+constexpr BulkShape kBulkShapes[] = {{4, 3}, {8, 3}, {16, 3}, {8, 6}};
+constexpr int kNumBulk = sizeof(kBulkShapes) / sizeof(kBulkShapes[0]);
+constexpr int kDeepBulk = 3;                          // index of the 6-stage shape
 constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
 constexpr uint64_t kBulkMinCallBytes = 24ull << 20;   // auto: bulk kernels from 24 MiB of x
@@ -821,9 +829,10 @@ struct KernelTable {
       tp_rmsnorm_vec_kernel<T, 4, 16, 1, 512, 1>,
   };
   static constexpr KernelFn bulk[kNumBulk] = {
-      tp_rmsnorm_bulk_kernel<T, 4, kBulkStages>,
-      tp_rmsnorm_bulk_kernel<T, 8, kBulkStages>,
-      tp_rmsnorm_bulk_kernel<T, 16, kBulkStages>,
+      tp_rmsnorm_bulk_kernel<T, 4, 3>,
+      tp_rmsnorm_bulk_kernel<T, 8, 3>,
+      tp_rmsnorm_bulk_kernel<T, 16, 3>,
+      tp_rmsnorm_bulk_kernel<T, 8, 6>,
   };
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
   static KernelFn get(int variant) {
@@ -907,15 +916,29 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     const uint32_t row_bytes = (uint32_t)(hl * eb);
     const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
     const int max_rows = tp > 1 ? 32 / tp : 32;          // one lane per (row, rank) in the exchange
-    const uint32_t target = row_bytes <= 8192u ? 8192u : row_bytes;
+    // TP >= 4: 4 KB tiles in 6 stages (lag of 3 tiles: the wait is for the
+    // slowest of 3+ peers); otherwise 8 KB tiles in 3 stages (lag 1)
+    const bool deep = tp >= 4 && row_bytes <= 4096u;
+    uint32_t target = deep ? 4096u : 8192u;
+    if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {
+      const long v = std::atol(env);
+      if (v >= 1024 && v <= 16384) target = (uint32_t)v;
+    }
+    if (target < row_bytes) target = row_bytes;
     int tile_rows = (int)(target / row_bytes);
     if (tile_rows > max_rows) tile_rows = max_rows;
     if (tile_rows < 1) tile_rows = 1;
     const uint32_t stage = ((uint32_t)tile_rows * row_bytes + 127u) & ~127u;
-    for (int i = kNumBulk - 1; i >= 0; --i) {
-      const uint32_t smem = w_bytes + (uint32_t)kBulkWarps[i] * kBulkStages * stage;
+    const uint32_t deep_smem = w_bytes + 8u * 6u * stage;
+    if (deep && deep_smem <= kBulkSmemBudget) {
+      VariantDesc v{kBulkBase + kDeepBulk, 6, 1, tile_rows, 8 * 32, stage, deep_smem, 3};
+      return v;
+    }
+    for (int i = 2; i >= 0; --i) {
+      const uint32_t smem = w_bytes + (uint32_t)kBulkShapes[i].warps * kBulkShapes[i].stages * stage;
       if (smem <= kBulkSmemBudget)
-        return VariantDesc{kBulkBase + i, kBulkStages, 1, tile_rows, kBulkWarps[i] * 32, stage, smem};
+        return VariantDesc{kBulkBase + i, kBulkShapes[i].stages, 1, tile_rows,
+                           kBulkShapes[i].warps * 32, stage, smem, 1};
     }
   }
   if (vec_ok) {
@@ -923,10 +946,11 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     for (int i = 0; i < kNumShapes; ++i) {
       const int64_t cap = 32ll * kShapes[i].w * kShapes[i].vec;
       if (V <= cap)
-        return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u};
+        return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u,
+                           0};
     }
   }
-  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u};
+  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0};
 }
 
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
@@ -966,6 +990,7 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   KArgs a = a_in;
   a.tile_rows = v.rows_per_tile;
   a.stage_bytes = v.stage_bytes;
+  a.lag = v.lag;
   const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
   void* args[] = {&a};
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
