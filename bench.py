@@ -95,6 +95,23 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def ncu_traffic(rows, hl, dtype):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape,
+    from the ncu table in profiles/ncu_traffic.md, or None if not captured."""
+    name = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 6 and cells[0] == name and cells[1] == str(rows) \
+                        and cells[2] == str(hl):
+                    return int(cells[4]) + int(cells[5])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def algorithmic_bytes(rows, hl, elem):
     return 2 * rows * hl * elem + hl * elem
 
@@ -424,15 +441,7 @@ def run_our_arm(args):
 
     peak, peak_kind = measured_peak_hbm()
     achieved = bytes_rank / (graph_ms * 1e-3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            with open(tpath) as f:
-                per_row = json.load(f)["bytes_per_row"][f"bf16_hl{hl}"]
-            traffic = int(per_row * rows)
-        except Exception:
-            traffic = None
+    traffic = ncu_traffic(rows, hl, w["dtype"])
 
     if rank == 0:
         line = {
@@ -501,28 +510,25 @@ class OursImpl:
     def __call__(self, x, w, out):
         self.m.forward(x, w, out=out)
 
-    def profile(self, step, calls=8):
-        """In-kernel counters over single launches: kernel span (first CTA start to
-        last CTA end), share of peer polls that had to wait, mean wait."""
+    def profile(self, step, world, n_capture=64, steps=256):
+        """In-kernel counters in steady state: a CUDA graph of back-to-back calls
+        replayed with the counters on (the pointer is captured with each launch).
+        Reports the share of peer polls that found the partial missing and the
+        mean wait of those polls."""
         import rmsnorm_tp_b200 as rtp
 
         if self.m.comm_buf is None:
             return None
-        spans, slow, fast, wait_ns = [], 0, 0, 0
-        for i in range(calls):
-            c = rtp.profile_counters()
-            self.m.comm_buf.set_profile(c)
-            torch.cuda.synchronize()
-            dist.barrier()
-            step(i)
-            torch.cuda.synchronize()
+        c = rtp.profile_counters()
+        self.m.comm_buf.set_profile(c)
+        try:
+            time_graph(step, n_capture, steps, world)
+        finally:
             self.m.comm_buf.set_profile(None)
-            v = c.cpu().tolist()
-            spans.append((v[4] - v[3]) / 1e3)
-            slow, fast, wait_ns = slow + v[1], fast + v[2], wait_ns + v[0]
-        return {"kernel_span_us_median": round(statistics.median(spans), 3),
-                "slow_poll_share": round(slow / max(1, slow + fast), 4),
-                "mean_wait_us": round(wait_ns / max(1, slow) / 1e3, 3)}
+        v = c.cpu().tolist()
+        polls = v[1] + v[2]
+        return {"polls": polls, "slow_poll_share": round(v[1] / max(1, polls), 4),
+                "mean_wait_us": round(v[0] / max(1, v[1]) / 1e3, 3)}
 
     def close(self):
         self.m.destroy()
@@ -641,7 +647,7 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
                     print(f"# graph skipped: {exc}", file=sys.stderr)
         if world > 1:
             dist.barrier()
-        prof = impl.profile(step) if hasattr(impl, "profile") else None
+        prof = impl.profile(step, world) if hasattr(impl, "profile") else None
         b = algorithmic_bytes(rows, hl, elem)
         return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
                 "profile": prof,
