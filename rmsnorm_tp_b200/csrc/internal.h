@@ -34,6 +34,9 @@ struct KArgs {
   int tile_rows;                       // bulk kernels: rows per shared-memory stage
   unsigned int stage_bytes;            // bulk kernels: bytes per stage (multiple of 128)
   int lag;                             // bulk kernels: tiles reduced before the oldest is finished
+  int schedule;                        // bulk kernels, tiles of several rows: bit 0 = reduce
+                                       // the rows one after another (else interleaved), bit 1 =
+                                       // normalise them one after another (else interleaved)
   unsigned long long timeout_ns;
   unsigned long long* prof;            // optional wait/timing counters (5 x u64), or null
 };
@@ -55,6 +58,7 @@ struct VariantDesc {
   unsigned int stage_bytes;   // bulk kernels only
   unsigned int smem_bytes;    // dynamic shared memory of the launch
   int lag;                    // bulk kernels: exchange lag in tiles
+  int schedule;               // bulk kernels: KArgs::schedule
 };
 
 constexpr int kBulkBase = 100;

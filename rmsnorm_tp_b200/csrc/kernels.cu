@@ -577,9 +577,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
-template <typename T, int kWarps, int kStages>
+template <typename T, int kWarps, int kStages, int kRowsMax>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     tp_rmsnorm_bulk_kernel(const __grid_constant__ KArgs a) {
+  static_assert(kRowsMax >= 1 && kRowsMax <= 32, "rows per tile");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long s_bar[kWarps][kStages];
   __shared__ float s_part[kWarps][kStages][32];   // partials of the tile in each stage
@@ -654,22 +655,46 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   };
 
   // sum of squares of every row of tile kk -> s_part[warp][kk & 1][r]
+  // sum of squares of every row of tile kk -> s_part[warp][kk % kStages][r]
   auto reduce = [&](int64_t kk) {
     const uint4* xs = stage_ptr(kk);
     const int nr = nrows_of(kk);
-    for (int r = 0; r < nr; ++r) {
-      const uint4* xr = xs + r * V;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      int v = lane;
-      for (; v + 96 < V; v += 128) {
-        a0 += sumsq16<T>(xr[v]);
-        a1 += sumsq16<T>(xr[v + 32]);
-        a2 += sumsq16<T>(xr[v + 64]);
-        a3 += sumsq16<T>(xr[v + 96]);
+    if (kRowsMax == 1 || (a.schedule & 1)) {
+      for (int r = 0; r < nr; ++r) {
+        const uint4* xr = xs + r * V;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int v = lane;
+        for (; v + 96 < V; v += 128) {
+          a0 += sumsq16<T>(xr[v]);
+          a1 += sumsq16<T>(xr[v + 32]);
+          a2 += sumsq16<T>(xr[v + 64]);
+          a3 += sumsq16<T>(xr[v + 96]);
+        }
+        for (; v < V; v += 32) a0 += sumsq16<T>(xr[v]);
+        const float ss = warp_allreduce_sum((a0 + a1) + (a2 + a3));
+        if (lane == 0) s_part[warp][kk % kStages][r] = ss;
       }
-      for (; v < V; v += 32) a0 += sumsq16<T>(xr[v]);
-      const float ss = warp_allreduce_sum((a0 + a1) + (a2 + a3));
-      if (lane == 0) s_part[warp][kk % kStages][r] = ss;
+    } else {
+      // every iteration loads one vector of each row (independent loads), and
+      // the rows' butterflies run interleaved (independent shuffle chains)
+      float acc[kRowsMax];
+#pragma unroll
+      for (int r = 0; r < kRowsMax; ++r) acc[r] = 0.f;
+      for (int v = lane; v < V; v += 32) {
+#pragma unroll
+        for (int r = 0; r < kRowsMax; ++r)
+          if (r < nr) acc[r] += sumsq16<T>(xs[r * V + v]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int r = 0; r < kRowsMax; ++r) acc[r] += __shfl_xor_sync(0xFFFFFFFFu, acc[r], o);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRowsMax; ++r)
+          if (r < nr) s_part[warp][kk % kStages][r] = acc[r];
+      }
     }
     __syncwarp();
   };
@@ -699,12 +724,28 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
     __syncwarp();
     const uint4* xs = stage_ptr(kk);
-    for (int r = 0; r < nr; ++r) {
-      const float inv = ok ? rsqrtf(s_sum[warp][r] / a.hidden_f + a.eps) : quiet_nan();
-      const uint4* xr = xs + r * V;
-      uint4* yr = yg + (row0 + r) * (int64_t)V;
+    float inv[kRowsMax];
+#pragma unroll
+    for (int r = 0; r < kRowsMax; ++r)
+      inv[r] = (r < nr && ok) ? rsqrtf(s_sum[warp][r] / a.hidden_f + a.eps) : quiet_nan();
+    if (kRowsMax == 1 || (a.schedule & 2)) {
+#pragma unroll
+      for (int r = 0; r < kRowsMax; ++r) {
+        if (r < nr) {
+          const uint4* xr = xs + r * V;
+          uint4* yr = yg + (row0 + r) * (int64_t)V;
 #pragma unroll 4
-      for (int v = lane; v < V; v += 32) ptx::st_v4(yr + v, normalize16<T>(xr[v], wsm[v], inv));
+          for (int v = lane; v < V; v += 32) ptx::st_v4(yr + v, normalize16<T>(xr[v], wsm[v], inv[r]));
+        }
+      }
+    } else {
+      uint4* yt = yg + row0 * (int64_t)V;
+      for (int v = lane; v < V; v += 32) {
+        const uint4 wv = wsm[v];   // one weight load serves every row of the tile
+#pragma unroll
+        for (int r = 0; r < kRowsMax; ++r)
+          if (r < nr) ptx::st_v4(yt + r * V + v, normalize16<T>(xs[r * V + v], wv, inv[r]));
+      }
     }
     __syncwarp();
     if (lane == 0 && kk + kStages < my_tiles) {
@@ -806,13 +847,15 @@ constexpr VariantShape kShapes[] = {
 constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 constexpr int kGenericBlock = 256;
 
-// Bulk kernels: (warps per CTA, stages per warp).
+// Bulk kernels: (warps per CTA, stages per warp) x bound on rows per tile.
 struct BulkShape {
   int warps, stages;
 };
-constexpr BulkShape kBulkShapes[] = {{4, 3}, {8, 3}, {16, 3}, {8, 6}};
-constexpr int kNumBulk = sizeof(kBulkShapes) / sizeof(kBulkShapes[0]);
-constexpr int kDeepBulk = 3;                          // index of the 6-stage shape
+constexpr BulkShape kBulkShapes[] = {{4, 3}, {8, 3}, {16, 3}};
+constexpr int kNumBulkShapes = sizeof(kBulkShapes) / sizeof(kBulkShapes[0]);
+constexpr int kBulkRowBounds[] = {1, 2, 4, 8};
+constexpr int kNumRowBounds = sizeof(kBulkRowBounds) / sizeof(kBulkRowBounds[0]);
+constexpr int kNumBulk = kNumBulkShapes * kNumRowBounds;   // variant = base + shape * 4 + bound
 constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
 constexpr uint64_t kBulkMinCallBytes = 24ull << 20;   // auto: bulk kernels from 24 MiB of x
@@ -829,10 +872,12 @@ struct KernelTable {
       tp_rmsnorm_vec_kernel<T, 4, 16, 1, 512, 1>,
   };
   static constexpr KernelFn bulk[kNumBulk] = {
-      tp_rmsnorm_bulk_kernel<T, 4, 3>,
-      tp_rmsnorm_bulk_kernel<T, 8, 3>,
-      tp_rmsnorm_bulk_kernel<T, 16, 3>,
-      tp_rmsnorm_bulk_kernel<T, 8, 6>,
+      tp_rmsnorm_bulk_kernel<T, 4, 3, 1>,  tp_rmsnorm_bulk_kernel<T, 4, 3, 2>,
+      tp_rmsnorm_bulk_kernel<T, 4, 3, 4>,  tp_rmsnorm_bulk_kernel<T, 4, 3, 8>,
+      tp_rmsnorm_bulk_kernel<T, 8, 3, 1>,  tp_rmsnorm_bulk_kernel<T, 8, 3, 2>,
+      tp_rmsnorm_bulk_kernel<T, 8, 3, 4>,  tp_rmsnorm_bulk_kernel<T, 8, 3, 8>,
+      tp_rmsnorm_bulk_kernel<T, 16, 3, 1>, tp_rmsnorm_bulk_kernel<T, 16, 3, 2>,
+      tp_rmsnorm_bulk_kernel<T, 16, 3, 4>, tp_rmsnorm_bulk_kernel<T, 16, 3, 8>,
   };
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
   static KernelFn get(int variant) {
@@ -915,30 +960,44 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
   if (vec_ok && want_bulk && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
     const uint32_t row_bytes = (uint32_t)(hl * eb);
     const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
-    const int max_rows = tp > 1 ? 32 / tp : 32;          // one lane per (row, rank) in the exchange
-    // TP >= 4: 4 KB tiles in 6 stages (lag of 3 tiles: the wait is for the
-    // slowest of 3+ peers); otherwise 8 KB tiles in 3 stages (lag 1)
-    const bool deep = tp >= 4 && row_bytes <= 4096u;
-    uint32_t target = deep ? 4096u : 8192u;
-    if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {
+    // one lane per (row, rank) in the exchange; at most 8 rows per tile
+    int max_rows = tp > 1 ? 32 / tp : 32;
+    if (max_rows > kBulkRowBounds[kNumRowBounds - 1]) max_rows = kBulkRowBounds[kNumRowBounds - 1];
+    // Tile size and row schedule by row size, as measured on B200 (TP = 1,
+    // 512 MiB of x): 8 KB rows -> 16 KB tiles, rows one after another (99% of
+    // the copy peak vs 85% with one-row tiles); 4 KB rows -> 8 KB tiles,
+    // per-row reduction, interleaved normalisation (99%); 2 KB rows -> 8 KB
+    // tiles, one after another (89%); <= 1 KB rows -> 8 KB tiles, interleaved.
+    uint32_t target = 8192u;
+    int schedule = 0;
+    if (row_bytes >= 8192u) {
+      target = 16384u;
+      schedule = 3;
+    } else if (row_bytes >= 4096u) {
+      schedule = 1;
+    } else if (row_bytes >= 2048u) {
+      schedule = 3;
+    }
+    if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {   // tuning override
       const long v = std::atol(env);
       if (v >= 1024 && v <= 16384) target = (uint32_t)v;
+    }
+    if (const char* env = std::getenv("RMSNORM_TP_BULK_SCHEDULE")) {      // tuning override
+      const int v = std::atoi(env);
+      if (v >= 0 && v <= 3) schedule = v;
     }
     if (target < row_bytes) target = row_bytes;
     int tile_rows = (int)(target / row_bytes);
     if (tile_rows > max_rows) tile_rows = max_rows;
     if (tile_rows < 1) tile_rows = 1;
+    int bound = 0;
+    while (kBulkRowBounds[bound] < tile_rows) ++bound;
     const uint32_t stage = ((uint32_t)tile_rows * row_bytes + 127u) & ~127u;
-    const uint32_t deep_smem = w_bytes + 8u * 6u * stage;
-    if (deep && deep_smem <= kBulkSmemBudget) {
-      VariantDesc v{kBulkBase + kDeepBulk, 6, 1, tile_rows, 8 * 32, stage, deep_smem, 3};
-      return v;
-    }
-    for (int i = 2; i >= 0; --i) {
+    for (int i = kNumBulkShapes - 1; i >= 0; --i) {
       const uint32_t smem = w_bytes + (uint32_t)kBulkShapes[i].warps * kBulkShapes[i].stages * stage;
       if (smem <= kBulkSmemBudget)
-        return VariantDesc{kBulkBase + i, kBulkShapes[i].stages, 1, tile_rows,
-                           kBulkShapes[i].warps * 32, stage, smem, 1};
+        return VariantDesc{kBulkBase + i * kNumRowBounds + bound, kBulkShapes[i].stages, 1,
+                           tile_rows, kBulkShapes[i].warps * 32, stage, smem, 1, schedule};
     }
   }
   if (vec_ok) {
@@ -947,10 +1006,10 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
       const int64_t cap = 32ll * kShapes[i].w * kShapes[i].vec;
       if (V <= cap)
         return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u,
-                           0};
+                           0, 0};
     }
   }
-  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0};
+  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0, 0};
 }
 
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
@@ -991,6 +1050,7 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   a.tile_rows = v.rows_per_tile;
   a.stage_bytes = v.stage_bytes;
   a.lag = v.lag;
+  a.schedule = v.schedule;
   const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
   void* args[] = {&a};
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
