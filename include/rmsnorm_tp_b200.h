@@ -207,7 +207,7 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
                                void* stream, int64_t* dev_out_ns);
 
 /* Kernel family used by every later launch of this process:
- * 0 = automatic (bulk-copy kernels for calls with >= 24 MiB of x per rank,
+ * 0 = automatic (bulk-copy kernels for calls with >= 48 MiB of x per rank,
  * register kernels below), 1 = register kernels only, 2 = bulk-copy kernels
  * wherever eligible (aligned rows of <= 16 KB). For tests and benchmarks that
  * compare the two implementations. */

@@ -858,7 +858,7 @@ constexpr int kNumRowBounds = sizeof(kBulkRowBounds) / sizeof(kBulkRowBounds[0])
 constexpr int kNumBulk = kNumBulkShapes * kNumRowBounds;   // variant = base + shape * 4 + bound
 constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
-constexpr uint64_t kBulkMinCallBytes = 24ull << 20;   // auto: bulk kernels from 24 MiB of x
+constexpr uint64_t kBulkMinCallBytes = 48ull << 20;   // auto: bulk kernels from 48 MiB of x
 constexpr int kSlots = kNumShapes + 1 + kNumBulk;     // register, generic, bulk
 
 using KernelFn = void (*)(const KArgs);
@@ -953,9 +953,12 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
   if (family == kFamilyAuto) family = get_family();
   // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank), register
-  // kernels below that, where their lower fixed cost wins (measured crossover
-  // between 16 and 64 MiB of x per rank on B200)
-  const bool large = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb >= kBulkMinCallBytes;
+  // kernels below that, where their lower fixed cost wins (measured on B200:
+  // register faster at 32 MiB, bulk faster from 64 MiB). Rows of 16 KB at TP = 1
+  // (one-row tiles, 4 warps per SM) stay on the register kernel, which measured
+  // faster there at every size; with an exchange (TP > 1) the bulk kernel wins.
+  const bool large = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb >= kBulkMinCallBytes &&
+                     (tp > 1 || (uint64_t)hl * eb < kBulkMaxRowBytes);
   const bool want_bulk = family == kFamilyBulk || (family == kFamilyAuto && large);
   if (vec_ok && want_bulk && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
     const uint32_t row_bytes = (uint32_t)(hl * eb);
