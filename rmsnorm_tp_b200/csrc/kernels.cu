@@ -967,14 +967,16 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     int max_rows = tp > 1 ? 32 / tp : 32;
     if (max_rows > kBulkRowBounds[kNumRowBounds - 1]) max_rows = kBulkRowBounds[kNumRowBounds - 1];
     // Tile size and row schedule by row size, as measured on B200 (TP = 1,
-    // 512 MiB of x): 8 KB rows -> 16 KB tiles, rows one after another (99% of
-    // the copy peak vs 85% with one-row tiles); 4 KB rows -> 8 KB tiles,
+    // 512 MiB of x): 8 KB rows -> 16 KB tiles at TP = 1, rows one after another
+    // (99% of the copy peak vs 85% with one-row tiles); 4 KB rows -> 8 KB tiles,
     // per-row reduction, interleaved normalisation (99%); 2 KB rows -> 8 KB
     // tiles, one after another (89%); <= 1 KB rows -> 8 KB tiles, interleaved.
     uint32_t target = 8192u;
     int schedule = 0;
     if (row_bytes >= 8192u) {
-      target = 16384u;
+      // 2-row 16 KB tiles win at TP = 1 only; with an exchange, one-row 8 KB
+      // tiles measured faster (TP 2, 65536 rows: 98% vs 83% of the copy peak)
+      if (tp == 1) target = 16384u;
       schedule = 3;
     } else if (row_bytes >= 4096u) {
       schedule = 1;
