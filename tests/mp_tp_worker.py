@@ -13,7 +13,9 @@ Checks, on the real group (TP = world size):
 4. failure detection: rank 1 skips one call; rank 0's wait ends with a
    device-side timeout (bounded), forward is refused until the collective
    reset, and results are correct afterwards;
-5. the one-hop round-trip probe between ranks 0 and 1.
+5. a prefill-size call (65536 rows, hidden 8192: the bulk-copy kernel), sampled
+   rows gathered across ranks and checked by the oracle;
+6. the one-hop round-trip probe between ranks 0 and 1.
 """
 import datetime
 import os
@@ -152,7 +154,25 @@ def main():
     compare_rank("bf16", xs, ws, 1e-6, y, rank, "after reset")
     check(m.comm_buf.poll_error() == 0, "clean after reset")
 
-    # 5. latency probe between ranks 0 and 1
+    # 5. prefill size (bulk-copy kernel over NVLink): 65536 rows of hidden 8192;
+    # sampled rows of every rank's slice are gathered and checked by the oracle
+    from rmsnorm_tp_b200.workloads import make_slice
+
+    rows, hidden = 65536, 8192
+    x, w = make_slice(rows, hidden // tp, torch.bfloat16, 2000 + rank, device=str(dev))
+    y = m.forward(x, w)
+    torch.cuda.synchronize()
+    idx = torch.randperm(rows, generator=torch.Generator().manual_seed(7))[:64].to(dev)
+    mine = [x.index_select(0, idx).contiguous(), w.contiguous()]
+    xs_all = [torch.empty_like(mine[0]) for _ in range(tp)]
+    ws_all = [torch.empty_like(mine[1]) for _ in range(tp)]
+    dist.all_gather(xs_all, mine[0])
+    dist.all_gather(ws_all, mine[1])
+    compare_rank("bf16", [t.cpu() for t in xs_all], [t.cpu() for t in ws_all], 1e-6,
+                 y.index_select(0, idx), rank, "prefill 65536 x 8192 (sampled rows)")
+    del x, y
+
+    # 6. latency probe between ranks 0 and 1
     import ctypes
     from rmsnorm_tp_b200._lib import LIB
 
