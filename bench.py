@@ -64,6 +64,8 @@ def parse_args(argv=None):
                          "the sweeps, its fused kernel (oracle/_ref) or its NCCL path")
     ap.add_argument("--family", choices=["auto", "register", "bulk"], default="auto",
                     help="kernel family of our arm (comparisons)")
+    ap.add_argument("--no-dependent-launch", action="store_true",
+                    help="launch our kernels without programmatic dependent launch (comparisons)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound on the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -339,6 +341,9 @@ def time_graph(fn, n_capture, steps, world):
 def plan_name(rtp, rows, hl, tp, dtype=torch.bfloat16):
     p = rtp.plan(rows, hl, dtype, tp=tp)
     v = p["variant"]
+    if v >= 200:
+        return (f"rmsnorm_local_vec_kernel<bf16,{p['vec_per_lane']},{p['team_warps']},"
+                f"{p['rows_per_tile']},{p['block_threads']}> {p['depth']} tiles in flight")
     if v >= 100:
         return (f"tp_rmsnorm_bulk_kernel<bf16,{p['teams_per_cta']} warps,{p['vec_per_lane']} stages>"
                 f" {p['rows_per_tile']} rows/stage")
@@ -352,6 +357,7 @@ def run_our_arm(args):
     import rmsnorm_tp_b200 as rtp
 
     rtp.set_kernel_family(args.family)
+    rtp.set_dependent_launch(not args.no_dependent_launch)
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
@@ -453,6 +459,7 @@ def run_our_arm(args):
             "config": {"workload": w["name"], "hidden": w["hidden"], "rows": rows, "tp": tp,
                        "local_hidden": hl, "eps": w["eps"], "parallelism": f"tp{tp}",
                        "launch": "CUDA graph of forward() calls, one kernel each",
+                       "dependent_launch": rtp.get_dependent_launch(),
                        "l2": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
                              f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB L2)"},
             "us_per_call": round(graph_ms * 1e3, 3),
@@ -506,6 +513,7 @@ class OursImpl:
 
         self.m = rtp.FusedTPRMSNorm(hidden, eps=eps, tp_group=group, num_max_rows=nmax)
         self.family = rtp.get_kernel_family()
+        self.dependent_launch = rtp.get_dependent_launch()
 
     def __call__(self, x, w, out):
         self.m.forward(x, w, out=out)
@@ -650,7 +658,7 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
         prof = impl.profile(step, world) if hasattr(impl, "profile") else None
         b = algorithmic_bytes(rows, hl, elem)
         return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
-                "profile": prof,
+                "dependent_launch": getattr(impl, "dependent_launch", None), "profile": prof,
                 "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
                 "eager_us_per_call": round(eager_us, 3), "host_wall_us_per_call": round(wall_us, 3),
                 "graph_us_per_call": round(graph_us, 3) if graph_us else None,

@@ -80,7 +80,8 @@ typedef struct rmsnorm_tp_plan_info {
   int32_t teams_per_cta;
   int64_t tiles;
   int32_t grid;
-  int32_t reserved;
+  int32_t depth;          /* tiles in flight per team: register kernels 3 with an exchange
+                             (TP > 1), 3/4/6 without (TP = 1); bulk kernels: stages; generic 1 */
 } rmsnorm_tp_plan_info;
 
 /* ---- communicator lifecycle -------------------------------------------- */
@@ -207,15 +208,30 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
                                void* stream, int64_t* dev_out_ns);
 
 /* Kernel family used by every later launch of this process:
- * 0 = automatic (bulk-copy kernels for calls with >= 48 MiB of x per rank,
- * register kernels below), 1 = register kernels only, 2 = bulk-copy kernels
+ * 0 = automatic (bulk-copy kernels for calls with >= 48 MiB of x per rank
+ * with an exchange, >= 256 MiB at TP = 1; register kernels below),
+ * 1 = register kernels only, 2 = bulk-copy kernels
  * wherever eligible (aligned rows of <= 16 KB). For tests and benchmarks that
  * compare the two implementations. */
 int rmsnorm_tp_set_kernel_family(int family);
 int rmsnorm_tp_get_kernel_family(void);
 
+/* Programmatic dependent launch for every later forward launch of this process
+ * (1 = on, the default; 0 = off). When on, a forward kernel is launched with
+ * CUDA's programmatic stream serialization: it may be scheduled while the
+ * previous kernel of the stream is still finishing, and waits (griddepcontrol)
+ * for that kernel's completion and memory before it reads anything; it also
+ * lets the next kernel of the stream be scheduled early. Results are identical
+ * either way; the overlap hides launch latency between back-to-back calls,
+ * eagerly or in a CUDA graph. The emulated group launch (cooperative) never
+ * uses it. No counterpart in the reference, which launches with <<<>>>
+ * (csrc/rmsnorm_tp.cu:199-207). */
+int rmsnorm_tp_set_dependent_launch(int enable);
+int rmsnorm_tp_get_dependent_launch(void);
+
 /* The launch plan the forward call would use (pure host arithmetic; no GPU).
- * variant: -1 generic, 0..7 register kernels, >= 100 bulk-copy kernels
+ * variant: -1 generic, 0..6 register kernels (TP > 1), 100..111 bulk-copy
+ * kernels, >= 200 register kernels without an exchange (TP = 1)
  * (vec_per_lane then = stages per warp, rows_per_tile = rows per stage). */
 int rmsnorm_tp_plan(int64_t rows, int64_t local_hidden, int dtype, int aligned, int tp,
                     int resident_ctas, rmsnorm_tp_plan_info* out);

@@ -21,6 +21,8 @@ from .api import (
     profile_counters,
     set_kernel_family,
     get_kernel_family,
+    set_dependent_launch,
+    get_dependent_launch,
     tag_of,
 )
 
@@ -39,6 +41,8 @@ __all__ = [
     "tag_of",
     "set_kernel_family",
     "get_kernel_family",
+    "set_dependent_launch",
+    "get_dependent_launch",
     "buffer_of",
     "dtype_code",
 ]

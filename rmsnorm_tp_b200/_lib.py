@@ -59,7 +59,7 @@ class PlanInfo(ctypes.Structure):
         ("teams_per_cta", _i32),
         ("tiles", _i64),
         ("grid", _i32),
-        ("reserved", _i32),
+        ("depth", _i32),
     ]
 
 
@@ -104,6 +104,8 @@ SIGNATURES = {
     "rmsnorm_tp_plan": (_i32, [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(PlanInfo)]),
     "rmsnorm_tp_set_kernel_family": (_i32, [_i32]),
     "rmsnorm_tp_get_kernel_family": (_i32, []),
+    "rmsnorm_tp_set_dependent_launch": (_i32, [_i32]),
+    "rmsnorm_tp_get_dependent_launch": (_i32, []),
     "rmsnorm_tp_plan_coverage": (_i32, [ctypes.POINTER(PlanInfo), _i64, ctypes.POINTER(ctypes.c_int32)]),
     "rmsnorm_tp_tag_of": (_u32, [_u64]),
     "rmsnorm_tp_buffer_of": (_u32, [_u64]),

@@ -428,6 +428,15 @@ def get_kernel_family() -> str:
     return {0: "auto", 1: "register", 2: "bulk"}[LIB.rmsnorm_tp_get_kernel_family()]
 
 
+def set_dependent_launch(enable: bool) -> None:
+    """Process-wide programmatic dependent launch of forward kernels (default on)."""
+    check(LIB.rmsnorm_tp_set_dependent_launch(1 if enable else 0), "rmsnorm_tp_set_dependent_launch")
+
+
+def get_dependent_launch() -> bool:
+    return LIB.rmsnorm_tp_get_dependent_launch() == 1
+
+
 def tag_of(generation: int) -> int:
     return LIB.rmsnorm_tp_tag_of(generation)
 

@@ -536,6 +536,15 @@ int rmsnorm_tp_set_kernel_family(int family) {
 
 int rmsnorm_tp_get_kernel_family(void) { return rtp::get_family(); }
 
+int rmsnorm_tp_set_dependent_launch(int enable) {
+  if (enable != 0 && enable != 1)
+    return fail(RMSNORM_TP_ERR_INVALID, "set_dependent_launch: expected 0 or 1, got %d", enable);
+  rtp::set_dependent_launch(enable == 1);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_get_dependent_launch(void) { return rtp::get_dependent_launch() ? 1 : 0; }
+
 int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int tp, int resident_ctas,
                     rmsnorm_tp_plan_info* out) {
   if (!out) return fail(RMSNORM_TP_ERR_INVALID, "plan: NULL out");
@@ -553,7 +562,7 @@ int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int tp, in
   out->teams_per_cta = p.teams_per_cta;
   out->tiles = p.tiles;
   out->grid = p.grid;
-  out->reserved = 0;
+  out->depth = p.depth;
   return RMSNORM_TP_OK;
 }
 

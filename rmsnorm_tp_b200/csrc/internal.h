@@ -48,6 +48,10 @@ enum Family { kFamilyAuto = 0, kFamilyRegister = 1, kFamilyBulk = 2 };
 void set_family(int family);
 int get_family();
 
+// Programmatic dependent launch of single-GPU launches (process-wide, default on).
+void set_dependent_launch(bool enable);
+bool get_dependent_launch();
+
 // Shape of a kernel variant (template parameters of the vectorised kernel).
 struct VariantDesc {
   int id;              // -1 = generic, 0..kNumShapes-1 register kernels, >= kBulkBase bulk kernels
@@ -59,9 +63,11 @@ struct VariantDesc {
   unsigned int smem_bytes;    // dynamic shared memory of the launch
   int lag;                    // bulk kernels: exchange lag in tiles
   int schedule;               // bulk kernels: KArgs::schedule
+  int depth;                  // tiles in flight per team (Plan::depth)
 };
 
 constexpr int kBulkBase = 100;
+constexpr int kLocalBase = 200;   // TP = 1 register kernels: base + shape * depths + depth index
 
 int elem_bytes(int dtype);
 

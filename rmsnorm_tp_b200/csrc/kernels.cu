@@ -281,6 +281,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   constexpr int kTeams = kBlock / 32 / kW;
   static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
   static_assert(kRows * kMaxTP <= 32, "one warp serves every (row, rank) pair of a tile");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
   const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -290,8 +292,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   const int rank = a.emulated ? (int)blockIdx.y : a.rank;
   const RankPtrs& rp = a.rp[ri];
   const int64_t V = a.hl / Pack<T>::kE;
-  const uint4* __restrict__ xg = reinterpret_cast<const uint4*>(rp.x);
-  const uint4* __restrict__ wg = reinterpret_cast<const uint4*>(rp.w);
+  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
   uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
   const bool exchange = a.tp > 1;
   const int tp = a.tp;
@@ -463,6 +465,117 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 }
 
 // ---------------------------------------------------------------------------
+// Local register kernel (TP = 1, no exchange). Same teams, tiles and column
+// mapping as the register kernel above, but without the exchange there is no
+// tile waiting for peers, so every buffer holds loads in flight: a team keeps
+// kDepth tiles in flight, reduces and stores its oldest straight from the
+// registers and refills that buffer with the tile kDepth strides ahead.
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kRows, int kBlock, int kMinBlocks, int kDepth>
+__global__ void __launch_bounds__(kBlock, kMinBlocks)
+    rmsnorm_local_vec_kernel(const __grid_constant__ KArgs a) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  static_assert(kDepth >= 2, "at least two tiles in flight");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const RankPtrs& rp = a.rp[0];
+  const int64_t V = a.hl / Pack<T>::kE;
+  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
+
+  // two slots: a warp rewrites slot s only after the next team barrier, which
+  // every warp of the team reaches after reading slot s
+  __shared__ float s_part[kTeams][2][kW][kRows];
+
+  const int64_t tiles = (a.rows + kRows - 1) / kRows;
+  const int64_t stride = (int64_t)gridDim.x * kTeams;
+  const int64_t first = (int64_t)blockIdx.x * kTeams + team;
+
+  auto nrows_of = [&](int64_t tt) { return (int)min((int64_t)kRows, a.rows - tt * kRows); };
+
+  auto load = [&](int64_t tt, uint4 (&xv)[kRows][kVec]) {
+    const int64_t row0 = tt * kRows;
+    const int nr = nrows_of(tt);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const uint4* xr = xg + (row0 + r) * V;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        if (r < nr && c < V)
+          xv[r][j] = ptx::ld_stream_v4(xr + c);
+        else
+          xv[r][j] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
+
+  // team-wide fp32 sum of squares, then y from the registers
+  auto finish = [&](int64_t tt, const uint4 (&xv)[kRows][kVec], int slot) {
+    float ss[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) s += sumsq16<T>(xv[r][j]);
+      ss[r] = warp_allreduce_sum(s);
+    }
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) s_part[team][slot][wit][r] = ss[r];
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) s += s_part[team][slot][w][r];
+        ss[r] = s;
+      }
+    }
+    const int64_t row0 = tt * kRows;
+    const int nr = nrows_of(tt);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (r < nr) {
+        const float inv = rsqrtf(ss[r] / a.hidden_f + a.eps);
+        uint4* yr = yg + (row0 + r) * V;
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int c = (j * kW + wit) * 32 + lane;
+          if (c < V) ptx::st_v4(yr + c, normalize16<T>(xv[r][j], ptx::ld_cached_v4(wg + c), inv));
+        }
+      }
+    }
+  };
+
+  uint4 xb[kDepth][kRows][kVec];
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d)
+    if (first + d * stride < tiles) load(first + d * stride, xb[d]);
+  int slot = 0;
+  for (int64_t base = first; base < tiles; base += kDepth * stride) {
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) {
+      const int64_t tt = base + d * stride;
+      if (tt >= tiles) break;
+      finish(tt, xb[d], slot);
+      slot ^= 1;
+      if (tt + kDepth * stride < tiles) load(tt + kDepth * stride, xb[d]);
+    }
+  }
+  flush_stats(a, WaitStats{}, t_start);
+}
+
+// ---------------------------------------------------------------------------
 // Generic kernel: any width and alignment. One CTA per row at a time, scalar
 // loads, x read twice (the second read normally hits L2). Same exchange.
 // ---------------------------------------------------------------------------
@@ -470,6 +583,8 @@ template <typename T, int kBlock>
 __global__ void __launch_bounds__(kBlock)
     tp_rmsnorm_generic_kernel(const __grid_constant__ KArgs a) {
   constexpr int kWarps = kBlock / 32;
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
   const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
   WaitStats ws;
   const int lane = threadIdx.x & 31;
@@ -587,6 +702,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   __shared__ float s_sum[kWarps][32];
   __shared__ unsigned long long s_call;
 
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
   const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
   WaitStats ws;
   const int lane = threadIdx.x & 31;
@@ -636,7 +753,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     for (int64_t kk = 0; kk < issued; ++kk) issue(kk);
   }
   // weight row -> shared memory while the first tiles are in flight
-  const uint4* wg = reinterpret_cast<const uint4*>(rp.w);
+  const uint4* wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
   uint4* wsm = reinterpret_cast<uint4*>(smem);
   for (int v = threadIdx.x; v < V; v += kWarps * 32) wsm[v] = ptx::ld_cached_v4(wg + v);
   if (exchange && threadIdx.x == 0) s_call = read_generation(rp.state);
@@ -654,7 +771,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     return reinterpret_cast<const uint4*>(ring + (size_t)(kk % kStages) * stage_bytes);
   };
 
-  // sum of squares of every row of tile kk -> s_part[warp][kk & 1][r]
   // sum of squares of every row of tile kk -> s_part[warp][kk % kStages][r]
   auto reduce = [&](int64_t kk) {
     const uint4* xs = stage_ptr(kk);
@@ -859,7 +975,17 @@ constexpr int kNumBulk = kNumBulkShapes * kNumRowBounds;   // variant = base + s
 constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stage
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
 constexpr uint64_t kBulkMinCallBytes = 48ull << 20;   // auto: bulk kernels from 48 MiB of x
-constexpr int kSlots = kNumShapes + 1 + kNumBulk;     // register, generic, bulk
+// TP = 1 register kernels: tiles in flight per team. Measured on B200 (TP = 1,
+// hidden 4096, 1..65536 rows): 3 is fastest for bf16 and, but at 4096 rows, for
+// fp32 (4096 x 4096 bf16: 12.8 us at 3, 13.3 us at 4, 15.1 us at 6, which spills)
+constexpr int kLocalDepths[] = {3, 4};
+constexpr int kNumLocalDepths = sizeof(kLocalDepths) / sizeof(kLocalDepths[0]);
+constexpr int kDefaultLocalDepth = 0;                 // index into kLocalDepths
+// auto at TP = 1: bulk kernels from 256 MiB of x (the local kernel measured
+// faster at 128 MiB, 45.3 vs 46.0 us; slower at 512 MiB, 169.6 vs 164.8 us)
+constexpr uint64_t kBulkMinLocalCallBytes = 256ull << 20;
+constexpr int kNumLocal = kNumShapes * kNumLocalDepths;
+constexpr int kSlots = kNumShapes + 1 + kNumBulk + kNumLocal;   // register, generic, bulk, local
 
 using KernelFn = void (*)(const KArgs);
 
@@ -879,9 +1005,18 @@ struct KernelTable {
       tp_rmsnorm_bulk_kernel<T, 16, 3, 1>, tp_rmsnorm_bulk_kernel<T, 16, 3, 2>,
       tp_rmsnorm_bulk_kernel<T, 16, 3, 4>, tp_rmsnorm_bulk_kernel<T, 16, 3, 8>,
   };
+#define RTP_LOCAL(V, W, R, B, M) \
+  rmsnorm_local_vec_kernel<T, V, W, R, B, M, 3>, rmsnorm_local_vec_kernel<T, V, W, R, B, M, 4>
+  static constexpr KernelFn local[kNumLocal] = {
+      RTP_LOCAL(1, 1, 4, 256, 2), RTP_LOCAL(2, 1, 2, 256, 2), RTP_LOCAL(4, 1, 1, 256, 2),
+      RTP_LOCAL(4, 2, 1, 256, 2), RTP_LOCAL(4, 4, 1, 256, 2), RTP_LOCAL(4, 8, 1, 256, 2),
+      RTP_LOCAL(4, 16, 1, 512, 1),
+  };
+#undef RTP_LOCAL
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
   static KernelFn get(int variant) {
     if (variant < 0) return generic;
+    if (variant >= kLocalBase) return local[variant - kLocalBase];
     if (variant >= kBulkBase) return bulk[variant - kBulkBase];
     return vec[variant];
   }
@@ -900,11 +1035,13 @@ KernelFn kernel_for(int dtype, int variant) {
 
 int slot_of(int variant) {
   if (variant < 0) return kNumShapes;
+  if (variant >= kLocalBase) return kNumShapes + 1 + kNumBulk + (variant - kLocalBase);
   if (variant >= kBulkBase) return kNumShapes + 1 + (variant - kBulkBase);
   return variant;
 }
 
 std::atomic<int> g_family{kFamilyAuto};
+std::atomic<bool> g_dependent_launch{true};
 
 constexpr int kMaxDevices = 64;
 // Per device/dtype/variant: (dynamic smem bytes << 32) | resident CTAs of the
@@ -945,20 +1082,54 @@ int resident_ctas(int device, int dtype, const VariantDesc& v, cudaError_t* err)
 
 void set_family(int family) { g_family.store(family); }
 int get_family() { return g_family.load(); }
+void set_dependent_launch(bool enable) { g_dependent_launch.store(enable); }
+bool get_dependent_launch() { return g_dependent_launch.load(); }
 
 int elem_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
+
+namespace {
+// Tuning overrides from the environment, read once per process (-1 = unset):
+// RMSNORM_TP_BULK_STAGE_BYTES (1024..16384), RMSNORM_TP_BULK_SCHEDULE (0..3),
+// RMSNORM_TP_LOCAL_DEPTH (3 or 4).
+struct Tuning {
+  long stage_bytes = -1;
+  int schedule = -1;
+  int local_depth = -1;   // index into kLocalDepths
+  Tuning() {
+    if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {
+      const long v = std::atol(env);
+      if (v >= 1024 && v <= 16384) stage_bytes = v;
+    }
+    if (const char* env = std::getenv("RMSNORM_TP_BULK_SCHEDULE")) {
+      const int v = std::atoi(env);
+      if (v >= 0 && v <= 3) schedule = v;
+    }
+    if (const char* env = std::getenv("RMSNORM_TP_LOCAL_DEPTH")) {
+      const int v = std::atoi(env);
+      for (int d = 0; d < kNumLocalDepths; ++d)
+        if (kLocalDepths[d] == v) local_depth = d;
+    }
+  }
+};
+const Tuning& tuning() {
+  static const Tuning t;
+  return t;
+}
+}  // namespace
 
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family) {
   const int eb = elem_bytes(dtype);
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
   if (family == kFamilyAuto) family = get_family();
-  // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank), register
-  // kernels below that, where their lower fixed cost wins (measured on B200:
-  // register faster at 32 MiB, bulk faster from 64 MiB). Rows of 16 KB at TP = 1
-  // (one-row tiles, 4 warps per SM) stay on the register kernel, which measured
-  // faster there at every size; with an exchange (TP > 1) the bulk kernel wins.
-  const bool large = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb >= kBulkMinCallBytes &&
-                     (tp > 1 || (uint64_t)hl * eb < kBulkMaxRowBytes);
+  // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank with an
+  // exchange, >= kBulkMinLocalCallBytes at TP = 1), register kernels below
+  // that, where their lower fixed cost wins (measured on B200: with an
+  // exchange, register faster at 32 MiB, bulk faster from 64 MiB). Rows of 16 KB
+  // at TP = 1 (one-row tiles, 4 warps per SM) stay on the register kernel, which
+  // measured faster there at every size; with an exchange the bulk kernel wins.
+  const uint64_t x_bytes = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb;
+  const bool large = tp > 1 ? x_bytes >= kBulkMinCallBytes
+                            : x_bytes >= kBulkMinLocalCallBytes && (uint64_t)hl * eb < kBulkMaxRowBytes;
   const bool want_bulk = family == kFamilyBulk || (family == kFamilyAuto && large);
   if (vec_ok && want_bulk && (uint64_t)hl * eb <= kBulkMaxRowBytes) {
     const uint32_t row_bytes = (uint32_t)(hl * eb);
@@ -983,14 +1154,8 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     } else if (row_bytes >= 2048u) {
       schedule = 3;
     }
-    if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {   // tuning override
-      const long v = std::atol(env);
-      if (v >= 1024 && v <= 16384) target = (uint32_t)v;
-    }
-    if (const char* env = std::getenv("RMSNORM_TP_BULK_SCHEDULE")) {      // tuning override
-      const int v = std::atoi(env);
-      if (v >= 0 && v <= 3) schedule = v;
-    }
+    if (tuning().stage_bytes > 0) target = (uint32_t)tuning().stage_bytes;
+    if (tuning().schedule >= 0) schedule = tuning().schedule;
     if (target < row_bytes) target = row_bytes;
     int tile_rows = (int)(target / row_bytes);
     if (tile_rows > max_rows) tile_rows = max_rows;
@@ -1002,19 +1167,27 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
       const uint32_t smem = w_bytes + (uint32_t)kBulkShapes[i].warps * kBulkShapes[i].stages * stage;
       if (smem <= kBulkSmemBudget)
         return VariantDesc{kBulkBase + i * kNumRowBounds + bound, kBulkShapes[i].stages, 1,
-                           tile_rows, kBulkShapes[i].warps * 32, stage, smem, 1, schedule};
+                           tile_rows, kBulkShapes[i].warps * 32, stage, smem, 1, schedule,
+                           kBulkShapes[i].stages};
     }
   }
   if (vec_ok) {
     const int64_t V = hl * eb / 16;
     for (int i = 0; i < kNumShapes; ++i) {
       const int64_t cap = 32ll * kShapes[i].w * kShapes[i].vec;
-      if (V <= cap)
-        return VariantDesc{i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u,
-                           0, 0};
+      if (V > cap) continue;
+      // without an exchange (TP = 1): the local kernel, all buffers loading
+      int id = i, in_flight = 3;
+      if (tp == 1) {
+        const int depth = tuning().local_depth >= 0 ? tuning().local_depth : kDefaultLocalDepth;
+        id = kLocalBase + i * kNumLocalDepths + depth;
+        in_flight = kLocalDepths[depth];
+      }
+      return VariantDesc{id, kShapes[i].vec, kShapes[i].w, kShapes[i].rows, kShapes[i].block, 0u, 0u,
+                         0, 0, in_flight};
     }
   }
-  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0, 0};
+  return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0, 0, 1};
 }
 
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
@@ -1024,6 +1197,7 @@ Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
   p.team_warps = v.team_warps;
   p.rows_per_tile = v.rows_per_tile;
   p.block_threads = v.block_threads;
+  p.depth = v.depth;
   p.teams_per_cta = v.block_threads / 32 / v.team_warps;
   p.tiles = rows > 0 ? (rows + v.rows_per_tile - 1) / v.rows_per_tile : 0;
   const int64_t need = (p.tiles + p.teams_per_cta - 1) / p.teams_per_cta;
@@ -1061,7 +1235,21 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
   const dim3 block((unsigned)p.block_threads);
   if (grid_y > 1) return cudaLaunchCooperativeKernel(fn, grid, block, args, v.smem_bytes, stream);
-  return cudaLaunchKernel(fn, grid, block, args, v.smem_bytes, stream);
+  if (!get_dependent_launch()) return cudaLaunchKernel(fn, grid, block, args, v.smem_bytes, stream);
+  // Programmatic dependent launch: the kernel may be scheduled while the
+  // stream's previous kernel finishes; its first instruction (griddepcontrol.wait)
+  // holds it until that kernel has completed and its writes are visible.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = v.smem_bytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,

@@ -114,6 +114,26 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Programmatic dependent launch. grid_dep_wait: block until every grid this
+// launch depends on programmatically has completed and its memory operations
+// are visible (returns at once for a launch without such a dependency); no
+// global memory is touched before it. grid_dep_launch_dependents: allow the
+// next launch in the stream to start being scheduled (its CTAs fill SMs as
+// this grid's CTAs exit, and wait in their own grid_dep_wait).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Returns p unchanged, through a volatile asm: loads through the result are
+// data-dependent on this point, so the (non-volatile) load asm above cannot be
+// scheduled before a preceding grid_dep_wait.
+template <typename P>
+__device__ __forceinline__ P* launder(P* p) {
+  asm volatile("" : "+l"(p));
+  return p;
+}
+
 // Barrier over the `nthreads` threads of one team (named barrier `id`, 1..15).
 __device__ __forceinline__ void team_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -123,6 +123,7 @@ struct Plan {
   int teams_per_cta;
   int64_t tiles;        // ceil(rows / rows_per_tile)
   int grid;             // CTAs (x); <= resident capacity
+  int depth;            // tiles in flight per team (bulk: stages per warp; generic: 1)
 };
 
 // First row of the tile a team handles at step `it`; rows [first, first + rows_per_tile)

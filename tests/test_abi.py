@@ -73,3 +73,18 @@ def test_check_maps_codes_to_exceptions():
     with pytest.raises(_lib.RMSNormTPError) as e:
         _lib.check(_lib.ERR_INVALID, "x")
     assert e.value.code == _lib.ERR_INVALID and isinstance(e.value, RuntimeError)
+
+
+def test_dependent_launch_switch_round_trips_and_rejects_other_values():
+    L = _lib.LIB
+    before = L.rmsnorm_tp_get_dependent_launch()
+    assert before == 1                                  # on by default
+    try:
+        assert L.rmsnorm_tp_set_dependent_launch(0) == _lib.OK
+        assert L.rmsnorm_tp_get_dependent_launch() == 0
+        assert L.rmsnorm_tp_set_dependent_launch(2) == _lib.ERR_INVALID
+        assert L.rmsnorm_tp_get_dependent_launch() == 0  # unchanged by the rejected call
+        assert L.rmsnorm_tp_set_dependent_launch(1) == _lib.OK
+        assert L.rmsnorm_tp_get_dependent_launch() == 1
+    finally:
+        L.rmsnorm_tp_set_dependent_launch(before)

@@ -28,16 +28,20 @@ def register_family():
     rtp.set_kernel_family("auto")
 
 
+@pytest.mark.parametrize("tp", [1, 2])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384, 32768, 65536])
-def test_register_plan_capacity(register_family, dtype, hl):
+def test_register_plan_capacity(register_family, dtype, hl, tp):
     es = torch.tensor([], dtype=dtype).element_size()
-    p = rtp.plan(100, hl, dtype)
+    p = rtp.plan(100, hl, dtype, tp=tp)
     if (hl * es) % 16 or hl * es // 16 > 2048:
-        assert p["variant"] == -1
+        assert p["variant"] == -1 and p["depth"] == 1
     else:
         V = hl * es // 16
-        assert 0 <= p["variant"] < 100
+        if tp == 1:                                   # no exchange: every buffer loading
+            assert 200 <= p["variant"] < 300 and p["depth"] in (3, 4, 6)
+        else:                                         # 2 buffers loading + 1 awaiting peers
+            assert 0 <= p["variant"] < 100 and p["depth"] == 3
         assert 32 * p["team_warps"] * p["vec_per_lane"] >= V            # whole row in registers
         assert p["rows_per_tile"] * 8 <= 32                               # one lane per (row, rank)
         assert p["vec_per_lane"] * p["rows_per_tile"] <= 4                # 3 tiles in flight fit
@@ -49,13 +53,16 @@ def test_register_plan_capacity(register_family, dtype, hl):
 @pytest.mark.parametrize("tp", [1, 2, 3, 4, 8])
 def test_bulk_plan_for_large_calls(dtype, hl, tp):
     es = torch.tensor([], dtype=dtype).element_size()
-    rows = -(-(48 << 20) // (hl * es))          # >= 48 MiB of x: the automatic choice is bulk
+    # >= 48 MiB of x per rank with an exchange, >= 256 MiB at TP = 1: the automatic choice is bulk
+    rows = -(-((48 if tp > 1 else 256) << 20) // (hl * es))
     p = rtp.plan(rows, hl, dtype, tp=tp)
+    below = rtp.plan(rows - 1, hl, dtype, tp=tp)
+    assert not 100 <= below["variant"] < 200                              # one row less: register
     row = hl * es
     if row % 16 or row > 16384 or (tp == 1 and row == 16384):
-        assert p["variant"] < 100
+        assert p["variant"] < 100 or p["variant"] >= 200
         return
-    assert p["variant"] >= 100 and p["team_warps"] == 1
+    assert 100 <= p["variant"] < 200 and p["team_warps"] == 1 and p["depth"] == 3
     assert p["teams_per_cta"] == p["block_threads"] // 32 in (4, 8, 16)
     assert 1 <= p["rows_per_tile"] <= (32 // tp if tp > 1 else 32)       # one exchange round
     stages = p["vec_per_lane"]
@@ -70,13 +77,18 @@ def test_unaligned_pointers_use_generic_kernel():
 
 def test_kernel_family_switch():
     assert rtp.get_kernel_family() == "auto"
-    assert rtp.plan(10, 1024, torch.bfloat16)["variant"] < 100           # small call: register
-    assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 100       # large call: bulk
+    bulk = range(100, 200)
+    assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 200          # small call: register (TP 1)
+    assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] < 100     # with an exchange
+    assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in bulk  # 128 MiB, exchange: bulk
+    assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 200         # 128 MiB, TP 1: local
+    assert rtp.plan(262144, 1024, torch.bfloat16)["variant"] in bulk        # 512 MiB, TP 1: bulk
     rtp.set_kernel_family("register")
     try:
-        assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] < 100
+        assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 200
+        assert rtp.plan(65536, 1024, torch.bfloat16, tp=4)["variant"] < 100
         rtp.set_kernel_family("bulk")
-        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 100
+        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] in bulk
     finally:
         rtp.set_kernel_family("auto")
 
