@@ -66,6 +66,8 @@ def parse_args(argv=None):
                     help="kernel family of our arm (comparisons)")
     ap.add_argument("--no-dependent-launch", action="store_true",
                     help="launch our kernels without programmatic dependent launch (comparisons)")
+    ap.add_argument("--residual", action="store_true",
+                    help="sweeps of our arm: the fused residual add (x + residual, then the norm)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound on the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -506,6 +508,7 @@ class OursImpl:
 
     name = "ours"
     graphable = True
+    residual_ok = True
     dtypes = (torch.float32, torch.bfloat16, torch.float16)
 
     def __init__(self, hidden, eps, group, nmax):
@@ -515,8 +518,8 @@ class OursImpl:
         self.family = rtp.get_kernel_family()
         self.dependent_launch = rtp.get_dependent_launch()
 
-    def __call__(self, x, w, out):
-        self.m.forward(x, w, out=out)
+    def __call__(self, x, w, out, res=None):
+        self.m.forward(x, w, out=out, residual=res)
 
     def profile(self, step, world, n_capture=64, steps=256):
         """In-kernel counters in steady state: a CUDA graph of back-to-back calls
@@ -626,15 +629,21 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
 
     def measure(impl, rows, hl, dtype, seed, steps, rotate=True):
         elem = torch.tensor([], dtype=dtype).element_size()
+        use_res = args.residual and getattr(impl, "residual_ok", False)
         if rotate:
-            xs, wt, outs = make_rotating_sets(rows, hl, dtype, seed, 3 * l2)
+            xs, wt, outs = make_rotating_sets(rows, hl, dtype, seed, (4.5 if use_res else 3) * l2)
         else:
             x, wt = make_slice(rows, hl, dtype, seed, device="cuda")
             xs, outs = [x], [torch.empty_like(x)]
         n = len(xs)
+        # fused residual add: one residual per set, updated in place by every call
+        rs = [x.flip(0).contiguous() for x in xs] if use_res else None
 
         def step(i):
-            impl(xs[i % n], wt, outs[i % n])
+            if use_res:
+                impl(xs[i % n], wt, outs[i % n], rs[i % n])
+            else:
+                impl(xs[i % n], wt, outs[i % n])
 
         for i in range(10):
             step(i)
@@ -656,8 +665,10 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
         if world > 1:
             dist.barrier()
         prof = impl.profile(step, world) if hasattr(impl, "profile") else None
-        b = algorithmic_bytes(rows, hl, elem)
+        # read x (and the residual), write y (and the residual), read w
+        b = algorithmic_bytes(rows, hl, elem) + (2 * rows * hl * elem if use_res else 0)
         return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
+                "residual": use_res,
                 "dependent_launch": getattr(impl, "dependent_launch", None), "profile": prof,
                 "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
                 "eager_us_per_call": round(eager_us, 3), "host_wall_us_per_call": round(wall_us, 3),

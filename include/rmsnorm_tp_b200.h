@@ -141,6 +141,23 @@ int rmsnorm_local_forward(void* out, const void* x, const void* weight,
                           int64_t rows, int64_t hidden, int dtype, float eps,
                           void* stream);
 
+/* Fused residual add + TP RMSNorm, in the same launch:
+ *   z = x + residual   (fp32 add, rounded once to the dtype; written back to residual)
+ *   out = z * rsqrt(S / hidden + eps) * weight, S = sum over the TP group of sum(z^2)
+ * residual is [rows, local_hidden] in x's dtype, read and overwritten; it must
+ * not overlap out. x may be out (in place). On a failed exchange the residual
+ * still holds z and out is NaN, as for rmsnorm_tp_forward. No counterpart in
+ * the reference (its forward has no residual); the norm is the same as
+ * rmsnorm_tp_forward's applied to z, i.e. the reference's AllReduce path
+ * (bench_rmsnorm_tp.py:16-22) on (x + residual).to(dtype). */
+int rmsnorm_tp_forward_residual(rmsnorm_tp_comm* comm, void* out, void* residual,
+                                const void* x, const void* weight, int64_t rows,
+                                int64_t local_hidden, int64_t hidden, int dtype, float eps,
+                                void* stream);
+int rmsnorm_local_forward_residual(void* out, void* residual, const void* x,
+                                   const void* weight, int64_t rows, int64_t hidden,
+                                   int dtype, float eps, void* stream);
+
 /* ---- failure detection and recovery (no reference counterpart) ---------- */
 
 /* Limit on each wait for a peer's partial sum, in nanoseconds (default
@@ -181,6 +198,12 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp,
                                 const void* const* weights, int64_t rows,
                                 int64_t local_hidden, int dtype, float eps,
                                 void* stream);
+/* The same with a fused residual add (rmsnorm_tp_forward_residual) per rank. */
+int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp,
+                                         void* const* outs, void* const* residuals,
+                                         const void* const* xs, const void* const* weights,
+                                         int64_t rows, int64_t local_hidden, int dtype,
+                                         float eps, void* stream);
 
 /* No counterpart in the reference. The fused TP RMSNorm of a whole TP group
  * whose `tp` slices all sit on the current GPU (outs/xs/weights[r] = rank r's

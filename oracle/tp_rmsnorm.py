@@ -16,6 +16,11 @@ bench_rmsnorm_tp.py:16-22 (identical to test_rmsnorm_tp.py:15-26):
     y_k        = (x_k * inv) * w_k                          (:162-170)
 which is what the CUDA kernels of this repository compute (in bf16/fp16 too).
 
+``residual_add`` / ``allreduce_path_residual`` / ``fused_path_residual`` cover
+the fused residual add, which the reference does not have: the updated residual
+is z_k = (x_k + r_k).to(dtype) (an fp32 add rounded once, as torch computes
+``x + r`` for bf16/fp16), and the norm is either path above applied to z_k.
+
 Arrays: fp32 values are np.float32; bf16 values are carried as np.uint16 bit
 patterns; fp16 values as np.float16. Sums are taken in float64 and rounded to
 fp32 once, which is within an ulp or two of torch's fp32 reductions.
@@ -130,6 +135,26 @@ def fused_path(xs: Sequence[np.ndarray], ws: Sequence[np.ndarray], eps: float,
         wf = to_f32(dtype, w)
         outs.append(((xf * inv).astype(np.float32) * wf).astype(np.float32))  # (:166-169)
     return outs
+
+
+def residual_add(x: np.ndarray, r: np.ndarray, dtype: str) -> np.ndarray:
+    """z = (x + r) rounded once to `dtype`, in the stored representation of `dtype`."""
+    with np.errstate(over="ignore"):
+        return from_f32(dtype, (to_f32(dtype, x) + to_f32(dtype, r)).astype(np.float32))
+
+
+def allreduce_path_residual(xs: Sequence[np.ndarray], rs: Sequence[np.ndarray],
+                            ws: Sequence[np.ndarray], eps: float, dtype: str):
+    """(outputs, updated residuals): the AllReduce path on z_k = x_k + r_k."""
+    zs = [residual_add(x, r, dtype) for x, r in zip(xs, rs)]
+    return allreduce_path(zs, ws, eps, dtype), zs
+
+
+def fused_path_residual(xs: Sequence[np.ndarray], rs: Sequence[np.ndarray],
+                        ws: Sequence[np.ndarray], eps: float, dtype: str):
+    """(outputs, updated residuals): the fused-kernel formula on z_k = x_k + r_k."""
+    zs = [residual_add(x, r, dtype) for x, r in zip(xs, rs)]
+    return fused_path(zs, ws, eps, dtype), zs
 
 
 # Tolerances of the parity bar: fp32 relative 1e-5; bf16/fp16 one ulp of the

@@ -80,6 +80,15 @@ SIGNATURES = {
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, ctypes.c_float, _c_void_p],
     ),
+    "rmsnorm_tp_forward_residual": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32,
+         ctypes.c_float, _c_void_p],
+    ),
+    "rmsnorm_local_forward_residual": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, ctypes.c_float, _c_void_p],
+    ),
     "rmsnorm_tp_set_timeout": (_i32, [_c_void_p, _u64]),
     "rmsnorm_tp_set_profile": (_i32, [_c_void_p, _c_void_p]),
     "rmsnorm_tp_poll_error": (_i32, [_c_void_p, ctypes.POINTER(_u32)]),
@@ -91,6 +100,14 @@ SIGNATURES = {
         [
             ctypes.POINTER(_c_void_p), _i32, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
             ctypes.POINTER(_c_void_p), _i64, _i64, _i32, ctypes.c_float, _c_void_p,
+        ],
+    ),
+    "rmsnorm_tp_forward_emulated_residual": (
+        _i32,
+        [
+            ctypes.POINTER(_c_void_p), _i32, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+            ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), _i64, _i64, _i32, ctypes.c_float,
+            _c_void_p,
         ],
     ),
     "rmsnorm_tp_forward_group_static": (

@@ -56,14 +56,33 @@ def _check_operands(x: torch.Tensor, weight: torch.Tensor) -> None:
         raise AssertionError("x and weight must be CUDA tensors on the same device")
 
 
+def _check_like(name: str, t: torch.Tensor, x: torch.Tensor) -> None:
+    if t.shape != x.shape or t.dtype != x.dtype or t.device != x.device or not t.is_contiguous():
+        raise AssertionError(f"{name} must be contiguous with x's shape, dtype and device")
+
+
 def local_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
-                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  out: Optional[torch.Tensor] = None,
+                  residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """TP = 1 RMSNorm on the GPU: ``x * rsqrt(mean(x^2) + eps) * weight`` in fp32,
-    rounded once to ``x.dtype`` (reference rmsnorm_tp/__init__.py:103-107)."""
+    rounded once to ``x.dtype`` (reference rmsnorm_tp/__init__.py:103-107).
+
+    ``residual`` (optional, not in the reference): fused residual add in the same
+    kernel -- ``z = x + residual`` (rounded to x's dtype) is written back into
+    ``residual`` and normalised instead of x."""
     _check_operands(x, weight)
     if out is None:
         out = torch.empty_like(x)
     rows, hidden = x.shape
+    if residual is not None:
+        _check_like("residual", residual, x)
+        check(
+            LIB.rmsnorm_local_forward_residual(out.data_ptr(), residual.data_ptr(), x.data_ptr(),
+                                               weight.data_ptr(), rows, hidden, _DTYPES[x.dtype],
+                                               float(eps), _stream_of(x.device.index)),
+            "rmsnorm_local_forward_residual",
+        )
+        return out
     check(
         LIB.rmsnorm_local_forward(out.data_ptr(), x.data_ptr(), weight.data_ptr(), rows, hidden,
                                   _DTYPES[x.dtype], float(eps), _stream_of(x.device.index)),
@@ -169,12 +188,24 @@ class TPCommBuffer:
         return self._generation
 
     def launch(self, out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, hidden: int,
-               eps: float) -> torch.Tensor:
+               eps: float, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One forward launch on the current stream, without the module around it
         (the counterpart of the reference's launch_fused_rmsnorm binding,
-        csrc/bindings.cpp:182-196, minus its generation argument)."""
+        csrc/bindings.cpp:182-196, minus its generation argument). ``residual``:
+        fused residual add, as in ``FusedTPRMSNorm.forward``."""
         _check_operands(x, weight)
         rows, hl = x.shape
+        if residual is not None:
+            _check_like("residual", residual, x)
+            self.next_generation()
+            check(
+                LIB.rmsnorm_tp_forward_residual(self._comm, out.data_ptr(), residual.data_ptr(),
+                                                x.data_ptr(), weight.data_ptr(), rows, hl, hidden,
+                                                _DTYPES[x.dtype], float(eps),
+                                                _stream_of(x.device.index)),
+                "rmsnorm_tp_forward_residual",
+            )
+            return out
         self.next_generation()
         check(
             LIB.rmsnorm_tp_forward(self._comm, out.data_ptr(), x.data_ptr(), weight.data_ptr(), rows,
@@ -271,19 +302,25 @@ class FusedTPRMSNorm:
         dist.barrier(group=tp_group)
 
     def forward(self, x: torch.Tensor, weight: torch.Tensor,
-                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                out: Optional[torch.Tensor] = None,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y = x * rsqrt(sum over the group of x^2 / (local_hidden_dim * tp_size) + eps) * weight.
 
         ``out`` (optional, not in the reference) receives the result instead of a
         fresh tensor; it must be contiguous with x's shape, dtype and device.
+        ``residual`` (optional, not in the reference): fused residual add in the
+        same kernel -- ``z = x + residual`` (rounded to x's dtype) is written back
+        into ``residual`` (the updated residual stream) and normalised instead of
+        x; ``residual`` must be x-shaped and must not overlap ``out``.
         """
         _check_operands(x, weight)
-        if out is not None and (out.shape != x.shape or out.dtype != x.dtype
-                                or out.device != x.device or not out.is_contiguous()):
-            raise AssertionError("out must be contiguous with x's shape, dtype and device")
+        if out is not None:
+            _check_like("out", out, x)
+        if residual is not None:
+            _check_like("residual", residual, x)
         num_rows, local_hidden_dim = x.shape
         if self.tp_size == 1:
-            return local_rmsnorm(x, weight, self.eps, out)
+            return local_rmsnorm(x, weight, self.eps, out, residual)
         if num_rows > self.num_max_rows:  # reference __init__.py:109
             raise AssertionError(f"num_rows {num_rows} > num_max_rows {self.num_max_rows}")
         if x.device.index != self.comm_buf.device:
@@ -292,6 +329,16 @@ class FusedTPRMSNorm:
             )
         output = torch.empty_like(x) if out is None else out
         self.comm_buf.next_generation()
+        if residual is not None:
+            check(
+                LIB.rmsnorm_tp_forward_residual(self.comm_buf._comm, output.data_ptr(),
+                                                residual.data_ptr(), x.data_ptr(), weight.data_ptr(),
+                                                num_rows, local_hidden_dim,
+                                                local_hidden_dim * self.tp_size, _DTYPES[x.dtype],
+                                                float(self.eps), _stream_of(x.device.index)),
+                "rmsnorm_tp_forward_residual",
+            )
+            return output
         check(
             LIB.rmsnorm_tp_forward(self.comm_buf._comm, output.data_ptr(), x.data_ptr(),
                                    weight.data_ptr(), num_rows, local_hidden_dim,
@@ -356,7 +403,10 @@ class EmulatedTPGroup:
             b.finalize_setup()
 
     def forward(self, xs: Sequence[torch.Tensor], weights: Sequence[torch.Tensor],
-                outs: Optional[Sequence[torch.Tensor]] = None) -> List[torch.Tensor]:
+                outs: Optional[Sequence[torch.Tensor]] = None,
+                residuals: Optional[Sequence[torch.Tensor]] = None) -> List[torch.Tensor]:
+        """Every rank's forward in one launch; ``residuals`` (one per rank): the
+        fused residual add of ``FusedTPRMSNorm.forward``."""
         tp = self.tp_size
         if len(xs) != tp or len(weights) != tp:
             raise AssertionError(f"need {tp} x slices and {tp} weights")
@@ -376,6 +426,19 @@ class EmulatedTPGroup:
         wptr = P(*[w.data_ptr() for w in weights])
         for b in self.bufs:
             b.next_generation()
+        if residuals is not None:
+            if len(residuals) != tp:
+                raise AssertionError(f"need {tp} residuals")
+            for r, x in zip(residuals, xs):
+                _check_like("residual", r, x)
+            rptr = P(*[r.data_ptr() for r in residuals])
+            check(
+                LIB.rmsnorm_tp_forward_emulated_residual(comms, tp, optr, rptr, xptr, wptr, rows, hl,
+                                                         _DTYPES[xs[0].dtype], float(self.eps),
+                                                         _stream_of(xs[0].device.index)),
+                "rmsnorm_tp_forward_emulated_residual",
+            )
+            return list(outs)
         check(
             LIB.rmsnorm_tp_forward_emulated(comms, tp, optr, xptr, wptr, rows, hl,
                                             _DTYPES[xs[0].dtype], float(self.eps),

@@ -56,6 +56,11 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(RMSNORM_TP_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
+int cuda_fail(cudaError_t e, const char* who, const char* what) {
+  return fail(RMSNORM_TP_ERR_CUDA, "%s: %s: %s (%s)", who, what, cudaGetErrorString(e),
+              cudaGetErrorName(e));
+}
+
 #define RTP_CUDA(call, what)                 \
   do {                                       \
     cudaError_t e_ = (call);                 \
@@ -331,25 +336,38 @@ static int check_shape(const char* who, int64_t rows, int64_t hl, int64_t hidden
   return RMSNORM_TP_OK;
 }
 
-int rmsnorm_tp_forward(rmsnorm_tp_comm* c, void* out, const void* x, const void* w, int64_t rows,
-                       int64_t hl, int64_t hidden, int dtype, float eps, void* stream) {
-  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "forward: NULL communicator");
-  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "forward: communicator not finalized");
-  int rc = check_shape("forward", rows, hl, hidden, dtype, out, x, w);
+// The residual of a fused residual add must not overlap the output (the kernel
+// writes both); any other overlap follows element-wise semantics.
+static int check_residual(const char* who, int64_t rows, int64_t hl, int dtype, const void* res,
+                          const void* out) {
+  if (rows > 0 && !res) return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL residual", who);
+  const uintptr_t n = (uintptr_t)rows * (uintptr_t)hl * (uintptr_t)rtp::elem_bytes(dtype);
+  const uintptr_t r0 = reinterpret_cast<uintptr_t>(res), o0 = reinterpret_cast<uintptr_t>(out);
+  if (rows > 0 && r0 < o0 + n && o0 < r0 + n)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: residual overlaps the output", who);
+  return RMSNORM_TP_OK;
+}
+
+static int forward_impl(const char* who, rmsnorm_tp_comm* c, void* out, void* res, const void* x,
+                        const void* w, int64_t rows, int64_t hl, int64_t hidden, int dtype,
+                        float eps, void* stream) {
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL communicator", who);
+  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "%s: communicator not finalized", who);
+  int rc = check_shape(who, rows, hl, hidden, dtype, out, x, w);
   if (rc != RMSNORM_TP_OK) return rc;
   if (rows > c->nmax)
-    return fail(RMSNORM_TP_ERR_ROWS, "forward: rows %lld > num_max_rows %lld", (long long)rows,
+    return fail(RMSNORM_TP_ERR_ROWS, "%s: rows %lld > num_max_rows %lld", who, (long long)rows,
                 (long long)c->nmax);
   const unsigned flag = *reinterpret_cast<volatile unsigned*>(c->host_flag);
   if (flag != 0u)
     return fail(RMSNORM_TP_ERR_DEVICE,
-                "forward: an earlier launch recorded device failure %u (a peer's partial sum "
+                "%s: an earlier launch recorded device failure %u (a peer's partial sum "
                 "never arrived); reset the communicator on every rank",
-                flag);
+                who, flag);
   if (rows == 0) return RMSNORM_TP_OK;
   KArgs a;
   std::memset(&a, 0, sizeof(a));
-  a.rp[0] = rtp::RankPtrs{out, x, w, c->state, c->host_flag_dev};
+  a.rp[0] = rtp::RankPtrs{out, x, w, c->state, c->host_flag_dev, res};
   for (int q = 0; q < c->tp; ++q) a.mbox[q] = c->peers[q];
   a.rows = rows;
   a.hl = hl;
@@ -370,18 +388,39 @@ int rmsnorm_tp_forward(rmsnorm_tp_comm* c, void* out, const void* x, const void*
     DeviceGuard guard(c->device);
     e = rtp::launch_forward(a, dtype, c->device, 1, reinterpret_cast<cudaStream_t>(stream), nullptr);
   }
-  if (e != cudaSuccess) return cuda_fail(e, "forward: kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, who, "kernel launch");
   return RMSNORM_TP_OK;
 }
 
-int rmsnorm_local_forward(void* out, const void* x, const void* w, int64_t rows, int64_t hidden,
-                          int dtype, float eps, void* stream) {
-  int rc = check_shape("local_forward", rows, hidden, hidden, dtype, out, x, w);
+int rmsnorm_tp_forward(rmsnorm_tp_comm* c, void* out, const void* x, const void* w, int64_t rows,
+                       int64_t hl, int64_t hidden, int dtype, float eps, void* stream) {
+  return forward_impl("forward", c, out, nullptr, x, w, rows, hl, hidden, dtype, eps, stream);
+}
+
+int rmsnorm_tp_forward_residual(rmsnorm_tp_comm* c, void* out, void* residual, const void* x,
+                                const void* w, int64_t rows, int64_t hl, int64_t hidden,
+                                int dtype, float eps, void* stream) {
+  if (valid_dtype(dtype) && rows >= 0 && hl >= 1) {
+    const int rc = check_residual("forward_residual", rows, hl, dtype, residual, out);
+    if (rc != RMSNORM_TP_OK) return rc;
+  }
+  return forward_impl("forward_residual", c, out, residual, x, w, rows, hl, hidden, dtype, eps,
+                      stream);
+}
+
+static int local_forward_impl(const char* who, bool with_res, void* out, void* res, const void* x,
+                              const void* w, int64_t rows, int64_t hidden, int dtype, float eps,
+                              void* stream) {
+  int rc = check_shape(who, rows, hidden, hidden, dtype, out, x, w);
   if (rc != RMSNORM_TP_OK) return rc;
+  if (with_res) {
+    rc = check_residual(who, rows, hidden, dtype, res, out);
+    if (rc != RMSNORM_TP_OK) return rc;
+  }
   if (rows == 0) return RMSNORM_TP_OK;
   KArgs a;
   std::memset(&a, 0, sizeof(a));
-  a.rp[0] = rtp::RankPtrs{out, x, w, nullptr, nullptr};
+  a.rp[0] = rtp::RankPtrs{out, x, w, nullptr, nullptr, res};
   a.rows = rows;
   a.hl = hidden;
   a.nmax = rows;
@@ -393,40 +432,59 @@ int rmsnorm_local_forward(void* out, const void* x, const void* w, int64_t rows,
   RTP_CUDA(cudaGetDevice(&dev), "local_forward: cudaGetDevice");
   cudaError_t e =
       rtp::launch_forward(a, dtype, dev, 1, reinterpret_cast<cudaStream_t>(stream), nullptr);
-  if (e != cudaSuccess) return cuda_fail(e, "local_forward: kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, who, "kernel launch");
   return RMSNORM_TP_OK;
 }
 
-int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
-                                const void* const* xs, const void* const* ws, int64_t rows,
-                                int64_t hl, int dtype, float eps, void* stream) {
+int rmsnorm_local_forward(void* out, const void* x, const void* w, int64_t rows, int64_t hidden,
+                          int dtype, float eps, void* stream) {
+  return local_forward_impl("local_forward", false, out, nullptr, x, w, rows, hidden, dtype, eps,
+                            stream);
+}
+
+int rmsnorm_local_forward_residual(void* out, void* residual, const void* x, const void* w,
+                                   int64_t rows, int64_t hidden, int dtype, float eps,
+                                   void* stream) {
+  return local_forward_impl("local_forward_residual", true, out, residual, x, w, rows, hidden, dtype,
+                            eps, stream);
+}
+
+static int forward_emulated_impl(const char* who, rmsnorm_tp_comm* const* comms, int tp,
+                                 void* const* outs, void* const* residuals, const void* const* xs,
+                                 const void* const* ws, int64_t rows, int64_t hl, int dtype,
+                                 float eps, void* stream) {
   if (!comms || !outs || !xs || !ws)
-    return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: NULL argument");
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL argument", who);
   if (tp < 2 || tp > rtp::kMaxTP)
-    return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: tp %d outside [2, %d]", tp, rtp::kMaxTP);
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: tp %d outside [2, %d]", who, tp, rtp::kMaxTP);
   for (int r = 0; r < tp; ++r) {
     const rmsnorm_tp_comm* c = comms[r];
-    if (!c) return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated: comms[%d] is NULL", r);
+    if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: comms[%d] is NULL", who, r);
     if (c->rank != r || c->tp != tp || c->device != comms[0]->device || c->nmax != comms[0]->nmax)
       return fail(RMSNORM_TP_ERR_INVALID,
-                  "forward_emulated: comms[%d] is rank %d of %d on device %d; expected rank %d of "
+                  "%s: comms[%d] is rank %d of %d on device %d; expected rank %d of "
                   "%d on device %d",
-                  r, c->rank, c->tp, c->device, r, tp, comms[0]->device);
+                  who, r, c->rank, c->tp, c->device, r, tp, comms[0]->device);
     if (!c->finalized)
-      return fail(RMSNORM_TP_ERR_STATE, "forward_emulated: comms[%d] not finalized", r);
-    int rc = check_shape("forward_emulated", rows, hl, hl * tp, dtype, outs[r], xs[r], ws[r]);
+      return fail(RMSNORM_TP_ERR_STATE, "%s: comms[%d] not finalized", who, r);
+    int rc = check_shape(who, rows, hl, hl * tp, dtype, outs[r], xs[r], ws[r]);
     if (rc != RMSNORM_TP_OK) return rc;
+    if (residuals != nullptr) {
+      rc = check_residual(who, rows, hl, dtype, residuals[r], outs[r]);
+      if (rc != RMSNORM_TP_OK) return rc;
+    }
     if (*reinterpret_cast<volatile unsigned*>(c->host_flag) != 0u)
-      return fail(RMSNORM_TP_ERR_DEVICE, "forward_emulated: rank %d recorded a device failure", r);
+      return fail(RMSNORM_TP_ERR_DEVICE, "%s: rank %d recorded a device failure", who, r);
   }
   if (rows > comms[0]->nmax)
-    return fail(RMSNORM_TP_ERR_ROWS, "forward_emulated: rows %lld > num_max_rows %lld",
-                (long long)rows, (long long)comms[0]->nmax);
+    return fail(RMSNORM_TP_ERR_ROWS, "%s: rows %lld > num_max_rows %lld",
+                who, (long long)rows, (long long)comms[0]->nmax);
   if (rows == 0) return RMSNORM_TP_OK;
   KArgs a;
   std::memset(&a, 0, sizeof(a));
   for (int r = 0; r < tp; ++r) {
-    a.rp[r] = rtp::RankPtrs{outs[r], xs[r], ws[r], comms[r]->state, comms[r]->host_flag_dev};
+    a.rp[r] = rtp::RankPtrs{outs[r], xs[r], ws[r], comms[r]->state, comms[r]->host_flag_dev,
+                            residuals != nullptr ? residuals[r] : nullptr};
     a.mbox[r] = comms[r]->mailbox;
   }
   a.rows = rows;
@@ -440,11 +498,27 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* con
   a.timeout_ns = comms[0]->timeout_ns;
   a.prof = comms[0]->prof;
   DeviceGuard guard(comms[0]->device);
-  if (guard.err != cudaSuccess) return cuda_fail(guard.err, "forward_emulated: cudaSetDevice");
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, who, "cudaSetDevice");
   cudaError_t e = rtp::launch_forward(a, dtype, comms[0]->device, tp,
                                       reinterpret_cast<cudaStream_t>(stream), nullptr);
-  if (e != cudaSuccess) return cuda_fail(e, "forward_emulated: cooperative launch");
+  if (e != cudaSuccess) return cuda_fail(e, who, "cooperative launch");
   return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
+                                const void* const* xs, const void* const* ws, int64_t rows,
+                                int64_t hl, int dtype, float eps, void* stream) {
+  return forward_emulated_impl("forward_emulated", comms, tp, outs, nullptr, xs, ws, rows, hl, dtype,
+                               eps, stream);
+}
+
+int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
+                                         void* const* residuals, const void* const* xs,
+                                         const void* const* ws, int64_t rows, int64_t hl,
+                                         int dtype, float eps, void* stream) {
+  if (!residuals) return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated_residual: NULL residuals");
+  return forward_emulated_impl("forward_emulated_residual", comms, tp, outs, residuals, xs, ws, rows,
+                               hl, dtype, eps, stream);
 }
 
 int rmsnorm_tp_set_profile(rmsnorm_tp_comm* c, uint64_t* dev_counters) {

@@ -17,6 +17,7 @@ struct RankPtrs {
   const void* w;
   DeviceState* state;        // null at TP = 1
   unsigned int* host_flag;   // device alias of the host-mapped failure flag (may be null)
+  void* res;                 // residual stream [rows, hl], read and rewritten (fused add); or null
 };
 
 // Kernel parameters (passed by value, read through __grid_constant__).
@@ -68,6 +69,11 @@ struct VariantDesc {
 
 constexpr int kBulkBase = 100;
 constexpr int kLocalBase = 200;   // TP = 1 register kernels: base + shape * depths + depth index
+// fused residual add: TP = 1 register kernels (base + shape), bulk kernels
+// (base + row bound), generic kernel
+constexpr int kLocalResBase = 300;
+constexpr int kBulkResBase = 400;
+constexpr int kGenericRes = -2;
 
 int elem_bytes(int dtype);
 
@@ -75,7 +81,7 @@ int elem_bytes(int dtype);
 // returns `code`.
 int record_error(int code, const char* msg);
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp = 1, int64_t rows = 0,
-                           int family = kFamilyAuto);
+                           int family = kFamilyAuto, bool residual = false);
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
 
 // Launch the forward kernel. grid_y > 1 only for the emulated (all ranks on one

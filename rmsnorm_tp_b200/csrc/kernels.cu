@@ -139,6 +139,17 @@ __device__ __forceinline__ uint4 normalize16(const uint4& xv, const uint4& wv, f
   return Pack<T>::pack(xf);
 }
 
+// Fused residual add: z = x + r in fp32, rounded once to T.
+template <typename T>
+__device__ __forceinline__ uint4 add16(const uint4& xv, const uint4& rv) {
+  float xf[Pack<T>::kE], rf[Pack<T>::kE];
+  Pack<T>::unpack(xv, xf);
+  Pack<T>::unpack(rv, rf);
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; ++e) xf[e] += rf[e];
+  return Pack<T>::pack(xf);
+}
+
 __device__ __forceinline__ float quiet_nan() { return __uint_as_float(0x7FC00000u); }
 
 // ---------------------------------------------------------------------------
@@ -470,8 +481,11 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 // tile waiting for peers, so every buffer holds loads in flight: a team keeps
 // kDepth tiles in flight, reduces and stores its oldest straight from the
 // registers and refills that buffer with the tile kDepth strides ahead.
+// kRes: fused residual add -- each buffer also holds the residual rows;
+// z = x + r (rounded to T) is written back to the residual and normalised.
 // ---------------------------------------------------------------------------
-template <typename T, int kVec, int kW, int kRows, int kBlock, int kMinBlocks, int kDepth>
+template <typename T, int kVec, int kW, int kRows, int kBlock, int kMinBlocks, int kDepth,
+          bool kRes = false>
 __global__ void __launch_bounds__(kBlock, kMinBlocks)
     rmsnorm_local_vec_kernel(const __grid_constant__ KArgs a) {
   constexpr int kTeams = kBlock / 32 / kW;
@@ -489,6 +503,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
   const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
   uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
+  uint4* __restrict__ rg = kRes ? ptx::launder(reinterpret_cast<uint4*>(rp.res)) : nullptr;
 
   // two slots: a warp rewrites slot s only after the next team barrier, which
   // every warp of the team reaches after reading slot s
@@ -500,7 +515,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 
   auto nrows_of = [&](int64_t tt) { return (int)min((int64_t)kRows, a.rows - tt * kRows); };
 
-  auto load = [&](int64_t tt, uint4 (&xv)[kRows][kVec]) {
+  auto load = [&](int64_t tt, uint4 (&xv)[kRows][kVec], uint4 (&rv)[kRows][kVec]) {
     const int64_t row0 = tt * kRows;
     const int nr = nrows_of(tt);
 #pragma unroll
@@ -509,16 +524,34 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
         const int c = (j * kW + wit) * 32 + lane;
-        if (r < nr && c < V)
+        if (r < nr && c < V) {
           xv[r][j] = ptx::ld_stream_v4(xr + c);
-        else
+          if constexpr (kRes) rv[r][j] = ptx::ld_stream_v4(rg + (row0 + r) * V + c);
+        } else {
           xv[r][j] = make_uint4(0u, 0u, 0u, 0u);
+          if constexpr (kRes) rv[r][j] = make_uint4(0u, 0u, 0u, 0u);
+        }
       }
     }
   };
 
-  // team-wide fp32 sum of squares, then y from the registers
-  auto finish = [&](int64_t tt, const uint4 (&xv)[kRows][kVec], int slot) {
+  // (kRes: z = x + r into xv, written back to the residual) team-wide fp32 sum
+  // of squares, then y from the registers
+  auto finish = [&](int64_t tt, uint4 (&xv)[kRows][kVec], const uint4 (&rv)[kRows][kVec],
+                    int slot) {
+    if constexpr (kRes) {
+      const int64_t row0 = tt * kRows;
+      const int nr = nrows_of(tt);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int c = (j * kW + wit) * 32 + lane;
+          xv[r][j] = add16<T>(xv[r][j], rv[r][j]);
+          if (r < nr && c < V) ptx::st_v4(rg + (row0 + r) * V + c, xv[r][j]);
+        }
+      }
+    }
     float ss[kRows];
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
@@ -558,18 +591,19 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   };
 
   uint4 xb[kDepth][kRows][kVec];
+  uint4 rb[kRes ? kDepth : 1][kRows][kVec];   // residual rows (kRes only)
 #pragma unroll
   for (int d = 0; d < kDepth; ++d)
-    if (first + d * stride < tiles) load(first + d * stride, xb[d]);
+    if (first + d * stride < tiles) load(first + d * stride, xb[d], rb[kRes ? d : 0]);
   int slot = 0;
   for (int64_t base = first; base < tiles; base += kDepth * stride) {
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) {
       const int64_t tt = base + d * stride;
       if (tt >= tiles) break;
-      finish(tt, xb[d], slot);
+      finish(tt, xb[d], rb[kRes ? d : 0], slot);
       slot ^= 1;
-      if (tt + kDepth * stride < tiles) load(tt + kDepth * stride, xb[d]);
+      if (tt + kDepth * stride < tiles) load(tt + kDepth * stride, xb[d], rb[kRes ? d : 0]);
     }
   }
   flush_stats(a, WaitStats{}, t_start);
@@ -579,7 +613,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 // Generic kernel: any width and alignment. One CTA per row at a time, scalar
 // loads, x read twice (the second read normally hits L2). Same exchange.
 // ---------------------------------------------------------------------------
-template <typename T, int kBlock>
+template <typename T, int kBlock, bool kRes = false>
 __global__ void __launch_bounds__(kBlock)
     tp_rmsnorm_generic_kernel(const __grid_constant__ KArgs a) {
   constexpr int kWarps = kBlock / 32;
@@ -595,6 +629,7 @@ __global__ void __launch_bounds__(kBlock)
   const T* __restrict__ xg = reinterpret_cast<const T*>(rp.x);
   const T* __restrict__ wg = reinterpret_cast<const T*>(rp.w);
   T* __restrict__ yg = reinterpret_cast<T*>(rp.out);
+  T* rg = reinterpret_cast<T*>(rp.res);   // kRes: residual, rewritten with z = x + r
   const bool exchange = a.tp > 1;
   const int64_t hl = a.hl;
 
@@ -617,7 +652,12 @@ __global__ void __launch_bounds__(kBlock)
     const T* xr = xg + row * hl;
     float s = 0.f;
     for (int64_t i = threadIdx.x; i < hl; i += kBlock) {
-      const float v = Pack<T>::to_f(xr[i]);
+      float v = Pack<T>::to_f(xr[i]);
+      if constexpr (kRes) {
+        const T z = Pack<T>::from_f(v + Pack<T>::to_f(rg[row * hl + i]));
+        rg[row * hl + i] = z;
+        v = Pack<T>::to_f(z);
+      }
       s = fmaf(v, v, s);
     }
     s = warp_allreduce_sum(s);
@@ -648,8 +688,9 @@ __global__ void __launch_bounds__(kBlock)
     const float var = s_sum / a.hidden_f;
     const float inv = s_ok ? rsqrtf(var + a.eps) : quiet_nan();
     T* yr = yg + row * hl;
+    const T* zr = kRes ? rg + row * hl : xr;   // this thread's own residual writes above
     for (int64_t i = threadIdx.x; i < hl; i += kBlock) {
-      const float v = Pack<T>::to_f(xr[i]);
+      const float v = Pack<T>::to_f(zr[i]);
       const float w = Pack<T>::to_f(wg[i]);
       yr[i] = Pack<T>::from_f((v * inv) * w);
     }
@@ -692,7 +733,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
-template <typename T, int kWarps, int kStages, int kRowsMax>
+// kRes (fused residual add): a stage holds the x tile and, stage_bytes / 2
+// further, the residual tile (two copies on the same mbarrier); the reduction
+// writes z = x + r (rounded to T) over the x tile and to the residual in HBM,
+// and the normalisation reads z.
+template <typename T, int kWarps, int kStages, int kRowsMax, bool kRes = false>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     tp_rmsnorm_bulk_kernel(const __grid_constant__ KArgs a) {
   static_assert(kRowsMax >= 1 && kRowsMax <= 32, "rows per tile");
@@ -732,6 +777,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int64_t wgid = (int64_t)blockIdx.x * kWarps + warp;
   const int64_t my_tiles = wgid < tiles ? (tiles - 1 - wgid) / nw + 1 : 0;
   const unsigned char* xg = reinterpret_cast<const unsigned char*>(rp.x);
+  unsigned char* rg = reinterpret_cast<unsigned char*>(rp.res);   // kRes only
+  const uint32_t res_off = kRes ? stage_bytes / 2u : 0u;          // residual tile in a stage
 
   auto row0_of = [&](int64_t kk) { return (wgid + kk * nw) * tile_rows; };
   auto nrows_of = [&](int64_t kk) { return (int)min((int64_t)tile_rows, a.rows - row0_of(kk)); };
@@ -740,9 +787,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const int st = (int)(kk % kStages);
     const uint32_t bytes = (uint32_t)nrows_of(kk) * row_bytes;
     const uint32_t bar = bar0 + 8u * (uint32_t)st;
-    ptx::mbar_arrive_expect_tx(bar, bytes);
+    ptx::mbar_arrive_expect_tx(bar, kRes ? 2u * bytes : bytes);
     ptx::bulk_load(ring_addr + (uint32_t)st * stage_bytes, xg + row0_of(kk) * (int64_t)row_bytes,
                    bytes, bar);
+    if constexpr (kRes)
+      ptx::bulk_load(ring_addr + (uint32_t)st * stage_bytes + res_off,
+                     rg + row0_of(kk) * (int64_t)row_bytes, bytes, bar);
   };
 
   int64_t issued = my_tiles < kStages ? my_tiles : kStages;
@@ -775,7 +825,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   auto reduce = [&](int64_t kk) {
     const uint4* xs = stage_ptr(kk);
     const int nr = nrows_of(kk);
-    if (kRowsMax == 1 || (a.schedule & 1)) {
+    if constexpr (kRes) {
+      // z = x + r over the x tile and into the residual rows, then sum z^2
+      uint4* zs = const_cast<uint4*>(xs);
+      const uint4* rs = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(xs) +
+                                                       res_off);
+      uint4* rgt = reinterpret_cast<uint4*>(rg) + row0_of(kk) * (int64_t)V;
+      for (int r = 0; r < nr; ++r) {
+        float acc = 0.f;
+        for (int v = lane; v < V; v += 32) {
+          const uint4 z = add16<T>(zs[r * V + v], rs[r * V + v]);
+          zs[r * V + v] = z;
+          ptx::st_v4(rgt + r * V + v, z);
+          acc += sumsq16<T>(z);
+        }
+        const float ss = warp_allreduce_sum(acc);
+        if (lane == 0) s_part[warp][kk % kStages][r] = ss;
+      }
+    } else if (kRowsMax == 1 || (a.schedule & 1)) {
       for (int r = 0; r < nr; ++r) {
         const uint4* xr = xs + r * V;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -976,8 +1043,9 @@ constexpr uint32_t kBulkMaxRowBytes = 16384;          // one row must fit a stag
 constexpr uint32_t kBulkSmemBudget = 216u * 1024u;    // dynamic smem of one CTA (1 CTA / SM)
 constexpr uint64_t kBulkMinCallBytes = 48ull << 20;   // auto: bulk kernels from 48 MiB of x
 // TP = 1 register kernels: tiles in flight per team. Measured on B200 (TP = 1,
-// hidden 4096, 1..65536 rows): 3 is fastest for bf16 and, but at 4096 rows, for
-// fp32 (4096 x 4096 bf16: 12.8 us at 3, 13.3 us at 4, 15.1 us at 6, which spills)
+// hidden 4096, 1..65536 rows): 3 is fastest for bf16 at every size and for fp32
+// but at 4096 rows (4096 x 4096 bf16: 12.8 us at 3, 13.3 us at 4, 15.1 us at 6,
+// which spills). With the fused residual add a buffer holds x and r: 2 tiles.
 constexpr int kLocalDepths[] = {3, 4};
 constexpr int kNumLocalDepths = sizeof(kLocalDepths) / sizeof(kLocalDepths[0]);
 constexpr int kDefaultLocalDepth = 0;                 // index into kLocalDepths
@@ -985,7 +1053,16 @@ constexpr int kDefaultLocalDepth = 0;                 // index into kLocalDepths
 // faster at 128 MiB, 45.3 vs 46.0 us; slower at 512 MiB, 169.6 vs 164.8 us)
 constexpr uint64_t kBulkMinLocalCallBytes = 256ull << 20;
 constexpr int kNumLocal = kNumShapes * kNumLocalDepths;
-constexpr int kSlots = kNumShapes + 1 + kNumBulk + kNumLocal;   // register, generic, bulk, local
+constexpr int kLocalResDepth = 2;
+// fused residual add, bulk kernels: 4 warps x 3 stages, stage = x tile + residual tile
+constexpr int kBulkResWarps = 4, kBulkResStages = 3;
+constexpr uint32_t kBulkResMaxRowBytes = 8192;
+// occupancy-cache slots: register, generic, bulk, local, then the residual
+// kernels: local, bulk, generic
+constexpr int kSlotLocalRes = kNumShapes + 1 + kNumBulk + kNumLocal;
+constexpr int kSlotBulkRes = kSlotLocalRes + kNumShapes;
+constexpr int kSlotGenericRes = kSlotBulkRes + kNumRowBounds;
+constexpr int kSlots = kSlotGenericRes + 1;
 
 using KernelFn = void (*)(const KArgs);
 
@@ -1013,9 +1090,26 @@ struct KernelTable {
       RTP_LOCAL(4, 16, 1, 512, 1),
   };
 #undef RTP_LOCAL
+#define RTP_LOCAL_RES(V, W, R, B, M) rmsnorm_local_vec_kernel<T, V, W, R, B, M, kLocalResDepth, true>
+  static constexpr KernelFn local_res[kNumShapes] = {
+      RTP_LOCAL_RES(1, 1, 4, 256, 2), RTP_LOCAL_RES(2, 1, 2, 256, 2), RTP_LOCAL_RES(4, 1, 1, 256, 2),
+      RTP_LOCAL_RES(4, 2, 1, 256, 2), RTP_LOCAL_RES(4, 4, 1, 256, 2), RTP_LOCAL_RES(4, 8, 1, 256, 2),
+      RTP_LOCAL_RES(4, 16, 1, 512, 1),
+  };
+#undef RTP_LOCAL_RES
+  static constexpr KernelFn bulk_res[kNumRowBounds] = {
+      tp_rmsnorm_bulk_kernel<T, kBulkResWarps, kBulkResStages, 1, true>,
+      tp_rmsnorm_bulk_kernel<T, kBulkResWarps, kBulkResStages, 2, true>,
+      tp_rmsnorm_bulk_kernel<T, kBulkResWarps, kBulkResStages, 4, true>,
+      tp_rmsnorm_bulk_kernel<T, kBulkResWarps, kBulkResStages, 8, true>,
+  };
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
+  static constexpr KernelFn generic_res = tp_rmsnorm_generic_kernel<T, kGenericBlock, true>;
   static KernelFn get(int variant) {
+    if (variant == kGenericRes) return generic_res;
     if (variant < 0) return generic;
+    if (variant >= kBulkResBase) return bulk_res[variant - kBulkResBase];
+    if (variant >= kLocalResBase) return local_res[variant - kLocalResBase];
     if (variant >= kLocalBase) return local[variant - kLocalBase];
     if (variant >= kBulkBase) return bulk[variant - kBulkBase];
     return vec[variant];
@@ -1034,7 +1128,10 @@ KernelFn kernel_for(int dtype, int variant) {
 }
 
 int slot_of(int variant) {
+  if (variant == kGenericRes) return kSlotGenericRes;
   if (variant < 0) return kNumShapes;
+  if (variant >= kBulkResBase) return kSlotBulkRes + (variant - kBulkResBase);
+  if (variant >= kLocalResBase) return kSlotLocalRes + (variant - kLocalResBase);
   if (variant >= kLocalBase) return kNumShapes + 1 + kNumBulk + (variant - kLocalBase);
   if (variant >= kBulkBase) return kNumShapes + 1 + (variant - kBulkBase);
   return variant;
@@ -1117,10 +1214,63 @@ const Tuning& tuning() {
 }
 }  // namespace
 
-VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family) {
+namespace {
+// Row-size dependent normalisation order of the bulk kernels (KArgs::schedule),
+// as measured on B200 (TP = 1, 512 MiB of x): 8 KB rows one after another;
+// 4 KB rows per-row reduction, interleaved normalisation; 2 KB rows one after
+// another; <= 1 KB rows interleaved.
+int bulk_schedule(uint32_t row_bytes) {
+  if (row_bytes >= 8192u) return 3;
+  if (row_bytes >= 4096u) return 1;
+  if (row_bytes >= 2048u) return 3;
+  return 0;
+}
+
+// Kernels of the fused residual add. TP = 1: the local register kernel (two
+// tiles of x and r in flight per team) unless the call is large or the bulk
+// family is forced. With an exchange: the bulk kernel (there is no register
+// kernel with both an exchange and a residual), for rows of up to 8 KB, whose
+// x + r stages fit shared memory; the generic kernel otherwise.
+VariantDesc choose_residual_variant(int64_t hl, int dtype, bool vec_ok, int tp, int64_t rows,
+                                    int family) {
+  const int eb = elem_bytes(dtype);
+  const uint32_t row_bytes = vec_ok ? (uint32_t)(hl * eb) : 0u;
+  const uint64_t x_bytes = (uint64_t)rows * (uint64_t)hl * (uint64_t)eb;
+  const bool bulk_fits = vec_ok && row_bytes <= kBulkResMaxRowBytes;
+  const bool want_bulk =
+      bulk_fits && (tp > 1 || family == kFamilyBulk ||
+                    (family == kFamilyAuto && x_bytes >= kBulkMinLocalCallBytes));
+  if (want_bulk) {
+    const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
+    int max_rows = tp > 1 ? 32 / tp : 32;
+    if (max_rows > kBulkRowBounds[kNumRowBounds - 1]) max_rows = kBulkRowBounds[kNumRowBounds - 1];
+    int tile_rows = (int)(8192u / row_bytes);   // 8 KB of x (and 8 KB of r) per stage
+    if (tile_rows > max_rows) tile_rows = max_rows;
+    if (tile_rows < 1) tile_rows = 1;
+    int bound = 0;
+    while (kBulkRowBounds[bound] < tile_rows) ++bound;
+    const uint32_t stage = 2u * (((uint32_t)tile_rows * row_bytes + 127u) & ~127u);
+    const uint32_t smem = w_bytes + (uint32_t)(kBulkResWarps * kBulkResStages) * stage;  // <= 200 KB
+    return VariantDesc{kBulkResBase + bound, kBulkResStages, 1, tile_rows, kBulkResWarps * 32,
+                       stage, smem, 1, bulk_schedule(row_bytes), kBulkResStages};
+  }
+  if (vec_ok && tp == 1) {
+    const int64_t V = hl * eb / 16;
+    for (int i = 0; i < kNumShapes; ++i)
+      if (V <= 32ll * kShapes[i].w * kShapes[i].vec)
+        return VariantDesc{kLocalResBase + i, kShapes[i].vec, kShapes[i].w, kShapes[i].rows,
+                           kShapes[i].block, 0u, 0u, 0, 0, kLocalResDepth};
+  }
+  return VariantDesc{kGenericRes, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0, 0, 1};
+}
+}  // namespace
+
+VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family,
+                           bool residual) {
   const int eb = elem_bytes(dtype);
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
   if (family == kFamilyAuto) family = get_family();
+  if (residual) return choose_residual_variant(hl, dtype, vec_ok, tp, rows, family);
   // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank with an
   // exchange, >= kBulkMinLocalCallBytes at TP = 1), register kernels below
   // that, where their lower fixed cost wins (measured on B200: with an
@@ -1137,23 +1287,13 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     // one lane per (row, rank) in the exchange; at most 8 rows per tile
     int max_rows = tp > 1 ? 32 / tp : 32;
     if (max_rows > kBulkRowBounds[kNumRowBounds - 1]) max_rows = kBulkRowBounds[kNumRowBounds - 1];
-    // Tile size and row schedule by row size, as measured on B200 (TP = 1,
-    // 512 MiB of x): 8 KB rows -> 16 KB tiles at TP = 1, rows one after another
-    // (99% of the copy peak vs 85% with one-row tiles); 4 KB rows -> 8 KB tiles,
-    // per-row reduction, interleaved normalisation (99%); 2 KB rows -> 8 KB
-    // tiles, one after another (89%); <= 1 KB rows -> 8 KB tiles, interleaved.
+    // tiles of 8 KB of x; 16 KB for 8 KB rows at TP = 1 (measured on B200 at
+    // 512 MiB of x: 99% of the copy peak vs 85% with one-row tiles)
     uint32_t target = 8192u;
-    int schedule = 0;
-    if (row_bytes >= 8192u) {
-      // 2-row 16 KB tiles win at TP = 1 only; with an exchange, one-row 8 KB
-      // tiles measured faster (TP 2, 65536 rows: 98% vs 83% of the copy peak)
-      if (tp == 1) target = 16384u;
-      schedule = 3;
-    } else if (row_bytes >= 4096u) {
-      schedule = 1;
-    } else if (row_bytes >= 2048u) {
-      schedule = 3;
-    }
+    int schedule = bulk_schedule(row_bytes);
+    // 2-row 16 KB tiles for 8 KB rows win at TP = 1 only; with an exchange,
+    // one-row 8 KB tiles measured faster (TP 2, 65536 rows: 98% vs 83% of the copy peak)
+    if (row_bytes >= 8192u && tp == 1) target = 16384u;
     if (tuning().stage_bytes > 0) target = (uint32_t)tuning().stage_bytes;
     if (tuning().schedule >= 0) schedule = tuning().schedule;
     if (target < row_bytes) target = row_bytes;
@@ -1210,14 +1350,17 @@ Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
 cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
                            cudaStream_t stream, Plan* plan_out) {
   const int nranks = a_in.emulated ? grid_y : 1;
+  const bool residual = a_in.rp[0].res != nullptr;
   bool aligned = true;
   for (int r = 0; r < nranks; ++r) {
     const uintptr_t bits = reinterpret_cast<uintptr_t>(a_in.rp[r].x) |
                            reinterpret_cast<uintptr_t>(a_in.rp[r].out) |
-                           reinterpret_cast<uintptr_t>(a_in.rp[r].w);
+                           reinterpret_cast<uintptr_t>(a_in.rp[r].w) |
+                           reinterpret_cast<uintptr_t>(a_in.rp[r].res);
     if (bits & 15u) aligned = false;
   }
-  const VariantDesc v = choose_variant(a_in.hl, dtype, aligned, a_in.tp, a_in.rows);
+  const VariantDesc v =
+      choose_variant(a_in.hl, dtype, aligned, a_in.tp, a_in.rows, kFamilyAuto, residual);
   cudaError_t err = cudaSuccess;
   int resident = resident_ctas(device, dtype, v, &err);
   if (err != cudaSuccess) return err;

@@ -67,6 +67,24 @@ def test_local_forward_validates_shape_without_gpu():
     assert L.rmsnorm_local_forward(None, None, None, 0, 8, 0, 1e-6, None) == _lib.OK  # no rows: no launch
 
 
+def test_residual_entry_points_validate_without_gpu():
+    L = _lib.LIB
+    out, x, w = 0x10000, 0x20000, 0x30000          # never dereferenced: every call fails first
+    # NULL residual
+    assert L.rmsnorm_local_forward_residual(out, None, x, w, 4, 8, 0, 1e-6, None) == _lib.ERR_INVALID
+    assert L.rmsnorm_tp_forward_residual(None, out, None, x, w, 4, 8, 16, 0, 1e-6, None) == \
+        _lib.ERR_INVALID
+    # residual overlapping the output (4 rows x 8 fp32 = 128 bytes)
+    assert L.rmsnorm_local_forward_residual(out, out, x, w, 4, 8, 0, 1e-6, None) == _lib.ERR_INVALID
+    assert L.rmsnorm_local_forward_residual(out, out + 124, x, w, 4, 8, 0, 1e-6, None) == \
+        _lib.ERR_INVALID
+    assert "overlaps" in _lib.last_error()
+    # adjacent is fine up to the launch, which needs a communicator / GPU: no rows -> no launch
+    assert L.rmsnorm_local_forward_residual(out, out + 128, x, w, 0, 8, 0, 1e-6, None) == _lib.OK
+    assert L.rmsnorm_tp_forward_emulated_residual(None, 2, None, None, None, None, 4, 8, 0, 1e-6,
+                                                  None) == _lib.ERR_INVALID
+
+
 def test_check_maps_codes_to_exceptions():
     with pytest.raises(_lib.RMSNormTPDeviceError):
         _lib.check(_lib.ERR_DEVICE, "x")
