@@ -158,6 +158,29 @@ int rmsnorm_local_forward_residual(void* out, void* residual, const void* x,
                                    const void* weight, int64_t rows, int64_t hidden,
                                    int dtype, float eps, void* stream);
 
+/* ---- backward (no reference counterpart: the reference is forward-only) --- */
+
+/* Gradients of out = x * rsqrt(S / hidden + eps) * weight (S over the TP group):
+ *   D  = sum over the group of sum(dy * weight * x)       (per row, exchanged)
+ *   dx = inv * dy * weight - x * inv^3 * D / hidden,  inv = rsqrt(S / hidden + eps)
+ *   dw = sum over rows of dy * x * inv                     (this rank's columns)
+ * S and D are exchanged through the mailbox in two consecutive generations, so
+ * a backward call counts as two calls of the collective's generation. dx is
+ * [rows, local_hidden], dw [local_hidden], both in x's dtype; dx must not
+ * overlap x or dy. `workspace` is device memory of at least
+ * rmsnorm_tp_backward_workspace_bytes(rows, local_hidden) bytes (per-CTA fp32
+ * partials of dw, summed in a fixed order: deterministic). local_hidden may be
+ * at most 53248. Stream-ordered, graph-capturable like rmsnorm_tp_forward. */
+size_t rmsnorm_tp_backward_workspace_bytes(int64_t rows, int64_t local_hidden);
+int rmsnorm_tp_backward(rmsnorm_tp_comm* comm, void* dx, void* dw, const void* dy,
+                        const void* x, const void* weight, int64_t rows, int64_t local_hidden,
+                        int64_t hidden, int dtype, float eps, void* workspace,
+                        size_t workspace_bytes, void* stream);
+/* TP = 1, no communicator. */
+int rmsnorm_local_backward(void* dx, void* dw, const void* dy, const void* x, const void* weight,
+                           int64_t rows, int64_t hidden, int dtype, float eps, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* ---- failure detection and recovery (no reference counterpart) ---------- */
 
 /* Limit on each wait for a peer's partial sum, in nanoseconds (default
@@ -198,6 +221,13 @@ int rmsnorm_tp_forward_emulated(rmsnorm_tp_comm* const* comms, int tp,
                                 const void* const* weights, int64_t rows,
                                 int64_t local_hidden, int dtype, float eps,
                                 void* stream);
+/* The backward (rmsnorm_tp_backward) of every rank in one cooperative launch;
+ * workspaces[r] of workspace_bytes each. */
+int rmsnorm_tp_backward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* dxs,
+                                 void* const* dws, const void* const* dys, const void* const* xs,
+                                 const void* const* weights, int64_t rows, int64_t local_hidden,
+                                 int dtype, float eps, void* const* workspaces,
+                                 size_t workspace_bytes, void* stream);
 /* The same with a fused residual add (rmsnorm_tp_forward_residual) per rank. */
 int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp,
                                          void* const* outs, void* const* residuals,

@@ -157,6 +157,69 @@ def fused_path_residual(xs: Sequence[np.ndarray], rs: Sequence[np.ndarray],
     return fused_path(zs, ws, eps, dtype), zs
 
 
+def backward_path(xs: Sequence[np.ndarray], dys: Sequence[np.ndarray], ws: Sequence[np.ndarray],
+                  eps: float, dtype: str):
+    """Gradients of the TP RMSNorm (the reference is forward-only; this is the
+    derivative of its formula, bench_rmsnorm_tp.py:16-22, in float64):
+    with g = dy * w, S = sum over ranks of sum(x^2), D = sum over ranks of sum(g * x),
+    inv = 1 / sqrt(S / hidden + eps):
+        dx_k = inv * g_k - x_k * inv^3 * D / hidden,   dw_k = sum over rows of dy_k * x_k * inv.
+    Returns (dxs, dws) as float32 values (before rounding to x's dtype)."""
+    tp = len(xs)
+    hidden = xs[0].shape[-1] * tp
+    X = [to_f32(dtype, x).astype(np.float64) for x in xs]
+    DY = [to_f32(dtype, d).astype(np.float64) for d in dys]
+    W = [to_f32(dtype, w).astype(np.float64) for w in ws]
+    S = sum((x * x).sum(axis=-1) for x in X)[..., None]
+    D = sum((dy * w * x).sum(axis=-1) for x, dy, w in zip(X, DY, W))[..., None]
+    inv = 1.0 / np.sqrt(S / hidden + eps)
+    dxs = [(inv * dy * w - x * inv ** 3 * D / hidden).astype(np.float32)
+           for x, dy, w in zip(X, DY, W)]
+    dws = [(dy * x * inv).sum(axis=0).astype(np.float32) for x, dy in zip(X, DY)]
+    return dxs, dws
+
+
+def dw_magnitude(xs: Sequence[np.ndarray], dys: Sequence[np.ndarray], eps: float,
+                 dtype: str) -> List[np.ndarray]:
+    """Per rank and column, sum over rows of |dy * x * inv|: the scale of the
+    rounding error of any fp32 summation of dw (a sum over rows whose result can be
+    much smaller than its terms)."""
+    tp = len(xs)
+    hidden = xs[0].shape[-1] * tp
+    X = [to_f32(dtype, x).astype(np.float64) for x in xs]
+    S = sum((x * x).sum(axis=-1) for x in X)[..., None]
+    inv = 1.0 / np.sqrt(S / hidden + eps)
+    return [np.abs(to_f32(dtype, dy).astype(np.float64) * x * inv).sum(axis=0)
+            for x, dy in zip(X, dys)]
+
+
+# Backward tolerances: the fp32 kernels accumulate S, D and dw in fp32 in another
+# order than the float64 oracle, and dx subtracts two terms of similar size. For
+# dw, a sum over rows, the absolute tolerance also grows with the sum of the
+# magnitudes of its terms (`scale`, from dw_magnitude): 32 fp32 units of it, above
+# the typical error of the kernels' two-level summation (per-CTA partials of a
+# few rows, then at most 296 partials).
+BACKWARD_TOLERANCE = {
+    "f32": dict(rtol=1e-4, atol=1e-5),
+    "bf16": dict(rtol=1.6e-2, atol=2e-2),
+    "f16": dict(rtol=1.6e-2, atol=2e-2),
+}
+FP32_UNIT = 2.0 ** -24
+
+
+def compare_backward(dtype: str, got_f32: np.ndarray, want_f32: np.ndarray,
+                     scale: np.ndarray = None) -> dict:
+    """``compare`` with the backward tolerances (``scale``: see dw_magnitude)."""
+    tol = BACKWARD_TOLERANCE[dtype]
+    got = np.asarray(got_f32, dtype=np.float64)
+    want = np.asarray(want_f32, dtype=np.float64)
+    diff = np.abs(got - want)
+    atol = tol["atol"] if scale is None else np.maximum(tol["atol"], 32 * FP32_UNIT * scale)
+    bad = (diff > atol + tol["rtol"] * np.abs(want)) | (np.isnan(got) != np.isnan(want))
+    return {"ok": not bool(bad.any()), "max_abs": float(np.nanmax(diff)) if diff.size else 0.0,
+            "bad": int(bad.sum())}
+
+
 # Tolerances of the parity bar: fp32 relative 1e-5; bf16/fp16 one ulp of the
 # output type (atol 1e-2, rtol 1.6e-2).
 TOLERANCE = {

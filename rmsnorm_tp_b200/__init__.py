@@ -16,6 +16,7 @@ from .api import (
     buffer_of,
     dtype_code,
     local_rmsnorm,
+    local_rmsnorm_backward,
     plan,
     plan_coverage,
     profile_counters,
@@ -33,6 +34,7 @@ __all__ = [
     "EmulatedTPGroup",
     "exchange_handles",
     "local_rmsnorm",
+    "local_rmsnorm_backward",
     "RMSNormTPError",
     "RMSNormTPDeviceError",
     "plan",

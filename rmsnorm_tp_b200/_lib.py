@@ -110,6 +110,25 @@ SIGNATURES = {
             _c_void_p,
         ],
     ),
+    "rmsnorm_tp_backward_workspace_bytes": (_sz, [_i64, _i64]),
+    "rmsnorm_tp_backward": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32,
+         ctypes.c_float, _c_void_p, _sz, _c_void_p],
+    ),
+    "rmsnorm_local_backward": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, ctypes.c_float,
+         _c_void_p, _sz, _c_void_p],
+    ),
+    "rmsnorm_tp_backward_emulated": (
+        _i32,
+        [
+            ctypes.POINTER(_c_void_p), _i32, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+            ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), _i64,
+            _i64, _i32, ctypes.c_float, ctypes.POINTER(_c_void_p), _sz, _c_void_p,
+        ],
+    ),
     "rmsnorm_tp_forward_group_static": (
         _i32,
         [

@@ -91,6 +91,32 @@ def local_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
     return out
 
 
+def _backward_operands(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor):
+    _check_operands(x, weight)
+    _check_like("dy", dy, x)
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(weight)
+    rows, hl = x.shape
+    nbytes = LIB.rmsnorm_tp_backward_workspace_bytes(rows, hl)
+    ws = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=x.device)
+    return dx, dw, ws, nbytes
+
+
+def local_rmsnorm_backward(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor,
+                           eps: float = 1e-6):
+    """Gradients (dx, dw) of ``local_rmsnorm(x, weight, eps)`` for the output gradient dy
+    (no reference counterpart: the reference is forward-only)."""
+    dx, dw, ws, nbytes = _backward_operands(dy, x, weight)
+    rows, hidden = x.shape
+    check(
+        LIB.rmsnorm_local_backward(dx.data_ptr(), dw.data_ptr(), dy.data_ptr(), x.data_ptr(),
+                                   weight.data_ptr(), rows, hidden, _DTYPES[x.dtype], float(eps),
+                                   ws.data_ptr(), nbytes, _stream_of(x.device.index)),
+        "rmsnorm_local_backward",
+    )
+    return dx, dw
+
+
 class IpcHandle:
     """Serialised mailbox handle (128 bytes), the counterpart of the reference's
     ``IpcHandle`` POD with ``to_bytes``/``from_bytes`` (csrc/common.hpp:13-16,
@@ -214,6 +240,22 @@ class TPCommBuffer:
             "rmsnorm_tp_forward",
         )
         return out
+
+    def launch_backward(self, dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, hidden: int,
+                        eps: float):
+        """One backward launch on the current stream (two generations); returns (dx, dw)."""
+        dx, dw, ws, nbytes = _backward_operands(dy, x, weight)
+        rows, hl = x.shape
+        self.next_generation()
+        self.next_generation()
+        check(
+            LIB.rmsnorm_tp_backward(self._comm, dx.data_ptr(), dw.data_ptr(), dy.data_ptr(),
+                                    x.data_ptr(), weight.data_ptr(), rows, hl, hidden,
+                                    _DTYPES[x.dtype], float(eps), ws.data_ptr(), nbytes,
+                                    _stream_of(x.device.index)),
+            "rmsnorm_tp_backward",
+        )
+        return dx, dw
 
     # -- failure detection / recovery
     def set_timeout(self, seconds: float) -> None:
@@ -350,6 +392,34 @@ class FusedTPRMSNorm:
 
     __call__ = forward
 
+    def backward(self, dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor):
+        """Gradients ``(dx, dw)`` of ``forward(x, weight)`` for the output gradient ``dy``
+        (no reference counterpart). A collective like ``forward``; it uses two of the
+        group's generations (one exchange of sum(x^2), one of sum(dy * w * x) per row).
+        ``dw`` is this rank's slice of the weight gradient."""
+        if self.tp_size == 1:
+            return local_rmsnorm_backward(dy, x, weight, self.eps)
+        num_rows, local_hidden_dim = x.shape
+        if num_rows > self.num_max_rows:
+            raise AssertionError(f"num_rows {num_rows} > num_max_rows {self.num_max_rows}")
+        dx, dw, ws, nbytes = _backward_operands(dy, x, weight)
+        self.comm_buf.next_generation()
+        self.comm_buf.next_generation()
+        check(
+            LIB.rmsnorm_tp_backward(self.comm_buf._comm, dx.data_ptr(), dw.data_ptr(), dy.data_ptr(),
+                                    x.data_ptr(), weight.data_ptr(), num_rows, local_hidden_dim,
+                                    local_hidden_dim * self.tp_size, _DTYPES[x.dtype],
+                                    float(self.eps), ws.data_ptr(), nbytes,
+                                    _stream_of(x.device.index)),
+            "rmsnorm_tp_backward",
+        )
+        return dx, dw
+
+    def apply(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        """``forward`` recorded for autograd: ``backward`` runs this module's
+        backward kernel (a collective, so every rank must run the backward pass)."""
+        return _TPRMSNormFunction.apply(self, x, weight)
+
     # -- failure detection / recovery (no reference counterpart)
     def status(self) -> dict:
         return self.comm_buf.status() if self.comm_buf else {"code": 0}
@@ -447,6 +517,32 @@ class EmulatedTPGroup:
         )
         return list(outs)
 
+    def backward(self, dys: Sequence[torch.Tensor], xs: Sequence[torch.Tensor],
+                 weights: Sequence[torch.Tensor]):
+        """Every rank's backward in one launch; returns (dxs, dws)."""
+        tp = self.tp_size
+        if len(xs) != tp or len(weights) != tp or len(dys) != tp:
+            raise AssertionError(f"need {tp} dy, x and weight slices")
+        ops = [_backward_operands(dy, x, w) for dy, x, w in zip(dys, xs, weights)]
+        rows, hl = xs[0].shape
+        if any(tuple(x.shape) != (rows, hl) for x in xs) or any(x.dtype != xs[0].dtype for x in xs):
+            raise AssertionError("every rank needs the same shape and dtype")
+        P = ctypes.c_void_p * tp
+        comms = P(*[b._comm.value for b in self.bufs])
+        for b in self.bufs:
+            b.next_generation()
+            b.next_generation()
+        check(
+            LIB.rmsnorm_tp_backward_emulated(
+                comms, tp, P(*[o[0].data_ptr() for o in ops]), P(*[o[1].data_ptr() for o in ops]),
+                P(*[d.data_ptr() for d in dys]), P(*[x.data_ptr() for x in xs]),
+                P(*[w.data_ptr() for w in weights]), rows, hl, _DTYPES[xs[0].dtype],
+                float(self.eps), P(*[o[2].data_ptr() for o in ops]), ops[0][3],
+                _stream_of(xs[0].device.index)),
+            "rmsnorm_tp_backward_emulated",
+        )
+        return [o[0] for o in ops], [o[1] for o in ops]
+
     def reset(self, generation: int = 0) -> None:
         for b in self.bufs:
             b.reset(generation)
@@ -454,6 +550,22 @@ class EmulatedTPGroup:
     def destroy(self) -> None:
         for b in self.bufs:
             b.destroy()
+
+
+class _TPRMSNormFunction(torch.autograd.Function):
+    """Autograd around FusedTPRMSNorm: forward kernel, backward kernel."""
+
+    @staticmethod
+    def forward(ctx, module, x, weight):
+        ctx.module = module
+        ctx.save_for_backward(x, weight)
+        return module.forward(x, weight)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dx, dw = ctx.module.backward(dy.contiguous(), x, weight)
+        return None, dx, dw
 
 
 def profile_counters(device=None) -> torch.Tensor:

@@ -1,7 +1,8 @@
 """Build the C-ABI shared library ``librmsnorm_tp_b200.so`` in-tree for sm_100a.
 
 The library is plain CUDA C++ (no torch, no pybind11): kernels.cu holds the
-kernels and their launcher, comm.cpp the extern "C" entry points declared in
+forward kernels and their launcher, backward.cu the backward kernels,
+noalloc.cu the allocation-free group entry point, comm.cpp the extern "C" entry points declared in
 include/rmsnorm_tp_b200.h. The CUDA runtime is linked statically, so the
 library loads (and its symbols can be listed) on a machine without a GPU.
 
@@ -25,9 +26,10 @@ OUT_DIR = os.path.join(PKG_DIR, "_C")
 LIB_NAME = "librmsnorm_tp_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
-SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "comm.cpp"),
-           os.path.join(CSRC, "noalloc.cu")]
+SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "backward.cu"),
+           os.path.join(CSRC, "comm.cpp"), os.path.join(CSRC, "noalloc.cu")]
 HEADERS = [
+    os.path.join(CSRC, "device_common.cuh"),
     os.path.join(CSRC, "rtp_common.h"),
     os.path.join(CSRC, "internal.h"),
     os.path.join(CSRC, "ptx.cuh"),

@@ -1,0 +1,292 @@
+// Backward of the fused tensor-parallel RMSNorm for B200 (sm_100a).
+//
+// Forward (per row, rank k holding the columns of its slice):
+//   S = sum over ranks of sum(x^2),  inv = rsqrt(S / hidden + eps),  y = x * inv * w.
+// Backward, with g = dy * w:
+//   D  = sum over ranks of sum(g * x)
+//   dx = inv * g - x * (inv^3 * D / hidden)
+//   dw = sum over rows of dy * x * inv          (the rank's own columns: no exchange)
+// S and D are the only cross-rank quantities: one fp32 scalar each per row,
+// exchanged through the forward's mailbox protocol in two consecutive
+// generations (S with call g's tag in buffer g & 1, then D with call g + 1's
+// tag in the other buffer), so a backward launch advances the generation by 2.
+// A rank pushes a row's D only after it has received every peer's S of that
+// row; hence when a rank has all of a call's D partials, every peer is done
+// reading its S slots, and the next call may reuse that buffer.
+//
+// One CTA per row at a time (grid-stride over a grid of at most one resident
+// wave), x, dy and w read with 16-byte loads when aligned (else per element);
+// the second pass re-reads the row from L2. Each CTA accumulates its dw
+// partial in shared memory (fp32) and writes it to its row of the workspace;
+// a second kernel sums the partials in a fixed order (deterministic).
+// No counterpart in the reference, which is forward-only.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "device_common.cuh"
+#include "internal.h"
+#include "ptx.cuh"
+#include "rtp_common.h"
+
+namespace rtp {
+
+// kVec16: rows read as 16-byte chunks of Pack<T>::kE elements; else one element.
+template <typename T, int kBlock, bool kVec16>
+__global__ void __launch_bounds__(kBlock)
+    tp_rmsnorm_backward_kernel(const __grid_constant__ BArgs b) {
+  constexpr int kWarps = kBlock / 32;
+  constexpr int kC = kVec16 ? Pack<T>::kE : 1;   // elements per chunk
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const KArgs& a = b.k;
+  extern __shared__ float s_dw[];                // [hl]: this CTA's dw partial
+  __shared__ float s_red[kWarps][2];
+  __shared__ float s_tot[2];
+  __shared__ int s_ok;
+  __shared__ unsigned long long s_call;
+
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  WaitStats wst;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const T* __restrict__ xg = ptx::launder(reinterpret_cast<const T*>(rp.x));
+  const T* __restrict__ wg = ptx::launder(reinterpret_cast<const T*>(rp.w));
+  const T* __restrict__ dyg = ptx::launder(reinterpret_cast<const T*>(b.dy[ri]));
+  T* __restrict__ dxg = reinterpret_cast<T*>(rp.out);
+  const bool exchange = a.tp > 1;
+  const int64_t hl = a.hl;
+  const int64_t chunks = hl / kC;
+
+  auto load = [&](const T* base, int64_t c, float (&f)[kC]) {
+    if constexpr (kVec16) {
+      Pack<T>::unpack(ptx::ld_cached_v4(reinterpret_cast<const uint4*>(base) + c), f);
+    } else {
+      f[0] = Pack<T>::to_f(base[c]);
+    }
+  };
+  auto store = [&](T* base, int64_t c, const float (&f)[kC]) {
+    if constexpr (kVec16) {
+      ptx::st_v4(reinterpret_cast<uint4*>(base) + c, Pack<T>::pack(f));
+    } else {
+      base[c] = Pack<T>::from_f(f[0]);
+    }
+  };
+
+  for (int64_t c = threadIdx.x; c < chunks; c += kBlock) {
+#pragma unroll
+    for (int e = 0; e < kC; ++e) s_dw[c * kC + e] = 0.f;
+  }
+
+  unsigned long long call = 0ull;
+  uint32_t buf0 = 0u, tag0 = 0u, buf1 = 0u, tag1 = 0u;
+  if (exchange) {
+    if (threadIdx.x == 0) s_call = read_generation(rp.state);
+    __syncthreads();
+    call = s_call;
+    buf0 = buffer_of(call);
+    tag0 = tag_of(call);
+    buf1 = buffer_of(call + 1ull);
+    tag1 = tag_of(call + 1ull);
+  }
+
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const T* xr = xg + row * hl;
+    const T* dyr = dyg + row * hl;
+    // pass 1: local sum(x^2) and sum(dy * w * x)
+    float s = 0.f, d = 0.f;
+    for (int64_t c = threadIdx.x; c < chunks; c += kBlock) {
+      float xf[kC], dyf[kC], wf[kC];
+      load(xr, c, xf);
+      load(dyr, c, dyf);
+      load(wg, c, wf);
+#pragma unroll
+      for (int e = 0; e < kC; ++e) {
+        s = fmaf(xf[e], xf[e], s);
+        d = fmaf(dyf[e] * wf[e], xf[e], d);
+      }
+    }
+    s = warp_allreduce_sum(s);
+    d = warp_allreduce_sum(d);
+    if (lane == 0) {
+      s_red[warp][0] = s;
+      s_red[warp][1] = d;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float S = 0.f, D = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        S += s_red[w][0];
+        D += s_red[w][1];
+      }
+      bool ok = true;
+      if (exchange) {
+        // lane q < tp serves rank q: S first (generation `call`) ...
+        bool failed = false;
+        const float vs = push_poll(a, rank, rp, buf0, tag0, call, row, lane, lane < a.tp, S,
+                                   failed, wst);
+        ok = !__any_sync(0xFFFFFFFFu, failed);   // every lane's S poll ended before any D push
+        float tot = 0.f;
+        for (int p = 0; p < a.tp; ++p) tot += __shfl_sync(0xFFFFFFFFu, vs, p);
+        S = tot;
+        // ... then D (generation call + 1), rank order again
+        failed = false;
+        const float vd = push_poll(a, rank, rp, buf1, tag1, call + 1ull, row, lane, lane < a.tp, D,
+                                   failed, wst);
+        ok = !__any_sync(0xFFFFFFFFu, failed) && ok;
+        tot = 0.f;
+        for (int p = 0; p < a.tp; ++p) tot += __shfl_sync(0xFFFFFFFFu, vd, p);
+        D = tot;
+      }
+      if (lane == 0) {
+        s_tot[0] = S;
+        s_tot[1] = D;
+        s_ok = ok ? 1 : 0;
+      }
+    }
+    __syncthreads();
+    const float inv = s_ok ? rsqrtf(s_tot[0] / a.hidden_f + a.eps) : quiet_nan();
+    const float coef = (inv * inv * inv) * (s_tot[1] / a.hidden_f);
+    // pass 2 (x, dy, w again from L2): dx, and this CTA's dw partial
+    T* dxr = dxg + row * hl;
+    for (int64_t c = threadIdx.x; c < chunks; c += kBlock) {
+      float xf[kC], dyf[kC], wf[kC], dxf[kC];
+      load(xr, c, xf);
+      load(dyr, c, dyf);
+      load(wg, c, wf);
+#pragma unroll
+      for (int e = 0; e < kC; ++e) {
+        dxf[e] = inv * (dyf[e] * wf[e]) - xf[e] * coef;
+        s_dw[c * kC + e] += (dyf[e] * xf[e]) * inv;
+      }
+      store(dxr, c, dxf);
+    }
+    __syncthreads();   // s_red / s_tot are reused by the next row
+  }
+
+  // this CTA's dw partial -> its row of the workspace (each thread its own columns)
+  float* wsr = b.ws[ri] + (int64_t)blockIdx.x * hl;
+  for (int64_t c = threadIdx.x; c < chunks; c += kBlock) {
+#pragma unroll
+    for (int e = 0; e < kC; ++e) wsr[c * kC + e] = s_dw[c * kC + e];
+  }
+  if (exchange) finish_launch(rp.state, call, 2ull);
+  flush_stats(a, wst, t_start);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    backward_dw_reduce_kernel(const float* __restrict__ ws, int parts, int64_t hl,
+                              T* __restrict__ dw) {
+  ptx::grid_dep_wait();
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= hl) return;
+  float s = 0.f;
+  for (int c = 0; c < parts; ++c) s += ws[(int64_t)c * hl + j];
+  dw[j] = Pack<T>::from_f(s);
+}
+
+namespace {
+
+constexpr int kBwdBlock = 256;
+using BwdFn = void (*)(const BArgs);
+
+BwdFn backward_fn(int dtype, bool vec16) {
+  switch (dtype) {
+    case kF32:
+      return vec16 ? tp_rmsnorm_backward_kernel<float, kBwdBlock, true>
+                   : tp_rmsnorm_backward_kernel<float, kBwdBlock, false>;
+    case kBF16:
+      return vec16 ? tp_rmsnorm_backward_kernel<__nv_bfloat16, kBwdBlock, true>
+                   : tp_rmsnorm_backward_kernel<__nv_bfloat16, kBwdBlock, false>;
+    default:
+      return vec16 ? tp_rmsnorm_backward_kernel<__half, kBwdBlock, true>
+                   : tp_rmsnorm_backward_kernel<__half, kBwdBlock, false>;
+  }
+}
+
+constexpr int kMaxDevices = 64;
+std::atomic<unsigned int> g_smem_set[kMaxDevices][3][2];   // max dynamic smem raised to this
+
+}  // namespace
+
+cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, cudaStream_t stream,
+                            int* grid_out) {
+  const KArgs& a = b.k;
+  const int nranks = a.emulated ? grid_y : 1;
+  const int eb = elem_bytes(dtype);
+  bool vec16 = (a.hl * eb) % 16 == 0;
+  for (int r = 0; r < nranks; ++r) {
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(a.rp[r].x) |
+                           reinterpret_cast<uintptr_t>(a.rp[r].out) |
+                           reinterpret_cast<uintptr_t>(a.rp[r].w) |
+                           reinterpret_cast<uintptr_t>(b.dy[r]);
+    if (bits & 15u) vec16 = false;
+  }
+  const BwdFn fn = backward_fn(dtype, vec16);
+  const void* fp = reinterpret_cast<const void*>(fn);
+  const size_t smem = (size_t)a.hl * sizeof(float);
+  cudaError_t err;
+  if (smem > 48u * 1024u) {
+    const bool cacheable = device >= 0 && device < kMaxDevices;
+    if (!cacheable || g_smem_set[device][dtype][vec16 ? 1 : 0].load() < smem) {
+      err = cudaFuncSetAttribute(fp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (err != cudaSuccess) return err;
+      if (cacheable) g_smem_set[device][dtype][vec16 ? 1 : 0].store((unsigned)smem);
+    }
+  }
+  int per_sm = 0, sms = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp, kBwdBlock, smem);
+  if (err != cudaSuccess) return err;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return err;
+  int64_t grid = (int64_t)per_sm * sms / (grid_y > 1 ? grid_y : 1);   // one resident wave
+  if (grid > kBackwardMaxGrid) grid = kBackwardMaxGrid;
+  if (grid > a.rows) grid = a.rows;
+  if (grid < 1) return cudaErrorCooperativeLaunchTooLarge;
+  if (grid_out) *grid_out = (int)grid;
+  BArgs bb = b;
+  void* args[] = {&bb};
+  const dim3 g3((unsigned)grid, (unsigned)grid_y), blk(kBwdBlock);
+  if (grid_y > 1) return cudaLaunchCooperativeKernel(fp, g3, blk, args, smem, stream);
+  if (!get_dependent_launch()) return cudaLaunchKernel(fp, g3, blk, args, smem, stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g3;
+  cfg.blockDim = blk;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fp, args);
+}
+
+cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, int dtype,
+                             cudaStream_t stream) {
+  const dim3 grid((unsigned)((hl + 255) / 256)), blk(256);
+  switch (dtype) {
+    case kF32:
+      backward_dw_reduce_kernel<float><<<grid, blk, 0, stream>>>(ws, parts, hl,
+                                                                 static_cast<float*>(dw));
+      break;
+    case kBF16:
+      backward_dw_reduce_kernel<__nv_bfloat16><<<grid, blk, 0, stream>>>(
+          ws, parts, hl, static_cast<__nv_bfloat16*>(dw));
+      break;
+    default:
+      backward_dw_reduce_kernel<__half><<<grid, blk, 0, stream>>>(ws, parts, hl,
+                                                                  static_cast<__half*>(dw));
+      break;
+  }
+  return cudaPeekAtLastError();
+}
+
+}  // namespace rtp

@@ -521,6 +521,167 @@ int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp, 
                                hl, dtype, eps, stream);
 }
 
+// ---- backward ---------------------------------------------------------------
+
+size_t rmsnorm_tp_backward_workspace_bytes(int64_t rows, int64_t hl) {
+  if (rows <= 0 || hl < 1) return 0;
+  const int64_t parts = rows < rtp::kBackwardMaxGrid ? rows : rtp::kBackwardMaxGrid;
+  return (size_t)parts * (size_t)hl * sizeof(float);
+}
+
+static bool overlaps(const void* a, const void* b, uintptr_t n) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return n > 0 && a0 < b0 + n && b0 < a0 + n;
+}
+
+static int check_backward(const char* who, int64_t rows, int64_t hl, int64_t hidden, int dtype,
+                          const void* dx, const void* dw, const void* dy, const void* x,
+                          const void* w, const void* workspace, size_t workspace_bytes) {
+  int rc = check_shape(who, rows, hl, hidden, dtype, dx, x, w);
+  if (rc != RMSNORM_TP_OK) return rc;
+  if (hl > rtp::kBackwardMaxHidden)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: local_hidden %lld > %lld", who, (long long)hl,
+                (long long)rtp::kBackwardMaxHidden);
+  if (!dw || (rows > 0 && (!dy || !workspace)))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL dw, dy or workspace", who);
+  if (workspace_bytes < rmsnorm_tp_backward_workspace_bytes(rows, hl))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: workspace of %zu bytes < %zu", who, workspace_bytes,
+                rmsnorm_tp_backward_workspace_bytes(rows, hl));
+  const uintptr_t n = (uintptr_t)rows * (uintptr_t)hl * (uintptr_t)rtp::elem_bytes(dtype);
+  if (overlaps(dx, x, n) || overlaps(dx, dy, n))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: dx overlaps x or dy", who);
+  return RMSNORM_TP_OK;
+}
+
+// Launch the backward of `nranks` ranks (cooperative when emulated), then one
+// dw reduction per rank. rows == 0: only dw = 0.
+static int run_backward(const char* who, const rtp::BArgs& b, int dtype, int device, int nranks,
+                        void* const* dws, void* stream) {
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int parts = 0;
+  if (b.k.rows > 0) {
+    const cudaError_t e = rtp::launch_backward(b, dtype, device, b.k.emulated ? nranks : 1, st,
+                                               &parts);
+    if (e != cudaSuccess) return cuda_fail(e, who, "backward launch");
+  }
+  for (int r = 0; r < nranks; ++r) {
+    const cudaError_t e = rtp::launch_dw_reduce(b.ws[r], parts, b.k.hl, dws[r], dtype, st);
+    if (e != cudaSuccess) return cuda_fail(e, who, "dw reduction launch");
+  }
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_backward(rmsnorm_tp_comm* c, void* dx, void* dw, const void* dy, const void* x,
+                        const void* w, int64_t rows, int64_t hl, int64_t hidden, int dtype,
+                        float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "backward";
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL communicator", who);
+  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "%s: communicator not finalized", who);
+  int rc = check_backward(who, rows, hl, hidden, dtype, dx, dw, dy, x, w, workspace,
+                          workspace_bytes);
+  if (rc != RMSNORM_TP_OK) return rc;
+  if (rows > c->nmax)
+    return fail(RMSNORM_TP_ERR_ROWS, "%s: rows %lld > num_max_rows %lld", who, (long long)rows,
+                (long long)c->nmax);
+  const unsigned flag = *reinterpret_cast<volatile unsigned*>(c->host_flag);
+  if (flag != 0u)
+    return fail(RMSNORM_TP_ERR_DEVICE,
+                "%s: an earlier launch recorded device failure %u; reset the communicator on "
+                "every rank",
+                who, flag);
+  rtp::BArgs b;
+  std::memset(&b, 0, sizeof(b));
+  b.k.rp[0] = rtp::RankPtrs{dx, x, w, c->state, c->host_flag_dev, nullptr};
+  for (int q = 0; q < c->tp; ++q) b.k.mbox[q] = c->peers[q];
+  b.k.rows = rows;
+  b.k.hl = hl;
+  b.k.nmax = c->nmax;
+  b.k.hidden_f = (float)hidden;
+  b.k.eps = eps;
+  b.k.rank = c->rank;
+  b.k.tp = c->tp;
+  b.k.timeout_ns = c->timeout_ns;
+  b.k.prof = c->prof;
+  b.dy[0] = dy;
+  b.ws[0] = static_cast<float*>(workspace);
+  DeviceGuard guard(c->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, who, "cudaSetDevice");
+  void* dws[1] = {dw};
+  return run_backward(who, b, dtype, c->device, 1, dws, stream);
+}
+
+int rmsnorm_local_backward(void* dx, void* dw, const void* dy, const void* x, const void* w,
+                           int64_t rows, int64_t hidden, int dtype, float eps, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  const char* who = "local_backward";
+  int rc = check_backward(who, rows, hidden, hidden, dtype, dx, dw, dy, x, w, workspace,
+                          workspace_bytes);
+  if (rc != RMSNORM_TP_OK) return rc;
+  rtp::BArgs b;
+  std::memset(&b, 0, sizeof(b));
+  b.k.rp[0] = rtp::RankPtrs{dx, x, w, nullptr, nullptr, nullptr};
+  b.k.rows = rows;
+  b.k.hl = hidden;
+  b.k.nmax = rows;
+  b.k.hidden_f = (float)hidden;
+  b.k.eps = eps;
+  b.k.tp = 1;
+  b.dy[0] = dy;
+  b.ws[0] = static_cast<float*>(workspace);
+  int dev = 0;
+  RTP_CUDA(cudaGetDevice(&dev), "local_backward: cudaGetDevice");
+  void* dws[1] = {dw};
+  return run_backward(who, b, dtype, dev, 1, dws, stream);
+}
+
+int rmsnorm_tp_backward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* dxs,
+                                 void* const* dws, const void* const* dys, const void* const* xs,
+                                 const void* const* ws, int64_t rows, int64_t hl, int dtype,
+                                 float eps, void* const* workspaces, size_t workspace_bytes,
+                                 void* stream) {
+  const char* who = "backward_emulated";
+  if (!comms || !dxs || !dws || !dys || !xs || !ws || !workspaces)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL argument", who);
+  if (tp < 2 || tp > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: tp %d outside [2, %d]", who, tp, rtp::kMaxTP);
+  for (int r = 0; r < tp; ++r) {
+    const rmsnorm_tp_comm* c = comms[r];
+    if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: comms[%d] is NULL", who, r);
+    if (c->rank != r || c->tp != tp || c->device != comms[0]->device || c->nmax != comms[0]->nmax)
+      return fail(RMSNORM_TP_ERR_INVALID, "%s: comms[%d] is not rank %d of one group", who, r, r);
+    if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "%s: comms[%d] not finalized", who, r);
+    int rc = check_backward(who, rows, hl, hl * tp, dtype, dxs[r], dws[r], dys[r], xs[r], ws[r],
+                            workspaces[r], workspace_bytes);
+    if (rc != RMSNORM_TP_OK) return rc;
+    if (*reinterpret_cast<volatile unsigned*>(c->host_flag) != 0u)
+      return fail(RMSNORM_TP_ERR_DEVICE, "%s: rank %d recorded a device failure", who, r);
+  }
+  if (rows > comms[0]->nmax)
+    return fail(RMSNORM_TP_ERR_ROWS, "%s: rows %lld > num_max_rows %lld", who, (long long)rows,
+                (long long)comms[0]->nmax);
+  rtp::BArgs b;
+  std::memset(&b, 0, sizeof(b));
+  for (int r = 0; r < tp; ++r) {
+    b.k.rp[r] = rtp::RankPtrs{dxs[r], xs[r], ws[r], comms[r]->state, comms[r]->host_flag_dev,
+                              nullptr};
+    b.k.mbox[r] = comms[r]->mailbox;
+    b.dy[r] = dys[r];
+    b.ws[r] = static_cast<float*>(workspaces[r]);
+  }
+  b.k.rows = rows;
+  b.k.hl = hl;
+  b.k.nmax = comms[0]->nmax;
+  b.k.hidden_f = (float)(hl * tp);
+  b.k.eps = eps;
+  b.k.tp = tp;
+  b.k.emulated = 1;
+  b.k.timeout_ns = comms[0]->timeout_ns;
+  b.k.prof = comms[0]->prof;
+  DeviceGuard guard(comms[0]->device);
+  if (guard.err != cudaSuccess) return cuda_fail(guard.err, who, "cudaSetDevice");
+  return run_backward(who, b, dtype, comms[0]->device, tp, dws, stream);
+}
+
 int rmsnorm_tp_set_profile(rmsnorm_tp_comm* c, uint64_t* dev_counters) {
   if (!c) return fail(RMSNORM_TP_ERR_INVALID, "set_profile: NULL communicator");
   if (reinterpret_cast<uintptr_t>(dev_counters) & 7u)

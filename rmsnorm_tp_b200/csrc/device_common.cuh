@@ -1,0 +1,258 @@
+// Device helpers shared by the forward kernels (kernels.cu) and the backward
+// kernels (backward.cu): 16-byte element packing, warp sums, and one lane's
+// share of the cross-GPU exchange (push a partial into a peer's mailbox slot,
+// poll the local slot with a bounded wait), plus the generation bookkeeping.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+#include "rtp_common.h"
+
+namespace rtp {
+
+// ---------------------------------------------------------------------------
+// Element packing: 16 bytes = 4 fp32 or 8 bf16/fp16.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Pack;
+
+template <>
+struct Pack<float> {
+  static constexpr int kE = 4;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[4]) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[4]) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+};
+
+__device__ __forceinline__ void bf16x2_unpack(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xFFFF0000u);
+}
+__device__ __forceinline__ uint32_t bf16x2_pack(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Pack<__nv_bfloat16> {
+  static constexpr int kE = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
+    bf16x2_unpack(v.x, f[0], f[1]);
+    bf16x2_unpack(v.y, f[2], f[3]);
+    bf16x2_unpack(v.z, f[4], f[5]);
+    bf16x2_unpack(v.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+    return make_uint4(bf16x2_pack(f[0], f[1]), bf16x2_pack(f[2], f[3]), bf16x2_pack(f[4], f[5]),
+                      bf16x2_pack(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ void f16x2_unpack(uint32_t u, float& lo, float& hi) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  float2 f = __half22float2(h);
+  lo = f.x;
+  hi = f.y;
+}
+__device__ __forceinline__ uint32_t f16x2_pack(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Pack<__half> {
+  static constexpr int kE = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
+    f16x2_unpack(v.x, f[0], f[1]);
+    f16x2_unpack(v.y, f[2], f[3]);
+    f16x2_unpack(v.z, f[4], f[5]);
+    f16x2_unpack(v.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+    return make_uint4(f16x2_pack(f[0], f[1]), f16x2_pack(f[2], f[3]), f16x2_pack(f[4], f[5]),
+                      f16x2_pack(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
+};
+
+// Butterfly sum: every lane ends with the bit-identical total (IEEE addition is
+// commutative, and each step adds the same two operands on both partner lanes).
+__device__ __forceinline__ float warp_allreduce_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float sumsq16(const uint4& v) {
+  float f[Pack<T>::kE];
+  Pack<T>::unpack(v, f);
+  float a = 0.f, b = 0.f;
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; e += 2) {
+    a = fmaf(f[e], f[e], a);
+    b = fmaf(f[e + 1], f[e + 1], b);
+  }
+  return a + b;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 normalize16(const uint4& xv, const uint4& wv, float inv) {
+  float xf[Pack<T>::kE], wf[Pack<T>::kE];
+  Pack<T>::unpack(xv, xf);
+  Pack<T>::unpack(wv, wf);
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; ++e) xf[e] = (xf[e] * inv) * wf[e];
+  return Pack<T>::pack(xf);
+}
+
+// Fused residual add: z = x + r in fp32, rounded once to T.
+template <typename T>
+__device__ __forceinline__ uint4 add16(const uint4& xv, const uint4& rv) {
+  float xf[Pack<T>::kE], rf[Pack<T>::kE];
+  Pack<T>::unpack(xv, xf);
+  Pack<T>::unpack(rv, rf);
+#pragma unroll
+  for (int e = 0; e < Pack<T>::kE; ++e) xf[e] += rf[e];
+  return Pack<T>::pack(xf);
+}
+
+__device__ __forceinline__ float quiet_nan() { return __uint_as_float(0x7FC00000u); }
+
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange, one lane's share, in two steps.
+//
+// push_slot: store this rank's partial of `row` into rank q's mailbox slot
+// [buf][rank][row] (one relaxed system-scope 64-bit store over NVLink).
+// poll_slot: wait, bounded by the global timer, until slot [buf][q][row] of the
+// local mailbox carries `tag`, and return rank q's partial. Lanes with
+// q == rank or !active return `mine`. A timeout is recorded in the rank's
+// DeviceState (first failure wins) and mirrored to the host-mapped flag; it
+// also raises `abort`, which makes every other wait of this launch give up.
+// ---------------------------------------------------------------------------
+struct WaitStats {          // optional per-lane counters (KArgs::prof)
+  unsigned long long ns = 0;
+  unsigned int slow = 0;    // waits that found the slot not yet written
+  unsigned int fast = 0;    // waits satisfied by the first poll
+};
+
+__device__ __forceinline__ void push_slot(const KArgs& a, int rank, uint32_t buf, uint32_t tag,
+                                          int64_t row, int q, bool active, float mine) {
+  if (active && q != rank) {
+    unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, a.tp, a.nmax, row);
+    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
+  }
+}
+
+__device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankPtrs& rp,
+                                           uint32_t buf, uint32_t tag, unsigned long long call,
+                                           int64_t row, int q, bool active, float mine,
+                                           bool& failed, WaitStats& ws) {
+  failed = false;
+  if (!active || q == rank) return mine;
+  const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, a.tp, a.nmax, row);
+  unsigned long long w = ptx::ld_relaxed_sys_u64(src);
+  if (slot_tag(w) == tag) {
+    ws.fast += 1;
+    return slot_value(w);
+  }
+  uint32_t fail = kStatusOk;
+  const unsigned long long t0 = ptx::globaltimer();
+  unsigned long long now = t0;
+  for (;;) {
+    w = ptx::ld_relaxed_sys_u64(src);
+    if (slot_tag(w) == tag) break;
+    if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
+      fail = kStatusAborted;
+      break;
+    }
+    now = ptx::globaltimer();
+    if (now - t0 > a.timeout_ns) {
+      fail = kStatusTimeout;
+      break;
+    }
+  }
+  ws.slow += 1;
+  ws.ns += ptx::globaltimer() - t0;
+  if (fail == kStatusTimeout) {
+    DeviceState* st = rp.state;
+    if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {
+      st->err_src = (unsigned)q;
+      st->err_row = (long long)row;
+      st->err_expected = tag;
+      st->err_seen = slot_tag(w);
+      st->err_call = call;
+      if (rp.host_flag != nullptr) {
+        *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusTimeout;
+        __threadfence_system();
+      }
+    }
+    atomicExch(&st->abort, 1u);
+  }
+  failed = (fail != kStatusOk);
+  return slot_value(w);
+}
+
+__device__ __forceinline__ float push_poll(const KArgs& a, int rank, const RankPtrs& rp,
+                                           uint32_t buf, uint32_t tag, unsigned long long call,
+                                           int64_t row, int q, bool active, float mine,
+                                           bool& failed, WaitStats& ws) {
+  push_slot(a, rank, buf, tag, row, q, active, mine);
+  return poll_slot(a, rank, rp, buf, tag, call, row, q, active, mine, failed, ws);
+}
+
+// Adds the lanes' wait counters and the CTA's start/end times to KArgs::prof:
+// [0] wait ns summed over lanes, [1] slow waits, [2] fast waits,
+// [3] earliest CTA start, [4] latest CTA end (global timer, ns).
+__device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
+                                            unsigned long long t_start) {
+  if (a.prof == nullptr) return;
+  if (ws.slow) {
+    atomicAdd(a.prof + 0, ws.ns);
+    atomicAdd(a.prof + 1, (unsigned long long)ws.slow);
+  }
+  if (ws.fast) atomicAdd(a.prof + 2, (unsigned long long)ws.fast);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicMin(a.prof + 3, t_start);
+    atomicMax(a.prof + 4, ptx::globaltimer());
+  }
+}
+
+// Last CTA of the launch advances the rank's generation counter by `step`
+// (one per exchange the launch made: forward 1, backward 2).
+__device__ __forceinline__ void finish_launch(DeviceState* st, unsigned long long call,
+                                              unsigned long long step = 1ull) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&st->done, 1u);
+    if (prev == gridDim.x - 1) {
+      st->done = 0u;
+      st->call = call + step;
+      __threadfence();
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned long long read_generation(const DeviceState* st) {
+  return *reinterpret_cast<const volatile unsigned long long*>(&st->call);
+}
+
+}  // namespace rtp

@@ -89,6 +89,27 @@ Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
 cudaError_t launch_forward(const KArgs& a, int dtype, int device, int grid_y,
                            cudaStream_t stream, Plan* plan_out);
 
+// Backward launch: the forward's KArgs (rp[r].x = x, rp[r].w = weight,
+// rp[r].out = dx, the exchange fields) plus, per rank, dy and the fp32
+// workspace of per-CTA dw partials ([grid][hl]).
+struct BArgs {
+  KArgs k;
+  const void* dy[kMaxTP];
+  float* ws[kMaxTP];
+};
+// Upper bound of the backward grid (rows of the dw workspace).
+constexpr int kBackwardMaxGrid = 296;
+// Largest local width the backward kernel takes (its fp32 dw partial lives in
+// shared memory).
+constexpr int64_t kBackwardMaxHidden = 53248;
+// Launch the backward kernel (cooperative when grid_y > 1, emulated ranks);
+// *grid_out receives the grid (the dw partials per rank to reduce).
+cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, cudaStream_t stream,
+                            int* grid_out);
+// dw[j] = sum over parts c of ws[c][j], rounded to the dtype (fixed order).
+cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, int dtype,
+                             cudaStream_t stream);
+
 cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,
                          unsigned long long seq, int iters, int initiator,
                          unsigned long long timeout_ns, long long* out_ns,

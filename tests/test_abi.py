@@ -85,6 +85,31 @@ def test_residual_entry_points_validate_without_gpu():
                                                   None) == _lib.ERR_INVALID
 
 
+def test_backward_entry_points_validate_without_gpu():
+    L = _lib.LIB
+    assert L.rmsnorm_tp_backward_workspace_bytes(0, 64) == 0
+    assert L.rmsnorm_tp_backward_workspace_bytes(10, 64) == 10 * 64 * 4
+    assert L.rmsnorm_tp_backward_workspace_bytes(100000, 64) == 296 * 64 * 4   # grid bound
+    dx, dw, dy, x, w, ws = 0x10000, 0x20000, 0x30000, 0x40000, 0x50000, 0x60000
+    need = L.rmsnorm_tp_backward_workspace_bytes(4, 8)
+    # workspace too small
+    assert L.rmsnorm_local_backward(dx, dw, dy, x, w, 4, 8, 0, 1e-6, ws, need - 1, None) == \
+        _lib.ERR_INVALID
+    # dx overlapping dy / x
+    assert L.rmsnorm_local_backward(dy, dw, dy, x, w, 4, 8, 0, 1e-6, ws, need, None) == _lib.ERR_INVALID
+    assert L.rmsnorm_local_backward(x + 8, dw, dy, x, w, 4, 8, 0, 1e-6, ws, need, None) == \
+        _lib.ERR_INVALID
+    # NULL dw, width above the shared-memory bound
+    assert L.rmsnorm_local_backward(dx, None, dy, x, w, 4, 8, 0, 1e-6, ws, need, None) == \
+        _lib.ERR_INVALID
+    assert L.rmsnorm_local_backward(dx, dw, dy, x, w, 1, 53249, 0, 1e-6, ws, 1 << 20, None) == \
+        _lib.ERR_INVALID
+    assert L.rmsnorm_tp_backward(None, dx, dw, dy, x, w, 4, 8, 16, 0, 1e-6, ws, need, None) == \
+        _lib.ERR_INVALID
+    assert L.rmsnorm_tp_backward_emulated(None, 2, None, None, None, None, None, 4, 8, 0, 1e-6,
+                                          None, need, None) == _lib.ERR_INVALID
+
+
 def test_check_maps_codes_to_exceptions():
     with pytest.raises(_lib.RMSNormTPDeviceError):
         _lib.check(_lib.ERR_DEVICE, "x")
