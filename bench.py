@@ -68,6 +68,8 @@ def parse_args(argv=None):
                     help="launch our kernels without programmatic dependent launch (comparisons)")
     ap.add_argument("--residual", action="store_true",
                     help="sweeps of our arm: the fused residual add (x + residual, then the norm)")
+    ap.add_argument("--backward", action="store_true",
+                    help="sweeps of our arm: the backward pass (dx, dw) instead of the forward")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound on the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -521,6 +523,9 @@ class OursImpl:
     def __call__(self, x, w, out, res=None):
         self.m.forward(x, w, out=out, residual=res)
 
+    def backward(self, dy, x, w):
+        return self.m.backward(dy, x, w)
+
     def profile(self, step, world, n_capture=64, steps=256):
         """In-kernel counters in steady state: a CUDA graph of back-to-back calls
         replayed with the counters on (the pointer is captured with each launch).
@@ -630,17 +635,24 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
     def measure(impl, rows, hl, dtype, seed, steps, rotate=True):
         elem = torch.tensor([], dtype=dtype).element_size()
         use_res = args.residual and getattr(impl, "residual_ok", False)
+        use_bwd = args.backward and hasattr(impl, "backward")
         if rotate:
             xs, wt, outs = make_rotating_sets(rows, hl, dtype, seed, (4.5 if use_res else 3) * l2)
         else:
             x, wt = make_slice(rows, hl, dtype, seed, device="cuda")
             xs, outs = [x], [torch.empty_like(x)]
         n = len(xs)
-        # fused residual add: one residual per set, updated in place by every call
+        # fused residual add: one residual per set, updated in place by every call;
+        # backward: the set's out tensor stands for dy
         rs = [x.flip(0).contiguous() for x in xs] if use_res else None
+        if use_bwd:
+            for o, x in zip(outs, xs):
+                o.copy_(x.flip(1))
 
         def step(i):
-            if use_res:
+            if use_bwd:
+                impl.backward(outs[i % n], xs[i % n], wt)
+            elif use_res:
                 impl(xs[i % n], wt, outs[i % n], rs[i % n])
             else:
                 impl(xs[i % n], wt, outs[i % n])
@@ -665,10 +677,13 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
         if world > 1:
             dist.barrier()
         prof = impl.profile(step, world) if hasattr(impl, "profile") else None
-        # read x (and the residual), write y (and the residual), read w
+        # forward: read x (and the residual), write y (and the residual), read w;
+        # backward: read x and dy, write dx, read w, write dw
         b = algorithmic_bytes(rows, hl, elem) + (2 * rows * hl * elem if use_res else 0)
+        if use_bwd:
+            b = 3 * rows * hl * elem + 2 * hl * elem
         return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
-                "residual": use_res,
+                "residual": use_res, "backward": use_bwd,
                 "dependent_launch": getattr(impl, "dependent_launch", None), "profile": prof,
                 "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],
                 "eager_us_per_call": round(eager_us, 3), "host_wall_us_per_call": round(wall_us, 3),

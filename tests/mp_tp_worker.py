@@ -15,7 +15,9 @@ Checks, on the real group (TP = world size):
    reset, and results are correct afterwards;
 5. a prefill-size call (65536 rows, hidden 8192: the bulk-copy kernel), sampled
    rows gathered across ranks and checked by the oracle;
-6. the one-hop round-trip probe between ranks 0 and 1.
+6. the fused residual add and the backward pass (two exchanges per row) between
+   forward calls, checked by the oracle against every rank's inputs;
+7. the one-hop round-trip probe between ranks 0 and 1.
 """
 import datetime
 import os
@@ -172,7 +174,38 @@ def main():
                  y.index_select(0, idx), rank, "prefill 65536 x 8192 (sampled rows)")
     del x, y
 
-    # 6. latency probe between ranks 0 and 1
+    # 6. fused residual add, backward, forward again (the generation advances 1 + 2 + 1)
+    m.comm_buf.set_timeout(10.0)
+    g0 = m.comm_buf.device_generation()
+    for dtype in (torch.bfloat16, torch.float32):
+        name = NAMES[dtype]
+        rows, hidden = 300, 2048
+        xs, ws = make_group(rows, hidden, tp, dtype, 3000)
+        rs, _ = make_group(rows, hidden, tp, dtype, 3100)
+        dys, _ = make_group(rows, hidden, tp, dtype, 3200)
+        x, w, r, dy = (t[rank].to(dev) for t in (xs, ws, rs, dys))
+        y = m.forward(x, w, residual=r)
+        dx, dw = m.backward(dy, x, w)
+        y2 = m.forward(x, w)
+        torch.cuda.synchronize()
+        ys, zs = O.allreduce_path_residual([to_np(t) for t in xs], [to_np(t) for t in rs],
+                                           [to_np(t) for t in ws], 1e-6, name)
+        check(np.array_equal(np.asarray(zs[rank]), to_np(r)), f"residual z {name}")
+        res = O.compare(name, O.to_f32(name, to_np(y)), O.round_to(name, ys[rank]))
+        check(res["ok"], f"residual forward {name}: {res}")
+        want_dx, want_dw = O.backward_path([to_np(t) for t in xs], [to_np(t) for t in dys],
+                                           [to_np(t) for t in ws], 1e-6, name)
+        scale = O.dw_magnitude([to_np(t) for t in xs], [to_np(t) for t in dys], 1e-6, name)
+        res = O.compare_backward(name, O.to_f32(name, to_np(dx)), O.round_to(name, want_dx[rank]))
+        check(res["ok"], f"backward dx {name}: {res}")
+        res = O.compare_backward(name, O.to_f32(name, to_np(dw)), O.round_to(name, want_dw[rank]),
+                                 scale[rank])
+        check(res["ok"], f"backward dw {name}: {res}")
+        compare_rank(name, xs, ws, 1e-6, y2, rank, f"forward after backward {name}")
+    check(m.comm_buf.poll_error() == 0, "no device failure in residual / backward calls")
+    check(m.comm_buf.device_generation() == g0 + 8, "generation advanced by 4 per dtype")
+
+    # 7. latency probe between ranks 0 and 1
     import ctypes
     from rmsnorm_tp_b200._lib import LIB
 
