@@ -47,3 +47,25 @@ def allreduce_path_dist(x: torch.Tensor, w: torch.Tensor, eps: float, group=None
         dist.all_reduce(variance, op=dist.ReduceOp.SUM, group=group)   # (:20)
         variance = variance / tp                                       # (:21)
     return x * torch.rsqrt(variance + eps) * w                         # (:22)
+
+
+def backward_dist(x: torch.Tensor, dy: torch.Tensor, w: torch.Tensor, eps: float, group=None):
+    """This rank's (dx, dw) of the TP RMSNorm, the two per-row sums exchanged by
+    torch.distributed all_reduce (gloo on CPU in the multi-process tests). The
+    reference is forward-only; this restates the two-exchange backward of this
+    repository's kernel (S = sum x^2 over the group, then D = sum dy*w*x over the
+    group) in fp32 torch ops, as the derivative of bench_rmsnorm_tp.py:16-22."""
+    tp = dist.get_world_size(group)
+    hidden = x.shape[-1] * tp
+    xf, dyf, wf = x.float(), dy.float(), w.float()
+    S = (xf * xf).sum(dim=-1, keepdim=True)
+    if tp > 1:
+        dist.all_reduce(S, op=dist.ReduceOp.SUM, group=group)
+    g = dyf * wf
+    D = (g * xf).sum(dim=-1, keepdim=True)
+    if tp > 1:
+        dist.all_reduce(D, op=dist.ReduceOp.SUM, group=group)
+    inv = torch.rsqrt(S / hidden + eps)
+    dx = inv * g - xf * (inv ** 3) * (D / hidden)
+    dw = (dyf * xf * inv).sum(dim=0)
+    return dx, dw

@@ -14,6 +14,14 @@
 //    current call and compute the same sum in rank order.
 // 4. A rank that skips a call makes the others' waits run out (bounded), not
 //    hang, and no rank ever sums a wrong partial.
+// 5. Forward and backward calls mixed: a backward call takes two generations
+//    (sum(x^2) in generation g, buffer g & 1, then sum(dy * w * x) in g + 1, the
+//    other buffer) and pushes a row's second partial only after it has received
+//    every peer's first partial of that row, as the backward kernel does. With
+//    random skew, stale slots and the tag wrap, every partial read must be the
+//    current call's. Built with -DRTP_PLANT_EARLY_SECOND_PUSH, the second
+//    partial is pushed with the first (a planted protocol mistake): the program
+//    must then report failures (the negative control of this check).
 #include <algorithm>
 #include <atomic>
 #include <chrono>
@@ -159,6 +167,116 @@ struct Sim {
   }
 };
 
+// Forward (one exchange) and backward (two exchanges) calls mixed.
+struct MixedSim {
+  int tp;
+  int64_t nmax;
+  std::vector<std::vector<std::atomic<uint64_t>>> mbox;  // [rank][slot]
+  std::vector<int64_t> rows_of_call;
+  std::vector<int> backward;                             // 1: the call is a backward
+  std::vector<uint64_t> gen_of_call;                     // first generation of the call
+  std::atomic<int> errors{0};
+  std::atomic<int> timeouts{0};
+
+  MixedSim(int tp_, int64_t nmax_, int calls, uint64_t g0, unsigned seed)
+      : tp(tp_), nmax(nmax_), mbox(tp_) {
+    for (auto& m : mbox) {
+      std::vector<std::atomic<uint64_t>> v(mailbox_slots(tp, nmax));
+      for (auto& a : v) a.store(0, std::memory_order_relaxed);
+      m.swap(v);
+    }
+    std::mt19937 rng(seed);
+    uint64_t g = g0;
+    for (int c = 0; c < calls; ++c) {
+      rows_of_call.push_back(1 + (int64_t)(rng() % (uint64_t)nmax));
+      backward.push_back(rng() % 3 == 0 ? 1 : 0);
+      gen_of_call.push_back(g);
+      g += backward.back() ? 2u : 1u;
+    }
+  }
+
+  static float partial(int rank, int call, int64_t row, int which) {
+    return (float)((rank + 1) * 1000 + (call % 997)) + 0.25f * (float)row + 0.125f * (float)which;
+  }
+
+  void push(int rank, uint64_t g, int c, int64_t r, int which) {
+    for (int q = 0; q < tp; ++q)
+      if (q != rank)
+        mbox[q][slot_index(buffer_of(g), rank, tp, nmax, r)].store(
+            pack_slot(partial(rank, c, r, which), tag_of(g)), std::memory_order_relaxed);
+  }
+
+  // Sum of every rank's partial of row r in rank order; false on a timeout.
+  bool poll(int rank, uint64_t g, int c, int64_t r, int which, double timeout_s) {
+    float S = 0.f, want = 0.f;
+    for (int q = 0; q < tp; ++q) {
+      want += partial(q, c, r, which);
+      if (q == rank) {
+        S += partial(rank, c, r, which);
+        continue;
+      }
+      const auto t0 = std::chrono::steady_clock::now();
+      uint64_t w;
+      for (;;) {
+        w = mbox[rank][slot_index(buffer_of(g), q, tp, nmax, r)].load(std::memory_order_relaxed);
+        if (slot_tag(w) == tag_of(g)) break;
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+          timeouts.fetch_add(1);
+          return false;
+        }
+        std::this_thread::yield();
+      }
+      S += slot_value(w);
+    }
+    if (f32_bits(S) != f32_bits(want)) errors.fetch_add(1);
+    return true;
+  }
+
+  void run_rank(int rank, unsigned seed, double timeout_s) {
+    std::mt19937 rng(seed);
+    std::vector<int64_t> order;
+    for (int c = 0; c < (int)rows_of_call.size(); ++c) {
+      const uint64_t g = gen_of_call[c];
+      const int64_t R = rows_of_call[c];
+      order.resize(R);
+      for (int64_t r = 0; r < R; ++r) order[r] = r;
+      if (rng() % 8 == 0) std::this_thread::sleep_for(std::chrono::microseconds(rng() % 50));
+      std::shuffle(order.begin(), order.end(), rng);
+      for (int64_t r : order) {
+        push(rank, g, c, r, 0);
+#ifdef RTP_PLANT_EARLY_SECOND_PUSH
+        if (backward[c]) push(rank, g + 1, c, r, 1);   // planted: before the first exchange
+#endif
+      }
+      std::shuffle(order.begin(), order.end(), rng);
+      for (int64_t r : order) {
+        if (!poll(rank, g, c, r, 0, timeout_s)) return;
+#ifndef RTP_PLANT_EARLY_SECOND_PUSH
+        if (backward[c]) push(rank, g + 1, c, r, 1);   // only after row r's first exchange
+#endif
+      }
+      if (backward[c]) {
+        std::shuffle(order.begin(), order.end(), rng);
+        for (int64_t r : order)
+          if (!poll(rank, g + 1, c, r, 1, timeout_s)) return;
+      }
+    }
+  }
+};
+
+static void test_mixed_simulation(int tp, uint64_t g0, int calls, unsigned seed,
+                                  double timeout_s = 20.0) {
+  MixedSim sim(tp, 40, calls, g0, seed);
+  std::vector<std::thread> th;
+  for (int r = 0; r < tp; ++r)
+    th.emplace_back([&sim, r, seed, timeout_s] { sim.run_rank(r, seed * 17 + r, timeout_s); });
+  for (auto& t : th) t.join();
+  CHECK(sim.timeouts.load() == 0, "mixed tp %d: %d unexpected timeouts", tp, sim.timeouts.load());
+  CHECK(sim.errors.load() == 0, "mixed tp %d: %d wrong sums", tp, sim.errors.load());
+  std::printf("PASS mixed forward/backward simulation tp=%d g0=%llu calls=%d\n", tp,
+              (unsigned long long)g0, calls);
+}
+
 static void test_simulation(int tp, uint64_t g0, int calls, unsigned seed) {
   Sim sim(tp, 48, calls, g0, seed);
   std::vector<std::thread> th;
@@ -188,6 +306,11 @@ static void test_skipped_call_times_out() {
 }
 
 int main() {
+#ifdef RTP_PLANT_EARLY_SECOND_PUSH
+  test_mixed_simulation(4, 0ull, 2000, 5, 0.5);
+  std::printf("%d FAILURES\n", g_failures);
+  return g_failures ? 1 : 0;
+#endif
   test_generation();
   test_packing();
   const uint64_t P = 0xFFFFFFFFull;
@@ -195,6 +318,9 @@ int main() {
   test_simulation(4, P - 1500ull, 3000, 2);           // crosses the tag period
   test_simulation(8, (1ull << 32) - 1000ull, 2000, 3); // crosses the 32-bit wrap
   test_skipped_call_times_out();
+  test_mixed_simulation(2, 0ull, 3000, 4);
+  test_mixed_simulation(4, P - 1500ull, 2000, 5);           // crosses the tag period
+  test_mixed_simulation(8, (1ull << 32) - 1000ull, 1500, 6); // crosses the 32-bit wrap
   if (g_failures) {
     std::printf("%d FAILURES\n", g_failures);
     return 1;

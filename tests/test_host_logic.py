@@ -153,3 +153,16 @@ def test_protocol_host_program(tmp_path):
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "ALL PASS" in res.stdout
+
+
+def test_protocol_simulation_catches_an_early_second_push(tmp_path):
+    """Negative control of the mixed forward / backward simulation: pushing a
+    backward call's second partial before the row's first exchange completes lets
+    a fast rank overwrite slots a slow rank still awaits -- the program must fail."""
+    exe = tmp_path / "test_protocol_planted"
+    src = os.path.join(ROOT, "tests", "cpp", "test_protocol.cpp")
+    inc = os.path.join(ROOT, "rmsnorm_tp_b200", "csrc")
+    subprocess.run(["g++", "-O2", "-std=c++17", "-pthread", "-Wall", "-DRTP_PLANT_EARLY_SECOND_PUSH",
+                    "-I", inc, src, "-o", str(exe)], check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode != 0 and "FAIL" in res.stdout, res.stdout
