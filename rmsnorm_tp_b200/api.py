@@ -415,7 +415,7 @@ class FusedTPRMSNorm:
         )
         return dx, dw
 
-    def apply(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    def forward_with_grad(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
         """``forward`` recorded for autograd: ``backward`` runs this module's
         backward kernel (a collective, so every rank must run the backward pass)."""
         return _TPRMSNormFunction.apply(self, x, weight)

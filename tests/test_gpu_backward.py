@@ -130,7 +130,7 @@ def test_autograd_at_tp1_uses_the_backward_kernel():
     xs, ws, dys = _inputs(64, 2048, 1, torch.bfloat16, 43)
     x = xs[0].clone().requires_grad_()
     w = ws[0].clone().requires_grad_()
-    y = m.apply(x, w)
+    y = m.forward_with_grad(x, w)
     (y.float() * dys[0].float()).sum().backward()
     dx, dw = rtp.local_rmsnorm_backward(dys[0], xs[0], ws[0], 1e-6)
     torch.cuda.synchronize()
