@@ -301,7 +301,8 @@ uint32_t rmsnorm_tp_buffer_of(uint64_t generation);
 /* Message of the last failure on this thread ("" if none). */
 const char* rmsnorm_tp_last_error(void);
 
-/* ABI version (major * 100 + minor). */
+/* ABI version (major * 100 + minor). 1.01 added the residual, backward and
+ * dependent-launch entry points and named the plan's last field `depth`. */
 int rmsnorm_tp_abi_version(void);
 
 #ifdef __cplusplus

@@ -150,7 +150,7 @@ extern "C" {
 
 const char* rmsnorm_tp_last_error(void) { return g_last_error.c_str(); }
 
-int rmsnorm_tp_abi_version(void) { return 100; }
+int rmsnorm_tp_abi_version(void) { return 101; }
 
 uint32_t rmsnorm_tp_tag_of(uint64_t generation) { return rtp::tag_of(generation); }
 uint32_t rmsnorm_tp_buffer_of(uint64_t generation) { return rtp::buffer_of(generation); }
