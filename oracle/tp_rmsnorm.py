@@ -139,7 +139,7 @@ def fused_path(xs: Sequence[np.ndarray], ws: Sequence[np.ndarray], eps: float,
 
 def residual_add(x: np.ndarray, r: np.ndarray, dtype: str) -> np.ndarray:
     """z = (x + r) rounded once to `dtype`, in the stored representation of `dtype`."""
-    with np.errstate(over="ignore"):
+    with np.errstate(over="ignore", invalid="ignore"):
         return from_f32(dtype, (to_f32(dtype, x) + to_f32(dtype, r)).astype(np.float32))
 
 
