@@ -17,12 +17,18 @@ divided by the max-over-ranks time per step.
 Our arm prints one JSON line with the device-timed value (inputs resident in
 HBM, several input/output sets rotated so that they exceed L2), the roofline of
 the forward kernel, an end-to-end figure through the public API with pinned
-host buffers copied in and out inside the timed region, the CPU baseline, and
-clocks sampled with nvidia-smi during the timed region.
+host buffers copied in and out inside the timed region, the CPU baseline,
+clocks sampled with nvidia-smi around the timed region, the in-kernel wait
+counters (N > 1) and a parity check of real outputs against the oracle
+(after the timed region; the run fails if it does not pass).
 
 ``--impl reference`` times the reference's own CPU path (its AllReduce TP
 RMSNorm restated op for op on torch CPU tensors, all ranks' slices in one
-process, every host thread) on rank 0; other ranks exit without work.
+process, every host thread) on rank 0; other ranks exit without work. It never
+loads this repository's CUDA library. ``--ref-path gloo`` instead runs the
+reference's CPU/gloo configuration (world size 2, one process per rank, half the
+host threads each); ``--ref-path fused|nccl`` runs its GPU paths as sweep
+comparators.
 
 ``--sweep decode|prefill|llama|all`` additionally writes per-point JSON lines
 (decode latency, prefill GB/s, TP scaling) to --out.
@@ -31,9 +37,11 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import importlib.util
 import json
 import math
 import os
+import socket
 import statistics
 import subprocess
 import sys
@@ -44,6 +52,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
@@ -51,6 +60,15 @@ WORKLOAD = dict(name="llama3_8b", hidden=4096, rows=4096, dtype=torch.bfloat16, 
                 seed_base=1000)
 METRIC = "effective HBM GB/s, fused TP RMSNorm forward (Llama-3-8B rows, TP=N)"
 FALLBACK_HBM_GBS = 6650.0
+DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}
+
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# forward kernel on the benchmark workload, from ncu captures of this bench
+# command: several consecutive launches over the rotating sets with
+# --cache-control none, summed and divided by the launches, so that each
+# launch is charged the write-back of its y. Key: (workload, TP, dtype).
+# Absent keys are reported as null.
+TRAFFIC = {}
 
 
 def parse_args(argv=None):
@@ -59,10 +77,11 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ref-path", choices=["cpu", "fused", "nccl"], default="cpu",
-                    help="reference arm: its CPU path (default), or, as GPU comparators for "
-                         "the sweeps, its fused kernel (oracle/_ref) or its NCCL path")
-    ap.add_argument("--family", choices=["auto", "register", "bulk"], default="auto",
+    ap.add_argument("--ref-path", choices=["cpu", "gloo", "fused", "nccl"], default="cpu",
+                    help="reference arm: its CPU path on this workload (default), its CPU/gloo "
+                         "configuration (world size 2), or, as GPU comparators for the sweeps, "
+                         "its fused kernel (oracle/_ref) or its NCCL path")
+    ap.add_argument("--family", choices=["auto", "register", "bulk", "batch"], default="auto",
                     help="kernel family of our arm (comparisons)")
     ap.add_argument("--no-dependent-launch", action="store_true",
                     help="launch our kernels without programmatic dependent launch (comparisons)")
@@ -73,6 +92,8 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound on the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the untimed parity check (profiling runs)")
     ap.add_argument("--sweep", choices=["none", "decode", "prefill", "llama", "all"], default="none")
     ap.add_argument("--out", default=None, help="JSON-lines file for sweep points")
     ap.add_argument("--rows", type=int, default=None,
@@ -84,6 +105,21 @@ def parse_args(argv=None):
 
 
 # --------------------------------------------------------------------------- helpers
+def load_workloads():
+    """rmsnorm_tp_b200/workloads.py loaded by its path: the seeded input generators
+    without importing the package, whose __init__ loads the CUDA library (the
+    reference arm must not map this repository's library into its process)."""
+    name = "_rmsnorm_tp_b200_workloads"
+    mod = sys.modules.get(name)
+    if mod is None:
+        path = os.path.join(ROOT, "rmsnorm_tp_b200", "workloads.py")
+        spec = importlib.util.spec_from_file_location(name, path)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod            # dataclasses resolve their module by name
+        spec.loader.exec_module(mod)
+    return mod
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -101,25 +137,27 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic(rows, hl, dtype):
-    """dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape,
-    from the ncu table in profiles/ncu_traffic.md, or None if not captured."""
-    name = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
-    path = os.path.join(ROOT, "profiles", "ncu_traffic.md")
-    try:
-        with open(path) as f:
-            for line in f:
-                cells = [c.strip() for c in line.strip().strip("|").split("|")]
-                if len(cells) >= 6 and cells[0] == name and cells[1] == str(rows) \
-                        and cells[2] == str(hl):
-                    return int(cells[4]) + int(cells[5])
-    except (OSError, ValueError):
-        pass
-    return None
-
-
 def algorithmic_bytes(rows, hl, elem):
     return 2 * rows * hl * elem + hl * elem
+
+
+def workload_of(args):
+    w = dict(WORKLOAD)
+    if args.rows or args.hidden or args.dtype:
+        w["name"] = "custom"
+        w["rows"] = args.rows or w["rows"]
+        w["hidden"] = args.hidden or w["hidden"]
+        w["dtype"] = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
+                      None: w["dtype"]}[args.dtype]
+    return w
+
+
+def bench_config(w, tp):
+    """The `config` object of both arms' lines (identical for the same workload and N)."""
+    return {"workload": w["name"], "hidden": w["hidden"], "rows": w["rows"], "tp": tp,
+            "local_hidden": w["hidden"] // tp, "dtype": DTYPE_NAME[w["dtype"]], "eps": w["eps"],
+            "seed": f"{w['seed_base']} + rank", "parallelism": f"tp{tp}",
+            "l2": "inputs larger than L2: x/out sets rotated, more than 3x the L2 size in total"}
 
 
 class ClockSampler:
@@ -186,6 +224,12 @@ def gpu_uuid(device):
         return None
 
 
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_reference_time(xs, ws, eps, seconds, max_calls=10**6, min_calls=3):
     """Mean seconds per call of the reference's AllReduce path on torch CPU."""
@@ -221,23 +265,92 @@ def run_reference_gpu(args):
     return 0
 
 
+def _gloo_rank(rank, world, port, threads, steps, warmup, seconds, q):
+    """One rank of the CPU/gloo configuration: the reference's AllReduce path with
+    gloo's all_reduce, timed the reference's way (host wall clock, barrier inside)."""
+    import torch.distributed as d
+
+    from oracle import torch_port
+
+    torch.set_num_threads(threads)
+    d.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                         world_size=world, timeout=datetime.timedelta(seconds=120))
+    wl = load_workloads()
+    cfg = wl.BY_NAME["cpu_gloo_tp2"]
+    hl = cfg.hidden // world
+    x, w = wl.make_slice(cfg.rows[0], hl, cfg.dtype, cfg.seed_base + rank)
+    for _ in range(max(warmup, 1)):
+        torch_port.allreduce_path_dist(x, w, cfg.eps)
+    d.barrier()
+    n, t0 = 0, time.perf_counter()
+    while n < steps or (time.perf_counter() - t0 < seconds and n < 10 * steps):
+        torch_port.allreduce_path_dist(x, w, cfg.eps)
+        n += 1
+    d.barrier()
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt / n, float(n)], dtype=torch.float64)
+    d.all_reduce(t, op=d.ReduceOp.MAX)
+    if rank == 0:
+        q.put((float(t[0]), int(t[1]), hl, cfg.rows[0], cfg.eps))
+    d.destroy_process_group()
+
+
+def run_reference_gloo(args):
+    """--impl reference --ref-path gloo: the reference's CPU/gloo configuration
+    (world size 2, hidden 4096 split 2 x 2048, 1024 rows, fp32, eps 1e-6, seed
+    0 + rank), one process per rank with half the host threads each; prints one
+    JSON line with the per-call time (max over ranks)."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import torch.multiprocessing as mp
+
+    cores = os.cpu_count() or 2
+    threads = max(1, cores // 2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_gloo_rank,
+                         args=(r, 2, port, threads, max(args.steps, 100), args.warmup,
+                               args.cpu_seconds, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+    sec, n, hl, rows, eps = res
+    b = algorithmic_bytes(rows, hl, 4)
+    print(json.dumps({
+        "impl": "reference", "ref_path": "gloo", "metric": "ms per call, CPU/gloo TP RMSNorm",
+        "value": round(sec * 1e3, 4), "unit": "ms", "higher_is_better": False,
+        "per_rank_GBps": round(b / sec / 1e9, 3), "calls": n, "ranks": 2,
+        "threads_per_rank": threads, "cores": cores,
+        "config": {"workload": "cpu_gloo_tp2", "hidden": 2 * hl, "rows": rows, "tp": 2,
+                   "local_hidden": hl, "dtype": "f32", "eps": eps, "seed": "0 + rank"},
+        "sample": f"{n} calls per rank after warm-up, wall clock with a barrier at both ends, "
+                  "max over the two ranks"}), flush=True)
+    return 0
+
+
 def run_reference_arm(args):
     """--impl reference: rank 0 times the reference's CPU path on all ranks' data."""
+    if args.ref_path == "gloo":
+        return run_reference_gloo(args)
     if args.ref_path != "cpu":
         return run_reference_gpu(args)
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from rmsnorm_tp_b200.workloads import make_group
+    from oracle import torch_port
 
+    wl = load_workloads()
     tp = max(1, args.gpus)
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    w = WORKLOAD
-    xs, ws = make_group(w["rows"], w["hidden"], tp, w["dtype"], w["seed_base"])
+    w = workload_of(args)
+    xs, ws = wl.make_group(w["rows"], w["hidden"], tp, w["dtype"], w["seed_base"])
     hl = w["hidden"] // tp
-    from oracle import torch_port
-
+    elem = torch.tensor([], dtype=w["dtype"]).element_size()
     for _ in range(max(args.warmup, 1)):
         torch_port.allreduce_path_group(xs, ws, w["eps"])
     times = []
@@ -246,18 +359,19 @@ def run_reference_arm(args):
         torch_port.allreduce_path_group(xs, ws, w["eps"])
         times.append(time.perf_counter() - t0)
     s = sum(times) / len(times)
-    total = tp * algorithmic_bytes(w["rows"], hl, 2)
+    total = tp * algorithmic_bytes(w["rows"], hl, elem)
     value = total / s / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": tp, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(s * 1e3, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": w["name"], "hidden": w["hidden"], "rows": w["rows"], "tp": tp,
-                   "local_hidden": hl, "eps": w["eps"], "device": "cpu"},
+        "vs_baseline": None, "dtype": DTYPE_NAME[w["dtype"]], "data": "synthetic",
+        "config": bench_config(w, tp),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} full calls, all {tp} ranks' slices of "
-                                   f"{w['rows']}x{w['hidden']} bf16 in one process (torch CPU)"},
+                         "sample": f"{args.steps} full calls on the host CPU, all {tp} ranks' "
+                                   f"slices of {w['rows']}x{w['hidden']} "
+                                   f"{DTYPE_NAME[w['dtype']]} in one process (torch CPU, "
+                                   f"{cores} threads)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -284,15 +398,14 @@ def max_over_ranks(values, world):
 
 def make_rotating_sets(rows, hl, dtype, seed, min_bytes):
     """Enough (x, out) pairs that one pass over them moves more than `min_bytes`."""
-    from rmsnorm_tp_b200.workloads import make_slice
-
+    wl = load_workloads()
     elem = torch.tensor([], dtype=dtype).element_size()
     per = 2 * rows * hl * elem
     n = max(2, math.ceil(min_bytes / per))
     xs, outs = [], []
     w = None
     for i in range(n):
-        x, wi = make_slice(rows, hl, dtype, seed + 7919 * i, device="cuda")
+        x, wi = wl.make_slice(rows, hl, dtype, seed + 7919 * i, device="cuda")
         xs.append(x)
         outs.append(torch.empty_like(x))
         if w is None:
@@ -312,10 +425,7 @@ def time_steps(fn, steps):
     return start.elapsed_time(end)
 
 
-def time_graph(fn, n_capture, steps, world):
-    """Capture n_capture calls of fn(i) in a CUDA graph, replay it until about
-    `steps` calls ran, and return the CUDA-event time per call (ms, max over
-    ranks). Every replayed call is a full launch of the kernel."""
+def capture_graph(fn, n_capture):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
@@ -323,6 +433,16 @@ def time_graph(fn, n_capture, steps, world):
         for i in range(n_capture):
             fn(i)
     torch.cuda.synchronize()
+    return g
+
+
+def time_graph(fn, n_capture, steps, world, g=None):
+    """Capture n_capture calls of fn(i) in a CUDA graph (or use `g`), replay it
+    until about `steps` calls ran, and return the CUDA-event time per call (ms,
+    max over ranks). Every replayed call is a full launch of the kernel."""
+    own = g is None
+    if own:
+        g = capture_graph(fn, n_capture)
     if world > 1:
         dist.barrier()
     g.replay()                       # warm replay
@@ -338,23 +458,162 @@ def time_graph(fn, n_capture, steps, world):
     e1.record()
     torch.cuda.synchronize()
     per = max_over_ranks([e0.elapsed_time(e1) / (reps * n_capture)], world)[0]
-    del g
+    if own:
+        del g
     return per, reps * n_capture
 
 
-def plan_name(rtp, rows, hl, tp, dtype=torch.bfloat16):
+def kernel_name(rtp, rows, hl, tp, dtype=torch.bfloat16):
     p = rtp.plan(rows, hl, dtype, tp=tp)
     v = p["variant"]
-    if v >= 200:
-        return (f"rmsnorm_local_vec_kernel<bf16,{p['vec_per_lane']},{p['team_warps']},"
+    dt = DTYPE_NAME[dtype]
+    if v >= 500:
+        return (f"tp_rmsnorm_batch_kernel<{dt},{p['block_threads'] // 32} warps> "
+                f"{p['rows_per_tile']} rows/batch, {p['vec_per_lane']} slots")
+    if v >= 200 and v < 300:
+        return (f"rmsnorm_local_vec_kernel<{dt},{p['vec_per_lane']},{p['team_warps']},"
                 f"{p['rows_per_tile']},{p['block_threads']}> {p['depth']} tiles in flight")
-    if v >= 100:
-        return (f"tp_rmsnorm_bulk_kernel<bf16,{p['teams_per_cta']} warps,{p['vec_per_lane']} stages>"
+    if v >= 100 and v < 200:
+        return (f"tp_rmsnorm_bulk_kernel<{dt},{p['teams_per_cta']} warps,{p['vec_per_lane']} stages>"
                 f" {p['rows_per_tile']} rows/stage")
-    if v >= 0:
-        return (f"tp_rmsnorm_vec_kernel<bf16,{p['vec_per_lane']},{p['team_warps']},"
+    if v >= 0 and v < 100:
+        return (f"tp_rmsnorm_vec_kernel<{dt},{p['vec_per_lane']},{p['team_warps']},"
                 f"{p['rows_per_tile']},{p['block_threads']}>")
-    return "tp_rmsnorm_generic_kernel<bf16,256>"
+    return f"tp_rmsnorm_generic_kernel<{dt},256>"
+
+
+# --------------------------------------------------------------------------- parity check
+def _np_of(t):
+    """Tensor (any device) -> oracle storage (f32 float32, bf16 uint16 bits, f16 float16)."""
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    return t.numpy().copy()
+
+
+def _gather(t, world):
+    """Every rank's copy of `t` (same shape on every rank), on the CPU, in rank order."""
+    t = t.contiguous()
+    if world == 1:
+        return [t.cpu()]
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.cpu() for p in parts]
+
+
+def parity_check(module, w, world, rank, x, wt, n_sample=128):
+    """Untimed check of real outputs against the oracle of the reference's AllReduce
+    path (oracle/tp_rmsnorm.py; the checker only -- nothing here is timed).
+
+    1. one forward of the benchmark call on set 0: `n_sample` rows (the same on
+       every rank) of every rank's x, y and weight are gathered to rank 0;
+    2. one fused residual add + norm and 3. one backward on a 256-row call whose
+       inputs every rank generates for the whole group from fixed seeds; every
+       rank's outputs are gathered to rank 0 and checked whole.
+    Every rank takes the same collective steps; the verdict is broadcast so that
+    every rank fails together."""
+    from oracle import tp_rmsnorm as O
+
+    wl = load_workloads()
+    dt = DTYPE_NAME[w["dtype"]]
+    tp, eps = world, w["eps"]
+    dev = x.device
+    rows = x.shape[0]
+    checks = {}
+
+    def sync():
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+
+    # 1. the benchmark call, sampled rows
+    y = module.forward(x, wt)
+    sync()
+    idx = np.sort(np.random.default_rng(0).choice(rows, size=min(n_sample, rows), replace=False))
+    ti = torch.from_numpy(idx).to(dev)
+    xs = _gather(x.index_select(0, ti), world)
+    ys = _gather(y.index_select(0, ti), world)
+    wts = _gather(wt, world)
+    if rank == 0:
+        want = O.allreduce_path([_np_of(t) for t in xs], [_np_of(t) for t in wts], eps, dt)
+        res = [O.compare(dt, O.to_f32(dt, _np_of(ys[r])), O.round_to(dt, want[r]))
+               for r in range(tp)]
+        checks["forward"] = {"ok": all(r["ok"] for r in res),
+                             "max_abs": max(r["max_abs"] for r in res),
+                             "rows_checked": len(idx) * tp}
+
+    # 2. fused residual add and 3. backward, 256 rows of the same width
+    small = 256
+    gxs, gws = wl.make_group(small, w["hidden"], tp, w["dtype"], 4242)
+    grs, _ = wl.make_group(small, w["hidden"], tp, w["dtype"], 4343)
+    gdys, _ = wl.make_group(small, w["hidden"], tp, w["dtype"], 4444)
+    # the oracle's copies first: the residual call rewrites its residual in place
+    npx, npw, npr, npdy = ([_np_of(t) for t in ts] for ts in (gxs, gws, grs, gdys))
+    sx, sw, sr, sdy = (t[rank].to(dev).clone() for t in (gxs, gws, grs, gdys))
+    sy = module.forward(sx, sw, residual=sr)
+    dx, dw = module.backward(sdy, sx, sw)
+    sync()
+    ys_r, zs_r = _gather(sy, world), _gather(sr, world)
+    dxs, dws = _gather(dx, world), _gather(dw, world)
+    if rank == 0:
+        want_y, want_z = O.allreduce_path_residual(npx, npr, npw, eps, dt)
+        res = [O.compare(dt, O.to_f32(dt, _np_of(ys_r[r])), O.round_to(dt, want_y[r]))
+               for r in range(tp)]
+        z_ok = all(np.array_equal(np.asarray(want_z[r]), _np_of(zs_r[r])) for r in range(tp))
+        checks["residual"] = {"ok": z_ok and all(r["ok"] for r in res),
+                              "max_abs": max(r["max_abs"] for r in res),
+                              "rows_checked": small * tp, "residual_bit_exact": z_ok}
+        want_dx, want_dw = O.backward_path(npx, npdy, npw, eps, dt)
+        scale = O.dw_magnitude(npx, npdy, eps, dt)
+        rdx = [O.compare_backward(dt, O.to_f32(dt, _np_of(dxs[r])), O.round_to(dt, want_dx[r]))
+               for r in range(tp)]
+        rdw = [O.compare_backward(dt, O.to_f32(dt, _np_of(dws[r])), O.round_to(dt, want_dw[r]),
+                                  scale[r]) for r in range(tp)]
+        checks["backward"] = {"ok": all(r["ok"] for r in rdx + rdw),
+                              "max_abs_dx": max(r["max_abs"] for r in rdx),
+                              "max_abs_dw": max(r["max_abs"] for r in rdw),
+                              "rows_checked": small * tp}
+    status = module.status() if world > 1 else {"code": 0}
+    ok_local = int(status.get("code", 0) == 0)
+    ok = torch.tensor([ok_local if rank != 0 else
+                       ok_local * int(all(c["ok"] for c in checks.values()))],
+                      dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    checks_ok = bool(int(ok.item()))
+    if rank != 0:
+        return {"ok": checks_ok}
+    return {"ok": checks_ok, "oracle": "allreduce path of the reference (oracle/tp_rmsnorm.py)",
+            "tolerance": O.TOLERANCE[dt], "checks": checks,
+            "device_status": "no device failure on any rank" if checks_ok or ok_local else
+                             f"rank 0 device status {status}"}
+
+
+def wait_counters(module, step, world, rank, n_capture=64, steps=256):
+    """In-kernel exchange counters at N > 1 in steady state (a CUDA graph of
+    back-to-back calls replayed with the counters on, untimed): per rank, the share
+    of peer polls that found the partial missing and the mean wait of those polls."""
+    import rmsnorm_tp_b200 as rtp
+
+    c = rtp.profile_counters()
+    module.comm_buf.set_profile(c)
+    try:
+        time_graph(step, n_capture, steps, world)
+    finally:
+        module.comm_buf.set_profile(None)
+    v = c.cpu().tolist()
+    polls = v[1] + v[2]
+    mine = {"slow_poll_share": round(v[1] / max(1, polls), 4),
+            "mean_wait_us": round(v[0] / max(1, v[1]) / 1e3, 3),
+            "polls_per_call": round(polls / (steps if steps >= n_capture else n_capture), 1),
+            "call_span_us": round((v[4] - v[3]) / 1e3 / max(1, steps), 3) if v[4] > v[3] else None}
+    gathered = [None] * world
+    dist.all_gather_object(gathered, mine)
+    if rank != 0:
+        return None
+    return {"per_rank": gathered,
+            "max_slow_poll_share": max(g["slow_poll_share"] for g in gathered),
+            "max_mean_wait_us": max(g["mean_wait_us"] for g in gathered),
+            "how": f"graph of {n_capture} calls replayed for {steps} calls, counters on, untimed"}
 
 
 def run_our_arm(args):
@@ -367,19 +626,14 @@ def run_our_arm(args):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     group = setup_group(world, local)
     dev = torch.device("cuda", local)
-    w = dict(WORKLOAD)
-    if args.rows or args.hidden or args.dtype:
-        w["name"] = "custom"
-        w["rows"] = args.rows or w["rows"]
-        w["hidden"] = args.hidden or w["hidden"]
-        w["dtype"] = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
-                      None: w["dtype"]}[args.dtype]
+    w = workload_of(args)
     tp = world
     hl = w["hidden"] // tp
     rows = w["rows"]
     elem = torch.tensor([], dtype=w["dtype"]).element_size()
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    module = rtp.FusedTPRMSNorm(w["hidden"], eps=w["eps"], tp_group=group, num_max_rows=rows)
+    module = rtp.FusedTPRMSNorm(w["hidden"], eps=w["eps"], tp_group=group,
+                                num_max_rows=max(rows, 256))
     xs, wt, outs = make_rotating_sets(rows, hl, w["dtype"], w["seed_base"] + rank, 3 * l2)
     nsets = len(xs)
     set_bytes = 2 * rows * hl * elem
@@ -395,23 +649,40 @@ def run_our_arm(args):
         module.forward(xs[i % nsets], wt, out=outs[i % nsets])
 
     # ---- timed region: the forward kernel replayed from a CUDA graph (no host
-    # launch cost), K calls over the rotating sets; clocks sampled meanwhile
+    # launch cost), K calls over the rotating sets; clocks sampled around it
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    graph = capture_graph(step, args.steps)
+    if world > 1:
+        dist.barrier()
     if sampler:
         sampler.start()
     # the graph holds exactly K calls and is timed over one replay (after one warm replay)
-    graph_ms, graph_calls = time_graph(step, args.steps, args.steps, world)
+    graph_ms, graph_calls = time_graph(step, args.steps, args.steps, world, g=graph)
+    # untimed replays of the same graph keep the GPUs under this load for ~0.3 s,
+    # so that the 50 ms clock sampler sees the timed region's conditions
+    t_end = time.perf_counter() + 0.3
+    n_extra = 0
+    while time.perf_counter() < t_end:
+        graph.replay()
+        n_extra += 1
+        if n_extra % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
+    if clocks is not None:
+        clocks["window"] = (f"the timed replay plus {n_extra} untimed replays of the same graph "
+                            "(~0.3 s)")
+    del graph
+    if world > 1:
+        dist.barrier()
     bytes_rank = algorithmic_bytes(rows, hl, elem)
     value = tp * bytes_rank / (graph_ms * 1e-3) / 1e9
 
     # ---- the same calls launched one by one from Python (host launch cost included)
-    if world > 1:
-        dist.barrier()
     torch.cuda.synchronize()
     eager_ms = max_over_ranks([time_steps(step, args.steps)], world)[0] / args.steps
     if world > 1:
@@ -437,6 +708,12 @@ def run_our_arm(args):
     e2e_ms = e2e_total / e2e_steps
     e2e_value = tp * bytes_rank / (e2e_ms * 1e-3) / 1e9
 
+    # ---- in-kernel exchange counters (N > 1), untimed
+    counters = wait_counters(module, step, world, rank) if world > 1 else None
+
+    # ---- parity of real outputs (untimed, after the timed region)
+    parity = None if args.no_parity else parity_check(module, w, world, rank, xs[0], wt)
+
     # ---- CPU baseline (rank 0, N = 1): the reference's CPU path on a bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -447,31 +724,34 @@ def run_our_arm(args):
         sec, n = cpu_reference_time(cx, cw, w["eps"], args.cpu_seconds)
         cpu = {"value": round(bytes_rank / sec / 1e9, 3), "unit": "GB/s", "cores": cores,
                "kind": "port", "ms_per_call": round(sec * 1e3, 3),
-               "sample": f"{n} full calls of {rows}x{hl} bf16 (TP=1), torch CPU, {cores} threads"}
+               "sample": f"{n} full calls of {rows}x{hl} {DTYPE_NAME[w['dtype']]} (TP=1), "
+                         f"torch CPU, {cores} threads"}
 
     peak, peak_kind = measured_peak_hbm()
     achieved = bytes_rank / (graph_ms * 1e-3) / 1e9
-    traffic = ncu_traffic(rows, hl, w["dtype"])
+    traffic = TRAFFIC.get((w["name"], tp, DTYPE_NAME[w["dtype"]]))
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": graph_calls, "warmup": args.warmup, "ms_per_step": round(graph_ms, 6),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[w["dtype"]],
-            "data": "synthetic",
-            "config": {"workload": w["name"], "hidden": w["hidden"], "rows": rows, "tp": tp,
-                       "local_hidden": hl, "eps": w["eps"], "parallelism": f"tp{tp}",
-                       "launch": "CUDA graph of forward() calls, one kernel each",
+            "dtype": DTYPE_NAME[w["dtype"]], "data": "synthetic",
+            "config": bench_config(w, tp),
+            "method": {"launch": "CUDA graph of forward() calls, one kernel each",
                        "dependent_launch": rtp.get_dependent_launch(),
-                       "l2": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
-                             f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB L2)"},
+                       "rotation": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
+                                   f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB "
+                                   "L2)"},
             "us_per_call": round(graph_ms * 1e3, 3),
             "eager_us_per_call": round(eager_ms * 1e3, 3),
             "eager_value": round(tp * bytes_rank / (eager_ms * 1e-3) / 1e9, 2),
-            "kernel": plan_name(rtp, rows, hl, tp, w["dtype"]),
+            "kernel": kernel_name(rtp, rows, hl, tp, w["dtype"]),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic[0] if traffic else None,
+                         "traffic_source": traffic[1] if traffic else
+                         "not captured for this workload and N",
                          "peak_kind": peak_kind, "bytes_per_launch": bytes_rank,
                          "per_launch_us": round(graph_ms * 1e3, 3)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
@@ -481,6 +761,8 @@ def run_our_arm(args):
             "cpu_baseline": cpu,
             "gpu_launches": graph_calls,
             "clocks": clocks,
+            "exchange_counters": counters,
+            "parity": parity,
         }
         print(json.dumps(line), flush=True)
 
@@ -491,6 +773,9 @@ def run_our_arm(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        print("parity check FAILED", file=sys.stderr, flush=True)
+        return 1
     return 0
 
 
@@ -626,8 +911,8 @@ class RefNcclImpl:
 
 
 def run_sweeps(args, impl_cls, group, world, rank, dev):
-    from rmsnorm_tp_b200.workloads import BY_NAME, make_slice
-
+    wl = load_workloads()
+    BY_NAME, make_slice = wl.BY_NAME, wl.make_slice
     tp = world
     kinds = ["decode", "prefill", "llama"] if args.sweep == "all" else [args.sweep]
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size

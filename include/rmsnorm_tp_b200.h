@@ -247,11 +247,21 @@ int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp,
  * Each call clears the part it uses on `stream` before its launch; calls that
  * overlap on the GPU share the array and race, so serialise them. The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress)
- * with that device current; make that first call before any stream capture. */
+ * with that device current; make that first call before any stream capture.
+ * A wait that runs out on the device is not returned by the call (it has
+ * returned by then): the affected rows are written as NaN and the failure stays
+ * in the array until the next call clears it; read it with
+ * rmsnorm_tp_forward_group_static_status before that next call. */
 #define RMSNORM_TP_STATIC_SCRATCH_BYTES (4u << 20)
 int rmsnorm_tp_forward_group_static(int tp, void* const* outs, const void* const* xs,
                                     const void* const* weights, int64_t rows,
                                     int64_t local_hidden, int dtype, float eps, void* stream);
+/* No counterpart in the reference. Blocking: waits for the current device, then
+ * reads the failure record the last rmsnorm_tp_forward_group_static call on this
+ * device left in the static array (out->code 0: no failure; otherwise the first
+ * failing rank's record, as rmsnorm_tp_status gives it). Allocates nothing.
+ * RMSNORM_TP_ERR_STATE if no call was made on this device yet. */
+int rmsnorm_tp_forward_group_static_status(rmsnorm_tp_status_info* out);
 
 /* One-hop NVLink latency probe between this rank and `peer`: `iters` round
  * trips of a store into the peer's mailbox and a poll of the local one. Both
@@ -261,13 +271,23 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
                                void* stream, int64_t* dev_out_ns);
 
 /* Kernel family used by every later launch of this process:
- * 0 = automatic (bulk-copy kernels for calls with >= 48 MiB of x per rank
- * with an exchange, >= 256 MiB at TP = 1; register kernels below),
- * 1 = register kernels only, 2 = bulk-copy kernels
- * wherever eligible (aligned rows of <= 16 KB). For tests and benchmarks that
- * compare the two implementations. */
+ * 0 = automatic (with an exchange: the batch kernels for aligned rows of
+ * <= 16 KB; at TP = 1: the local register kernels, bulk-copy kernels from
+ * 256 MiB of x), 1 = register kernels only, 2 = bulk-copy kernels wherever
+ * eligible (aligned rows of <= 16 KB), 3 = batch kernels wherever eligible
+ * (aligned rows of <= 16 KB, TP = 1 included). For tests and benchmarks that
+ * compare the implementations. */
 int rmsnorm_tp_set_kernel_family(int family);
 int rmsnorm_tp_get_kernel_family(void);
+
+/* Encoding of the exchange for every later launch of this process:
+ * 0 = {tag, fp32 partial} in one 64-bit system-scope store per slot (default);
+ * 1 = the partial, then the tag with a separate release store, read with an
+ * acquire of the tag -- the reference's value + flag scheme
+ * (csrc/rmsnorm_tp.cu:102-115, :121-138), kept for measured comparison.
+ * Every rank of a group must use the same encoding. */
+int rmsnorm_tp_set_push_mode(int mode);
+int rmsnorm_tp_get_push_mode(void);
 
 /* Programmatic dependent launch for every later forward launch of this process
  * (1 = on, the default; 0 = off). When on, a forward kernel is launched with
@@ -284,8 +304,10 @@ int rmsnorm_tp_get_dependent_launch(void);
 
 /* The launch plan the forward call would use (pure host arithmetic; no GPU).
  * variant: -1 generic, 0..6 register kernels (TP > 1), 100..111 bulk-copy
- * kernels, >= 200 register kernels without an exchange (TP = 1)
- * (vec_per_lane then = stages per warp, rows_per_tile = rows per stage). */
+ * kernels (vec_per_lane then = stages per warp, rows_per_tile = rows per
+ * stage), 200..213 register kernels without an exchange (TP = 1), 500..501
+ * batch kernels (vec_per_lane = depth = ring slots, rows_per_tile = rows per
+ * batch, team_warps = warps per CTA). */
 int rmsnorm_tp_plan(int64_t rows, int64_t local_hidden, int dtype, int aligned, int tp,
                     int resident_ctas, rmsnorm_tp_plan_info* out);
 
@@ -302,7 +324,9 @@ uint32_t rmsnorm_tp_buffer_of(uint64_t generation);
 const char* rmsnorm_tp_last_error(void);
 
 /* ABI version (major * 100 + minor). 1.01 added the residual, backward and
- * dependent-launch entry points and named the plan's last field `depth`. */
+ * dependent-launch entry points and named the plan's last field `depth`; 1.02
+ * added rmsnorm_tp_forward_group_static_status, the batch kernel family
+ * (rmsnorm_tp_set_kernel_family(3)) and the push encodings. */
 int rmsnorm_tp_abi_version(void);
 
 #ifdef __cplusplus

@@ -28,9 +28,13 @@ OUT = os.path.join(HERE, "_ref")
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("RMSNORM_TP_REFERENCE"),
+                    help="checkout of the reference (default: $RMSNORM_TP_REFERENCE)")
     ap.add_argument("--nvcc", default="nvcc")
     args = ap.parse_args(argv)
+    if not args.reference:
+        print("no reference checkout given (--reference or RMSNORM_TP_REFERENCE); nothing to build")
+        return 0
     csrc = os.path.join(args.reference, "csrc")
     if not os.path.isdir(csrc):
         print(f"no reference checkout at {args.reference}; nothing to build")

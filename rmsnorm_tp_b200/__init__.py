@@ -22,6 +22,8 @@ from .api import (
     profile_counters,
     set_kernel_family,
     get_kernel_family,
+    set_push_mode,
+    get_push_mode,
     set_dependent_launch,
     get_dependent_launch,
     tag_of,
@@ -43,6 +45,8 @@ __all__ = [
     "tag_of",
     "set_kernel_family",
     "get_kernel_family",
+    "set_push_mode",
+    "get_push_mode",
     "set_dependent_launch",
     "get_dependent_launch",
     "buffer_of",

@@ -20,7 +20,9 @@ OK, ERR_INVALID, ERR_CUDA, ERR_STATE, ERR_ROWS, ERR_DEVICE, ERR_HANDLE = range(7
 # enum rmsnorm_tp_device_status
 STATUS_OK, STATUS_TIMEOUT, STATUS_ABORTED, STATUS_LOAD_TIMEOUT = 0, 1, 2, 3
 # kernel families (rmsnorm_tp_set_kernel_family)
-FAMILY_AUTO, FAMILY_REGISTER, FAMILY_BULK = 0, 1, 2
+FAMILY_AUTO, FAMILY_REGISTER, FAMILY_BULK, FAMILY_BATCH = 0, 1, 2, 3
+# push encodings (rmsnorm_tp_set_push_mode)
+PUSH_PACKED, PUSH_RELEASE = 0, 1
 
 MAX_TP = 8
 HANDLE_BYTES = 128
@@ -136,10 +138,13 @@ SIGNATURES = {
             _i64, _i64, _i32, ctypes.c_float, _c_void_p,
         ],
     ),
+    "rmsnorm_tp_forward_group_static_status": (_i32, [ctypes.POINTER(StatusInfo)]),
     "rmsnorm_tp_probe_roundtrip": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p]),
     "rmsnorm_tp_plan": (_i32, [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(PlanInfo)]),
     "rmsnorm_tp_set_kernel_family": (_i32, [_i32]),
     "rmsnorm_tp_get_kernel_family": (_i32, []),
+    "rmsnorm_tp_set_push_mode": (_i32, [_i32]),
+    "rmsnorm_tp_get_push_mode": (_i32, []),
     "rmsnorm_tp_set_dependent_launch": (_i32, [_i32]),
     "rmsnorm_tp_get_dependent_launch": (_i32, []),
     "rmsnorm_tp_plan_coverage": (_i32, [ctypes.POINTER(PlanInfo), _i64, ctypes.POINTER(ctypes.c_int32)]),

@@ -593,14 +593,31 @@ def plan_coverage(plan_dict: dict, rows: int):
     return list(counts)[:rows]
 
 
+_FAMILIES = {"auto": _lib.FAMILY_AUTO, "register": _lib.FAMILY_REGISTER, "bulk": _lib.FAMILY_BULK,
+             "batch": _lib.FAMILY_BATCH}
+
+
 def set_kernel_family(family: str) -> None:
-    """Process-wide kernel family: "auto", "register" or "bulk" (tests, benchmarks)."""
-    code = {"auto": _lib.FAMILY_AUTO, "register": _lib.FAMILY_REGISTER, "bulk": _lib.FAMILY_BULK}[family]
-    check(LIB.rmsnorm_tp_set_kernel_family(code), "rmsnorm_tp_set_kernel_family")
+    """Process-wide kernel family: "auto", "register", "bulk" or "batch" (tests, benchmarks)."""
+    check(LIB.rmsnorm_tp_set_kernel_family(_FAMILIES[family]), "rmsnorm_tp_set_kernel_family")
 
 
 def get_kernel_family() -> str:
-    return {0: "auto", 1: "register", 2: "bulk"}[LIB.rmsnorm_tp_get_kernel_family()]
+    return {v: k for k, v in _FAMILIES.items()}[LIB.rmsnorm_tp_get_kernel_family()]
+
+
+_PUSH_MODES = {"packed": _lib.PUSH_PACKED, "release": _lib.PUSH_RELEASE}
+
+
+def set_push_mode(mode: str) -> None:
+    """Process-wide exchange encoding: "packed" (one 64-bit {tag, partial} store, the
+    default) or "release" (the partial, then a release-stored tag: the reference's
+    scheme, for comparison). Every rank of a group must use the same one."""
+    check(LIB.rmsnorm_tp_set_push_mode(_PUSH_MODES[mode]), "rmsnorm_tp_set_push_mode")
+
+
+def get_push_mode() -> str:
+    return {v: k for k, v in _PUSH_MODES.items()}[LIB.rmsnorm_tp_get_push_mode()]
 
 
 def set_dependent_launch(enable: bool) -> None:

@@ -252,6 +252,7 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   if (grid < 1) return cudaErrorCooperativeLaunchTooLarge;
   if (grid_out) *grid_out = (int)grid;
   BArgs bb = b;
+  bb.k.push_mode = get_push_mode();
   void* args[] = {&bb};
   const dim3 g3((unsigned)grid, (unsigned)grid_y), blk(kBwdBlock);
   if (grid_y > 1) return cudaLaunchCooperativeKernel(fp, g3, blk, args, smem, stream);

@@ -150,7 +150,7 @@ extern "C" {
 
 const char* rmsnorm_tp_last_error(void) { return g_last_error.c_str(); }
 
-int rmsnorm_tp_abi_version(void) { return 101; }
+int rmsnorm_tp_abi_version(void) { return 102; }
 
 uint32_t rmsnorm_tp_tag_of(uint64_t generation) { return rtp::tag_of(generation); }
 uint32_t rmsnorm_tp_buffer_of(uint64_t generation) { return rtp::buffer_of(generation); }
@@ -763,13 +763,22 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* c, int peer, int iters, void* st
 }
 
 int rmsnorm_tp_set_kernel_family(int family) {
-  if (family < rtp::kFamilyAuto || family > rtp::kFamilyBulk)
+  if (family < rtp::kFamilyAuto || family > rtp::kFamilyBatch)
     return fail(RMSNORM_TP_ERR_INVALID, "set_kernel_family: unknown family %d", family);
   rtp::set_family(family);
   return RMSNORM_TP_OK;
 }
 
 int rmsnorm_tp_get_kernel_family(void) { return rtp::get_family(); }
+
+int rmsnorm_tp_set_push_mode(int mode) {
+  if (mode != rtp::kPushPacked && mode != rtp::kPushRelease)
+    return fail(RMSNORM_TP_ERR_INVALID, "set_push_mode: expected 0 or 1, got %d", mode);
+  rtp::set_push_mode(mode);
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_get_push_mode(void) { return rtp::get_push_mode(); }
 
 int rmsnorm_tp_set_dependent_launch(int enable) {
   if (enable != 0 && enable != 1)
@@ -806,6 +815,18 @@ int rmsnorm_tp_plan_coverage(const rmsnorm_tp_plan_info* p, int64_t rows, int32_
   if (p->grid < 1 || p->teams_per_cta < 1 || p->rows_per_tile < 1)
     return fail(RMSNORM_TP_ERR_INVALID, "plan_coverage: malformed plan");
   for (int64_t i = 0; i < rows; ++i) counts[i] = 0;
+  if (p->variant >= rtp::kBatchBase) {
+    // Batch kernels: CTA c owns batches [B c / G, B (c + 1) / G) of rows_per_tile rows.
+    const int64_t B = (rows + p->rows_per_tile - 1) / p->rows_per_tile;
+    const int64_t G = p->grid;
+    for (int64_t c = 0; c < G; ++c)
+      for (int64_t b = B * c / G; b < B * (c + 1) / G; ++b)
+        for (int r = 0; r < p->rows_per_tile; ++r) {
+          const int64_t row = b * p->rows_per_tile + r;
+          if (row < rows) counts[row] += 1;
+        }
+    return RMSNORM_TP_OK;
+  }
   // Same walk as the kernels: team g visits tiles g, g + T, g + 2T, ... (T = all teams).
   const int64_t teams_total = (int64_t)p->grid * p->teams_per_cta;
   const int64_t tiles = (rows + p->rows_per_tile - 1) / p->rows_per_tile;

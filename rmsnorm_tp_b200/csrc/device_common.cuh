@@ -152,11 +152,42 @@ struct WaitStats {          // optional per-lane counters (KArgs::prof)
   unsigned int fast = 0;    // waits satisfied by the first poll
 };
 
+// Stores {mine, tag} into a slot: one 64-bit system-scope store (packed encoding,
+// the default), or the value and then the tag with a release store (the
+// reference's flag scheme, KArgs::push_mode == kPushRelease).
+__device__ __forceinline__ void store_slot(const KArgs& a, unsigned long long* dst, float mine,
+                                           uint32_t tag) {
+  if (a.push_mode == kPushRelease) {
+    unsigned int* w = reinterpret_cast<unsigned int*>(dst);   // [0] value, [1] tag
+    ptx::st_relaxed_sys_u32(w, f32_bits(mine));
+    ptx::st_release_sys_u32(w + 1, tag);
+  } else {
+    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
+  }
+}
+
+// One look at a local slot: true if it carries `tag`; *word gets {tag seen, value}.
+__device__ __forceinline__ bool probe_slot(const KArgs& a, const unsigned long long* src,
+                                           uint32_t tag, unsigned long long* word) {
+  if (a.push_mode == kPushRelease) {
+    const unsigned int* w = reinterpret_cast<const unsigned int*>(src);
+    const unsigned int t = ptx::ld_acquire_sys_u32(w + 1);
+    if (t != tag) {
+      *word = (unsigned long long)t << 32;
+      return false;
+    }
+    *word = ((unsigned long long)t << 32) | ptx::ld_relaxed_sys_u32(w);
+    return true;
+  }
+  *word = ptx::ld_relaxed_sys_u64(src);
+  return slot_tag(*word) == tag;
+}
+
 __device__ __forceinline__ void push_slot(const KArgs& a, int rank, uint32_t buf, uint32_t tag,
                                           int64_t row, int q, bool active, float mine) {
   if (active && q != rank) {
     unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, a.tp, a.nmax, row);
-    ptx::st_relaxed_sys_u64(dst, pack_slot(mine, tag));
+    store_slot(a, dst, mine, tag);
   }
 }
 
@@ -167,8 +198,8 @@ __device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankP
   failed = false;
   if (!active || q == rank) return mine;
   const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, a.tp, a.nmax, row);
-  unsigned long long w = ptx::ld_relaxed_sys_u64(src);
-  if (slot_tag(w) == tag) {
+  unsigned long long w = 0ull;
+  if (probe_slot(a, src, tag, &w)) {
     ws.fast += 1;
     return slot_value(w);
   }
@@ -176,8 +207,7 @@ __device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankP
   const unsigned long long t0 = ptx::globaltimer();
   unsigned long long now = t0;
   for (;;) {
-    w = ptx::ld_relaxed_sys_u64(src);
-    if (slot_tag(w) == tag) break;
+    if (probe_slot(a, src, tag, &w)) break;
     if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
       fail = kStatusAborted;
       break;

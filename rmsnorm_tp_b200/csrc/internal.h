@@ -40,12 +40,22 @@ struct KArgs {
                                        // normalise them one after another (else interleaved)
   unsigned long long timeout_ns;
   unsigned long long* prof;            // optional wait/timing counters (5 x u64), or null
+  int push_mode;                       // kPushPacked (default) or kPushRelease
+  int depth;                           // batch kernels: shared-memory ring slots
 };
+
+// Push encodings of the exchange (process-wide, rmsnorm_tp_set_push_mode):
+// kPushPacked: {tag, fp32 partial} in one 64-bit relaxed system-scope store;
+// kPushRelease: the value, then the tag with a release store, read back with an
+// acquire of the tag (the reference's scheme), for measured comparison.
+enum PushMode { kPushPacked = 0, kPushRelease = 1 };
+void set_push_mode(int mode);
+int get_push_mode();
 
 enum Dtype { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
 // Kernel family selection (process-wide): automatic, or one family forced.
-enum Family { kFamilyAuto = 0, kFamilyRegister = 1, kFamilyBulk = 2 };
+enum Family { kFamilyAuto = 0, kFamilyRegister = 1, kFamilyBulk = 2, kFamilyBatch = 3 };
 void set_family(int family);
 int get_family();
 
@@ -74,14 +84,16 @@ constexpr int kLocalBase = 200;   // TP = 1 register kernels: base + shape * dep
 constexpr int kLocalResBase = 300;
 constexpr int kBulkResBase = 400;
 constexpr int kGenericRes = -2;
+constexpr int kBatchBase = 500;   // batch kernels: base + index of the warp count
 
 int elem_bytes(int dtype);
 
 // Records `msg` as the calling thread's last error (rmsnorm_tp_last_error) and
 // returns `code`.
 int record_error(int code, const char* msg);
+// `sms`: SM count of the device (sizes the batch kernels' batches).
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp = 1, int64_t rows = 0,
-                           int family = kFamilyAuto, bool residual = false);
+                           int family = kFamilyAuto, bool residual = false, int sms = 148);
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas);
 
 // Launch the forward kernel. grid_y > 1 only for the emulated (all ranks on one

@@ -65,9 +65,10 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   const int rank = a.emulated ? (int)blockIdx.y : a.rank;
   const RankPtrs& rp = a.rp[ri];
   const int64_t V = a.hl / Pack<T>::kE;
-  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  // x and out may be the same memory (in place): no __restrict__ on either
+  const uint4* xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
   const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
-  uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
+  uint4* yg = reinterpret_cast<uint4*>(rp.out);
   const bool exchange = a.tp > 1;
   const int tp = a.tp;
   const int lr = exchange ? lane / tp : 0;      // exchange lane -> (row, rank)
@@ -262,10 +263,12 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   const int wit = warp - team * kW;
   const RankPtrs& rp = a.rp[0];
   const int64_t V = a.hl / Pack<T>::kE;
-  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  // x and out may be the same memory (in place), and the residual is read and
+  // rewritten: no __restrict__ on any of them
+  const uint4* xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
   const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
-  uint4* __restrict__ yg = reinterpret_cast<uint4*>(rp.out);
-  uint4* __restrict__ rg = kRes ? ptx::launder(reinterpret_cast<uint4*>(rp.res)) : nullptr;
+  uint4* yg = reinterpret_cast<uint4*>(rp.out);
+  uint4* rg = kRes ? ptx::launder(reinterpret_cast<uint4*>(rp.res)) : nullptr;
 
   // two slots: a warp rewrites slot s only after the next team barrier, which
   // every warp of the team reaches after reading slot s
@@ -388,9 +391,9 @@ __global__ void __launch_bounds__(kBlock)
   const int ri = a.emulated ? (int)blockIdx.y : 0;
   const int rank = a.emulated ? (int)blockIdx.y : a.rank;
   const RankPtrs& rp = a.rp[ri];
-  const T* __restrict__ xg = reinterpret_cast<const T*>(rp.x);
+  const T* xg = reinterpret_cast<const T*>(rp.x);    // may be out (in place)
   const T* __restrict__ wg = reinterpret_cast<const T*>(rp.w);
-  T* __restrict__ yg = reinterpret_cast<T*>(rp.out);
+  T* yg = reinterpret_cast<T*>(rp.out);
   T* rg = reinterpret_cast<T*>(rp.res);   // kRes: residual, rewritten with z = x + r
   const bool exchange = a.tp > 1;
   const int64_t hl = a.hl;
@@ -739,6 +742,220 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Batch kernel (TP > 1 default for aligned rows of up to 16 KB).
+//
+// Every CTA owns one contiguous block of rows, split into batches of
+// tile_rows (<= 32) consecutive rows. A batch is one contiguous span of x,
+// fetched by one cp.async.bulk into a ring of `depth` shared-memory slots; a
+// CTA whose block fits its ring has every byte of it in flight from the start.
+// Per batch, all warps:
+//   reduce  -- the sum of squares of each row (one or several warps per row),
+//   push    -- warp q writes the batch's partials into peer q's mailbox: lane j
+//              stores row j's {partial, tag}, so one store instruction moves
+//              the whole batch to that peer as one contiguous write of
+//              tile_rows x 8 bytes (one NVLink write per peer and batch, instead
+//              of one per peer and row),
+// and `lag` batches later
+//   poll    -- warp q reads rank q's slots of that batch from the local mailbox
+//              (lanes = rows, one contiguous load per peer), bounded waits,
+//   finish  -- S = s_0 + ... + s_{tp-1} in rank order, y = (x * rsqrt(S / H +
+//              eps)) * w from shared memory, 128-bit stores; the slot is refilled.
+// The lag lets each batch's NVLink round trip and the ranks' skew overlap the
+// reduction of the next batches while the ring keeps HBM busy. Every rank maps
+// rows to CTAs and batches the same way, pushes batch b before it polls batch
+// b - lag (lag >= 1), and every CTA is resident (one wave), so every wait is
+// for a push that precedes the waiter's own earlier-batch waits on the peer:
+// the waits always end.
+// ---------------------------------------------------------------------------
+constexpr int kBatchMaxRows = 32;
+constexpr int kBatchMaxSlots = 8;
+
+template <typename T, int kWarps>
+__global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
+    tp_rmsnorm_batch_kernel(const __grid_constant__ KArgs a) {
+  static_assert(kWarps >= kMaxTP, "one warp per rank in the exchange");
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) unsigned long long s_bar[kBatchMaxSlots];
+  __shared__ float s_red[kBatchMaxRows][kWarps];         // per (row, warp part) sums
+  __shared__ float s_part[kBatchMaxSlots][kBatchMaxRows];  // this rank's partials, by slot
+  __shared__ float s_val[kMaxTP][kBatchMaxRows];           // every rank's partials of the batch
+  __shared__ unsigned long long s_call;                    //   being finished
+  __shared__ int s_fail;
+
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  WaitStats ws;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const bool exchange = a.tp > 1;
+  const int tp = a.tp;
+  const int V = (int)(a.hl / Pack<T>::kE);                   // 16-byte vectors per row
+  const uint32_t row_bytes = (uint32_t)a.hl * (uint32_t)sizeof(T);
+  const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
+  const int bR = a.tile_rows;
+  const int nslots = a.depth;
+  const uint32_t slot_bytes = a.stage_bytes;
+  // warps per row (g, a power of two) and the rows one pass of the CTA covers
+  const int g = bR >= kWarps ? 1 : kWarps / bR;
+  const int rows_per_pass = kWarps / g;
+  const int wrow = warp / g, wpart = warp - wrow * g;
+
+  const int64_t batches = (a.rows + bR - 1) / bR;
+  const int64_t b_lo = batches * (int64_t)blockIdx.x / (int64_t)gridDim.x;
+  const int64_t b_hi = batches * ((int64_t)blockIdx.x + 1) / (int64_t)gridDim.x;
+  const int64_t nb = b_hi - b_lo;
+  // lag: batches pushed but not finished; with refills it leaves copies issued
+  // at least two batches ahead of use
+  int lag = a.lag < 1 ? 1 : a.lag;
+  if (nb > nslots && lag > nslots - 3) lag = nslots - 3 < 1 ? 1 : nslots - 3;
+
+  const unsigned char* xg = reinterpret_cast<const unsigned char*>(rp.x);
+  uint4* yg = reinterpret_cast<uint4*>(rp.out);
+  unsigned char* ring = smem + w_bytes;
+  const uint32_t ring_addr = ptx::smem_addr(ring);
+  const uint32_t bar0 = ptx::smem_addr(&s_bar[0]);
+  auto row0_of = [&](int64_t kk) { return (b_lo + kk) * bR; };
+  auto nrows_of = [&](int64_t kk) { return (int)min((int64_t)bR, a.rows - row0_of(kk)); };
+  auto issue = [&](int64_t kk) {   // thread 0: batch kk -> slot kk % nslots
+    const int st = (int)(kk % nslots);
+    const uint32_t bytes = (uint32_t)nrows_of(kk) * row_bytes;
+    const uint32_t bar = bar0 + 8u * (uint32_t)st;
+    ptx::mbar_arrive_expect_tx(bar, bytes);
+    ptx::bulk_load(ring_addr + (uint32_t)st * slot_bytes, xg + row0_of(kk) * (int64_t)row_bytes,
+                   bytes, bar);
+  };
+  int64_t issued = 0;   // thread 0 only
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < nslots; ++st) ptx::mbar_init(bar0 + 8u * st, 1u);
+    ptx::fence_mbar_init();
+    issued = nb < nslots ? nb : nslots;
+    for (int64_t kk = 0; kk < issued; ++kk) issue(kk);
+    if (exchange) s_call = read_generation(rp.state);
+  }
+  // weight row -> shared memory while the first batches are in flight
+  const uint4* wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  uint4* wsm = reinterpret_cast<uint4*>(smem);
+  for (int v = threadIdx.x; v < V; v += kWarps * 32) wsm[v] = ptx::ld_cached_v4(wg + v);
+  __syncthreads();
+  unsigned long long call = 0ull;
+  uint32_t buf = 0u, tag = 0u;
+  if (exchange) {
+    call = s_call;
+    buf = buffer_of(call);
+    tag = tag_of(call);
+  }
+  auto slot_ptr = [&](int64_t kk) {
+    return reinterpret_cast<const uint4*>(ring + (size_t)(kk % nslots) * slot_bytes);
+  };
+
+  bool load_ok = true;
+  int64_t b = 0;
+  for (; b < nb + lag; ++b) {
+    // A: batch b has landed (every thread observes its barrier, bounded), and the
+    // previous iteration's reads of the slot finished there are complete
+    bool ok = true;
+    if (b < nb)
+      ok = mbar_wait_bounded(bar0 + 8u * (uint32_t)(b % nslots), (uint32_t)((b / nslots) & 1),
+                             kLoadTimeoutNs);
+    if (!__syncthreads_and(ok)) {
+      load_ok = false;
+      break;
+    }
+    const int64_t f = b - lag;   // batch finished in this iteration
+    if (threadIdx.x == 0) {
+      // every thread has finished batch f - 1 (read its slot and s_fail) before A;
+      // this iteration's polls set s_fail only after barrier B
+      s_fail = 0;
+      if (f >= 1 && f - 1 + nslots < nb) {
+        ptx::fence_proxy_async_smem();   // the reads of slot (f - 1) before its refill
+        issue(f - 1 + nslots);
+        issued = f + nslots;
+      }
+    }
+    int nr = 0;
+    if (b < nb) {   // reduce
+      nr = nrows_of(b);
+      const uint4* xs = slot_ptr(b);
+      for (int r = wrow; r < nr; r += rows_per_pass) {
+        const uint4* xr = xs + r * V;
+        float a0 = 0.f, a1 = 0.f;
+        int v = wpart * 32 + lane;
+        for (; v + g * 32 < V; v += 2 * g * 32) {
+          a0 += sumsq16<T>(xr[v]);
+          a1 += sumsq16<T>(xr[v + g * 32]);
+        }
+        if (v < V) a0 += sumsq16<T>(xr[v]);
+        const float s = warp_allreduce_sum(a0 + a1);
+        if (lane == 0) s_red[r][wpart] = s;
+      }
+    }
+    __syncthreads();   // B
+    if (b < nb && warp < tp && lane < nr) {   // push batch b: warp q -> rank q
+      float part = 0.f;
+      for (int k = 0; k < g; ++k) part += s_red[lane][k];
+      if (warp == rank) {
+        s_part[b % nslots][lane] = part;
+      } else {
+        unsigned long long* dst =
+            a.mbox[warp] + slot_index(buf, rank, tp, a.nmax, row0_of(b) + lane);
+        store_slot(a, dst, part, tag);
+      }
+    }
+    if (f >= 0 && warp < tp) {   // poll batch f: warp q <- rank q (lanes = rows)
+      const int nrf = nrows_of(f);
+      const bool active = lane < nrf;
+      bool failed = false;
+      const float mine = active && warp == rank ? s_part[f % nslots][lane] : 0.f;
+      const float val = poll_slot(a, rank, rp, buf, tag, call, row0_of(f) + lane, warp, active,
+                                  mine, failed, ws);
+      if (active) s_val[warp][lane] = val;
+      if (failed) s_fail = 1;
+    }
+    __syncthreads();   // C
+    if (f >= 0) {      // finish batch f
+      const int nrf = nrows_of(f);
+      const uint4* xs = slot_ptr(f);
+      const bool bad = s_fail != 0;
+      for (int r = wrow; r < nrf; r += rows_per_pass) {
+        float S = 0.f;
+        for (int q = 0; q < tp; ++q) S += s_val[q][r];
+        const float inv = bad ? quiet_nan() : rsqrtf(S / a.hidden_f + a.eps);
+        const uint4* xr = xs + r * V;
+        uint4* yr = yg + (row0_of(f) + r) * (int64_t)V;
+#pragma unroll 2
+        for (int v = wpart * 32 + lane; v < V; v += g * 32)
+          ptx::st_v4(yr + v, normalize16<T>(xr[v], wsm[v], inv));
+      }
+    }
+  }
+  if (!load_ok) {
+    // A copy never landed: record it, then wait (bounded) for the copies still in
+    // flight so none lands in shared memory this CTA no longer owns.
+    if (threadIdx.x == 0) {
+      if (rp.state != nullptr) {
+        if (atomicCAS(&rp.state->err_code, 0u, (unsigned)kStatusLoadTimeout) == 0u) {
+          rp.state->err_call = call;
+          if (rp.host_flag != nullptr) {
+            *reinterpret_cast<volatile unsigned int*>(rp.host_flag) = (unsigned)kStatusLoadTimeout;
+            __threadfence_system();
+          }
+        }
+        atomicExch(&rp.state->abort, 1u);
+      }
+      for (int64_t kk = b; kk < issued; ++kk)
+        mbar_wait_bounded(bar0 + 8u * (uint32_t)(kk % nslots), (uint32_t)((kk / nslots) & 1),
+                          kLoadTimeoutNs);
+    }
+  }
+  if (exchange) finish_launch(rp.state, call);
+  flush_stats(a, ws, t_start);
+}
+
+// ---------------------------------------------------------------------------
 // One-hop latency probe: a single thread bounces a counter between two GPUs.
 // ---------------------------------------------------------------------------
 __global__ void probe_roundtrip_kernel(unsigned long long* remote_slot,
@@ -819,12 +1036,23 @@ constexpr int kLocalResDepth = 2;
 // fused residual add, bulk kernels: 4 warps x 3 stages, stage = x tile + residual tile
 constexpr int kBulkResWarps = 4, kBulkResStages = 3;
 constexpr uint32_t kBulkResMaxRowBytes = 8192;
+// Batch kernels: 8 warps with 2 CTAs per SM (dynamic shared memory of a CTA at
+// most kBatchSmem2), or 16 warps with 1 CTA per SM (at most kBatchSmem1).
+constexpr int kBatchWarps[] = {8, 16};
+constexpr int kNumBatch = sizeof(kBatchWarps) / sizeof(kBatchWarps[0]);
+constexpr uint32_t kBatchSmem2 = 100u * 1024u;
+constexpr uint32_t kBatchSmem1 = 200u * 1024u;
+constexpr uint32_t kBatchMaxRowBytes = 16384;
+constexpr uint32_t kBatchBytes = 16384;      // target bytes of x per batch
+constexpr uint32_t kBatchMinBytes = 4096;    // smaller batches only to give every CTA work
+constexpr int kBatchLag = 2;
 // occupancy-cache slots: register, generic, bulk, local, then the residual
-// kernels: local, bulk, generic
+// kernels: local, bulk, generic; then the batch kernels
 constexpr int kSlotLocalRes = kNumShapes + 1 + kNumBulk + kNumLocal;
 constexpr int kSlotBulkRes = kSlotLocalRes + kNumShapes;
 constexpr int kSlotGenericRes = kSlotBulkRes + kNumRowBounds;
-constexpr int kSlots = kSlotGenericRes + 1;
+constexpr int kSlotBatch = kSlotGenericRes + 1;
+constexpr int kSlots = kSlotBatch + kNumBatch;
 
 using KernelFn = void (*)(const KArgs);
 
@@ -867,9 +1095,12 @@ struct KernelTable {
   };
   static constexpr KernelFn generic = tp_rmsnorm_generic_kernel<T, kGenericBlock>;
   static constexpr KernelFn generic_res = tp_rmsnorm_generic_kernel<T, kGenericBlock, true>;
+  static constexpr KernelFn batch[kNumBatch] = {tp_rmsnorm_batch_kernel<T, 8>,
+                                                tp_rmsnorm_batch_kernel<T, 16>};
   static KernelFn get(int variant) {
     if (variant == kGenericRes) return generic_res;
     if (variant < 0) return generic;
+    if (variant >= kBatchBase) return batch[variant - kBatchBase];
     if (variant >= kBulkResBase) return bulk_res[variant - kBulkResBase];
     if (variant >= kLocalResBase) return local_res[variant - kLocalResBase];
     if (variant >= kLocalBase) return local[variant - kLocalBase];
@@ -891,6 +1122,7 @@ KernelFn kernel_for(int dtype, int variant) {
 
 int slot_of(int variant) {
   if (variant == kGenericRes) return kSlotGenericRes;
+  if (variant >= kBatchBase) return kSlotBatch + (variant - kBatchBase);
   if (variant < 0) return kNumShapes;
   if (variant >= kBulkResBase) return kSlotBulkRes + (variant - kBulkResBase);
   if (variant >= kLocalResBase) return kSlotLocalRes + (variant - kLocalResBase);
@@ -901,6 +1133,7 @@ int slot_of(int variant) {
 
 std::atomic<int> g_family{kFamilyAuto};
 std::atomic<bool> g_dependent_launch{true};
+std::atomic<int> g_push_mode{kPushPacked};
 
 constexpr int kMaxDevices = 64;
 // Per device/dtype/variant: (dynamic smem bytes << 32) | resident CTAs of the
@@ -908,6 +1141,22 @@ constexpr int kMaxDevices = 64;
 // shared memory raised once (bit 31 of g_attr_set).
 std::atomic<unsigned long long> g_resident[kMaxDevices][3][kSlots];
 std::atomic<unsigned int> g_attr_set[kMaxDevices][3][kSlots];
+
+std::atomic<int> g_sms[kMaxDevices];
+
+int sm_count(int device, cudaError_t* err) {
+  *err = cudaSuccess;
+  const bool cacheable = device >= 0 && device < kMaxDevices;
+  if (cacheable) {
+    const int c = g_sms[device].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int sms = 0;
+  *err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (*err != cudaSuccess) return 0;
+  if (cacheable) g_sms[device].store(sms, std::memory_order_relaxed);
+  return sms;
+}
 
 int resident_ctas(int device, int dtype, const VariantDesc& v, cudaError_t* err) {
   *err = cudaSuccess;
@@ -943,6 +1192,8 @@ void set_family(int family) { g_family.store(family); }
 int get_family() { return g_family.load(); }
 void set_dependent_launch(bool enable) { g_dependent_launch.store(enable); }
 bool get_dependent_launch() { return g_dependent_launch.load(); }
+void set_push_mode(int mode) { g_push_mode.store(mode); }
+int get_push_mode() { return g_push_mode.load(); }
 
 int elem_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
 
@@ -954,7 +1205,26 @@ struct Tuning {
   long stage_bytes = -1;
   int schedule = -1;
   int local_depth = -1;   // index into kLocalDepths
+  // batch kernels: RMSNORM_TP_BATCH_BYTES (target bytes per batch, 1024..65536),
+  // RMSNORM_TP_BATCH_MIN_BYTES (1024..65536), RMSNORM_TP_BATCH_LAG (1..6),
+  // RMSNORM_TP_BATCH_CTAS (CTAs per SM: 1 or 2), RMSNORM_TP_BATCH_SLOTS (3..8)
+  long batch_bytes = -1, batch_min_bytes = -1;
+  int batch_lag = -1, batch_ctas = -1, batch_slots = -1;
   Tuning() {
+    auto env_long = [](const char* name, long lo, long hi, long& out) {
+      if (const char* env = std::getenv(name)) {
+        const long v = std::atol(env);
+        if (v >= lo && v <= hi) out = v;
+      }
+    };
+    long v = -1;
+    env_long("RMSNORM_TP_BATCH_BYTES", 1024, 65536, batch_bytes);
+    env_long("RMSNORM_TP_BATCH_MIN_BYTES", 1024, 65536, batch_min_bytes);
+    if (env_long("RMSNORM_TP_BATCH_LAG", 1, 6, v), v > 0) batch_lag = (int)v;
+    v = -1;
+    if (env_long("RMSNORM_TP_BATCH_CTAS", 1, 2, v), v > 0) batch_ctas = (int)v;
+    v = -1;
+    if (env_long("RMSNORM_TP_BATCH_SLOTS", 3, kBatchMaxSlots, v), v > 0) batch_slots = (int)v;
     if (const char* env = std::getenv("RMSNORM_TP_BULK_STAGE_BYTES")) {
       const long v = std::atol(env);
       if (v >= 1024 && v <= 16384) stage_bytes = v;
@@ -1027,12 +1297,52 @@ VariantDesc choose_residual_variant(int64_t hl, int dtype, bool vec_ok, int tp, 
 }
 }  // namespace
 
+namespace {
+// Batch kernel shape for rows of row_bytes (<= kBatchMaxRowBytes): rows per
+// batch, ring slots, lag. Batches of ~kBatchBytes of x, made smaller (down to
+// kBatchMinBytes) while the call has fewer than two batches per CTA, so that
+// small calls still spread over the chip and pipeline within a CTA.
+VariantDesc batch_variant(uint32_t row_bytes, int64_t rows, int sms) {
+  const Tuning& t = tuning();
+  const int ctas_per_sm = t.batch_ctas > 0 ? t.batch_ctas : 2;
+  const int idx = ctas_per_sm == 2 ? 0 : 1;
+  const uint32_t budget = ctas_per_sm == 2 ? kBatchSmem2 : kBatchSmem1;
+  const uint32_t w_bytes = (row_bytes + 127u) & ~127u;
+  const uint32_t target = t.batch_bytes > 0 ? (uint32_t)t.batch_bytes : kBatchBytes;
+  const uint32_t min_bytes = t.batch_min_bytes > 0 ? (uint32_t)t.batch_min_bytes : kBatchMinBytes;
+  int bR = (int)(target / row_bytes);
+  if (bR > kBatchMaxRows) bR = kBatchMaxRows;
+  if (bR < 1) bR = 1;
+  const int64_t ctas = (int64_t)sms * ctas_per_sm;
+  while (bR > 1 && (rows + bR - 1) / bR < 2 * ctas && (uint32_t)bR * row_bytes > min_bytes) bR /= 2;
+  // at least 3 slots: a refill is then issued before the batch it fetches is awaited
+  while (bR > 1 && (budget - w_bytes) / (((uint32_t)bR * row_bytes + 127u) & ~127u) < 3u) bR /= 2;
+  const uint32_t slot = ((uint32_t)bR * row_bytes + 127u) & ~127u;
+  int nslots = (int)((budget - w_bytes) / slot);
+  if (nslots > kBatchMaxSlots) nslots = kBatchMaxSlots;
+  if (t.batch_slots > 0 && t.batch_slots < nslots) nslots = t.batch_slots;
+  const int lag = t.batch_lag > 0 ? t.batch_lag : kBatchLag;
+  return VariantDesc{kBatchBase + idx, nslots, kBatchWarps[idx], bR, kBatchWarps[idx] * 32, slot,
+                     w_bytes + (uint32_t)nslots * slot, lag, 0, nslots};
+}
+}  // namespace
+
 VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t rows, int family,
-                           bool residual) {
+                           bool residual, int sms) {
   const int eb = elem_bytes(dtype);
   const bool vec_ok = aligned && hl > 0 && ((hl * eb) % 16 == 0);
   if (family == kFamilyAuto) family = get_family();
-  if (residual) return choose_residual_variant(hl, dtype, vec_ok, tp, rows, family);
+  if (residual) {
+    if (family == kFamilyBatch) family = kFamilyAuto;   // no batch kernel with a residual
+    return choose_residual_variant(hl, dtype, vec_ok, tp, rows, family);
+  }
+  // batch kernels: every aligned call with an exchange whose rows fit a slot
+  // (and any aligned call when the family is forced)
+  if (vec_ok && (uint64_t)hl * eb <= kBatchMaxRowBytes &&
+      (family == kFamilyBatch || (family == kFamilyAuto && tp > 1))) {
+    const VariantDesc v = batch_variant((uint32_t)(hl * eb), rows, sms);
+    if (v.depth >= 3) return v;
+  }
   // bulk kernels for large calls (>= kBulkMinCallBytes of x per rank with an
   // exchange, >= kBulkMinLocalCallBytes at TP = 1), register kernels below
   // that, where their lower fixed cost wins (measured on B200: with an
@@ -1121,9 +1431,11 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
                            reinterpret_cast<uintptr_t>(a_in.rp[r].res);
     if (bits & 15u) aligned = false;
   }
-  const VariantDesc v =
-      choose_variant(a_in.hl, dtype, aligned, a_in.tp, a_in.rows, kFamilyAuto, residual);
   cudaError_t err = cudaSuccess;
+  const int sms = sm_count(device, &err);
+  if (err != cudaSuccess) return err;
+  const VariantDesc v =
+      choose_variant(a_in.hl, dtype, aligned, a_in.tp, a_in.rows, kFamilyAuto, residual, sms);
   int resident = resident_ctas(device, dtype, v, &err);
   if (err != cudaSuccess) return err;
   if (grid_y > 1) resident /= grid_y;
@@ -1135,6 +1447,8 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   a.stage_bytes = v.stage_bytes;
   a.lag = v.lag;
   a.schedule = v.schedule;
+  a.depth = v.depth;
+  a.push_mode = get_push_mode();
   const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
   void* args[] = {&a};
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);

@@ -12,6 +12,11 @@
 // The array's name is only a host-side stand-in in host code: its device
 // address is looked up once per device with cudaGetSymbolAddress (with that
 // device current) and that address is what the kernel receives.
+//
+// A wait that runs out inside the kernel cannot be returned by the call that
+// launched it (the call has returned by then): it writes NaN rows and records
+// the failure in the rank's state in the array, where
+// rmsnorm_tp_forward_group_static_status reads it until the next call clears it.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -35,6 +40,7 @@ static __device__ __align__(256) unsigned char g_group_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::atomic<unsigned char*> g_scratch_ptr[kMaxDevices];
+std::atomic<int> g_last_tp[kMaxDevices];   // group size of the last call per device (0: none)
 std::mutex g_setup_mutex;
 
 int fail_static(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -89,14 +95,19 @@ extern "C" int rmsnorm_tp_forward_group_static(int tp, void* const* outs, const 
     if (rows > 0 && (!outs[r] || !xs[r] || !weights[r]))
       return fail_static(RMSNORM_TP_ERR_INVALID, "forward_group_static: NULL tensor of rank %d", r);
   if (rows == 0) return RMSNORM_TP_OK;
-  // per rank: one state + a mailbox u64 slot[2][tp][rows]
+  // per rank: one state + a mailbox u64 slot[2][tp][rows]. The row limit is
+  // checked before any product is formed, so a huge `rows` cannot wrap the
+  // byte count around to a small number.
+  const int64_t max_rows =
+      (int64_t)((kScratchBytes - (size_t)tp * kStateStride) / (16ull * (size_t)tp * (size_t)tp));
+  if (rows > max_rows)
+    return fail_static(RMSNORM_TP_ERR_ROWS,
+                       "forward_group_static: %d ranks x %lld rows do not fit; the static scratch "
+                       "holds %zu bytes (16 * tp^2 * rows + 256 * tp bytes must fit: at most "
+                       "%lld rows at tp %d)",
+                       tp, (long long)rows, kScratchBytes, (long long)max_rows, tp);
   const size_t mailbox_bytes = (size_t)rtp::mailbox_slots(tp, rows) * sizeof(unsigned long long);
   const size_t need = (size_t)tp * kStateStride + (size_t)tp * mailbox_bytes;
-  if (need > kScratchBytes)
-    return fail_static(RMSNORM_TP_ERR_ROWS,
-                       "forward_group_static: %d ranks x %lld rows need %zu bytes of scratch; the "
-                       "static scratch holds %zu (16 * tp^2 * rows + 256 * tp bytes must fit)",
-                       tp, (long long)rows, need, kScratchBytes);
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess || device < 0 || device >= kMaxDevices)
@@ -135,5 +146,45 @@ extern "C" int rmsnorm_tp_forward_group_static(int tp, void* const* outs, const 
   if (e != cudaSuccess)
     return fail_static(RMSNORM_TP_ERR_CUDA, "forward_group_static: cooperative launch: %s",
                        cudaGetErrorString(e));
+  g_last_tp[device].store(tp, std::memory_order_release);
+  return RMSNORM_TP_OK;
+}
+
+extern "C" int rmsnorm_tp_forward_group_static_status(rmsnorm_tp_status_info* out) {
+  if (!out) return fail_static(RMSNORM_TP_ERR_INVALID, "forward_group_static_status: NULL out");
+  std::memset(out, 0, sizeof(*out));
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess || device < 0 || device >= kMaxDevices)
+    return fail_static(RMSNORM_TP_ERR_CUDA, "forward_group_static_status: cudaGetDevice: %s",
+                       cudaGetErrorString(e));
+  const int tp = g_last_tp[device].load(std::memory_order_acquire);
+  if (tp == 0)
+    return fail_static(RMSNORM_TP_ERR_STATE,
+                       "forward_group_static_status: no call on device %d yet", device);
+  unsigned char* scratch = nullptr;
+  const int rc = scratch_of(device, &scratch);
+  if (rc != RMSNORM_TP_OK) return rc;
+  // the last call's kernel must have finished before its states are read
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess)
+    return fail_static(RMSNORM_TP_ERR_CUDA, "forward_group_static_status: synchronize: %s",
+                       cudaGetErrorString(e));
+  for (int r = 0; r < tp; ++r) {
+    rtp::DeviceState st;
+    e = cudaMemcpy(&st, scratch + (size_t)r * kStateStride, sizeof(st), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess)
+      return fail_static(RMSNORM_TP_ERR_CUDA, "forward_group_static_status: reading state: %s",
+                         cudaGetErrorString(e));
+    if (r == 0) out->next_generation = st.call;
+    if (st.err_code != rtp::kStatusOk && out->code == rtp::kStatusOk) {
+      out->code = st.err_code;
+      out->src_rank = st.err_src;
+      out->row = st.err_row;
+      out->expected_tag = st.err_expected;
+      out->seen_tag = st.err_seen;
+      out->generation = st.err_call;
+    }
+  }
   return RMSNORM_TP_OK;
 }

@@ -13,16 +13,20 @@
 namespace rtp {
 namespace ptx {
 
-// Streaming 128-bit load of data read once (x rows): no L1 allocation.
+// Streaming 128-bit load of data read once (x rows, the residual): no L1
+// allocation. A coherent load, not the read-only (.nc) path: the kernel may
+// write the same memory (out == x in place, the residual rewritten with
+// x + residual), which the read-only path does not allow within one kernel.
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 v;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm("ld.global.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
       : "l"(p));
   return v;
 }
 
-// 128-bit load of data every warp of the SM re-reads (the weight): L1-cached.
+// 128-bit load of data every warp of the SM re-reads and no kernel writes (the
+// weight): read-only path, L1-cached.
 __device__ __forceinline__ uint4 ld_cached_v4(const void* p) {
   uint4 v;
   asm("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -46,6 +50,27 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The reference's push encoding (csrc/rmsnorm_tp.cu:102-115, :121-138): the value
+// with a plain system-scope store, then a separate flag word with a release
+// store; the reader acquires the flag, then reads the value. Kept for the
+// measured comparison with the packed 64-bit word (push encoding 1).
+__device__ __forceinline__ void st_relaxed_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int ld_relaxed_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 

@@ -47,9 +47,9 @@ def _require_cuda_for_gpu_tests(request):
         assert torch.cuda.is_available(), "GPU test run without a CUDA device"
 
 
-@pytest.fixture(params=["bulk", "register"])
+@pytest.fixture(params=["bulk", "register", "batch"])
 def family(request):
-    """Run a test once per kernel family (bulk-copy and register kernels)."""
+    """Run a test once per kernel family (bulk-copy, register and batch kernels)."""
     import rmsnorm_tp_b200 as rtp
 
     rtp.set_kernel_family(request.param)

@@ -17,7 +17,10 @@ Checks, on the real group (TP = world size):
    rows gathered across ranks and checked by the oracle;
 6. the fused residual add and the backward pass (two exchanges per row) between
    forward calls, checked by the oracle against every rank's inputs;
-7. the one-hop round-trip probe between ranks 0 and 1.
+7. the one-hop round-trip probe between ranks 0 and 1;
+8. every kernel family (batch, register, bulk) under both push encodings
+   (packed {tag, partial} word; value + release-stored tag), decode to
+   prefill row counts, including the fused residual add.
 """
 import datetime
 import os
@@ -223,6 +226,32 @@ def main():
         ns = int(res.item())
         check(ns > 0, f"probe round trip {ns}")
         print(f"probe: store->poll round trip {ns} ns (one hop ~{ns / 2:.0f} ns)", flush=True)
+
+    # 8. kernel families x push encodings over NVLink
+    m.comm_buf.set_timeout(10.0)
+    for family in ("batch", "register", "bulk"):
+        for mode in ("packed", "release"):
+            rtp.set_kernel_family(family)
+            rtp.set_push_mode(mode)
+            try:
+                for rows in (1, 300, 4096):
+                    xs, ws = make_group(rows, 4096, tp, torch.bfloat16, 5000 + rows)
+                    rs, _ = make_group(rows, 4096, tp, torch.bfloat16, 5100 + rows)
+                    x, w, r = (t[rank].to(dev) for t in (xs, ws, rs))
+                    y = m.forward(x, w)
+                    y2 = m.forward(x, w, residual=r)
+                    torch.cuda.synchronize()
+                    compare_rank("bf16", xs, ws, 1e-6, y, rank, f"{family}/{mode} rows={rows}")
+                    want, zs = O.allreduce_path_residual(
+                        [to_np(t) for t in xs], [to_np(t) for t in rs], [to_np(t) for t in ws],
+                        1e-6, "bf16")
+                    res = O.compare("bf16", O.to_f32("bf16", to_np(y2)),
+                                    O.round_to("bf16", want[rank]))
+                    check(res["ok"], f"{family}/{mode} residual rows={rows}: {res}")
+            finally:
+                rtp.set_kernel_family("auto")
+                rtp.set_push_mode("packed")
+    check(m.comm_buf.poll_error() == 0, "no device failure across families and encodings")
 
     m.destroy()
     fails = torch.tensor([len(FAILS)], device=dev)

@@ -48,20 +48,38 @@ def test_register_plan_capacity(register_family, dtype, hl, tp):
     assert p["block_threads"] % (32 * p["team_warps"]) == 0
 
 
+@pytest.fixture
+def bulk_family():
+    rtp.set_kernel_family("bulk")
+    yield
+    rtp.set_kernel_family("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384])
 @pytest.mark.parametrize("tp", [1, 2, 3, 4, 8])
 def test_bulk_plan_for_large_calls(dtype, hl, tp):
     es = torch.tensor([], dtype=dtype).element_size()
-    # >= 48 MiB of x per rank with an exchange, >= 256 MiB at TP = 1: the automatic choice is bulk
-    rows = -(-((48 if tp > 1 else 256) << 20) // (hl * es))
-    p = rtp.plan(rows, hl, dtype, tp=tp)
-    below = rtp.plan(rows - 1, hl, dtype, tp=tp)
-    assert not 100 <= below["variant"] < 200                              # one row less: register
     row = hl * es
-    if row % 16 or row > 16384 or (tp == 1 and row == 16384):
-        assert p["variant"] < 100 or p["variant"] >= 200
-        return
+    if tp == 1:
+        # >= 256 MiB of x at TP = 1: the automatic choice is bulk; one row less: register
+        rows = -(-(256 << 20) // row)
+        p = rtp.plan(rows, hl, dtype, tp=tp)
+        below = rtp.plan(rows - 1, hl, dtype, tp=tp)
+        assert not 100 <= below["variant"] < 200
+        if row % 16 or row >= 16384:
+            assert p["variant"] < 100 or p["variant"] >= 200
+            return
+    else:
+        # with an exchange the bulk kernels run when forced
+        rtp.set_kernel_family("bulk")
+        try:
+            p = rtp.plan(1 << 16, hl, dtype, tp=tp)
+        finally:
+            rtp.set_kernel_family("auto")
+        if row % 16 or row > 16384:
+            assert p["variant"] < 100 or p["variant"] >= 200
+            return
     assert 100 <= p["variant"] < 200 and p["team_warps"] == 1 and p["depth"] == 3
     assert p["teams_per_cta"] == p["block_threads"] // 32 in (4, 8, 16)
     assert 1 <= p["rows_per_tile"] <= (32 // tp if tp > 1 else 32)       # one exchange round
@@ -71,16 +89,44 @@ def test_bulk_plan_for_large_calls(dtype, hl, tp):
     assert smem <= 216 * 1024                                             # fits one CTA per SM
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hl", [8, 64, 96, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("tp", [2, 3, 4, 8])
+@pytest.mark.parametrize("rows", [1, 7, 256, 4096, 65536])
+def test_batch_plan_with_an_exchange(dtype, hl, tp, rows):
+    """Aligned rows of up to 16 KB with an exchange take the batch kernels: batches
+    of at most 32 rows (one lane per row in the exchange), a ring of at least 3
+    slots in the shared-memory budget of 2 CTAs per SM, a grid of at most one
+    resident wave."""
+    es = torch.tensor([], dtype=dtype).element_size()
+    row = hl * es
+    p = rtp.plan(rows, hl, dtype, tp=tp, resident_ctas=296)
+    if row % 16 or row > 16384:
+        assert not 500 <= p["variant"] < 600
+        return
+    assert p["variant"] == 500 and p["block_threads"] == 256 and p["teams_per_cta"] == 1
+    bR, slots = p["rows_per_tile"], p["depth"]
+    assert 1 <= bR <= 32 and bR * row <= max(16384, row)
+    assert 3 <= slots <= 8 and p["vec_per_lane"] == slots
+    slot = -(-bR * row // 128) * 128
+    assert -(-row // 128) * 128 + slots * slot <= 100 * 1024               # 2 CTAs per SM
+    assert p["tiles"] == -(-rows // bR) and p["grid"] == min(296, p["tiles"])
+    if rows >= 2 * 296 * 32:
+        assert bR == min(32, max(1, 16384 // row))                        # no needless shrinking
+
+
 def test_unaligned_pointers_use_generic_kernel():
     assert rtp.plan(10, 1024, torch.bfloat16, aligned=False)["variant"] == -1
 
 
 def test_kernel_family_switch():
     assert rtp.get_kernel_family() == "auto"
-    bulk = range(100, 200)
+    bulk, batch = range(100, 200), range(500, 600)
     assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 200          # small call: register (TP 1)
-    assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] < 100     # with an exchange
-    assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in bulk  # 128 MiB, exchange: bulk
+    assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] in batch  # with an exchange: batch
+    assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in batch
+    assert rtp.plan(10, 1000, torch.float32, tp=2)["variant"] in batch   # 4000-byte rows
+    assert rtp.plan(10, 16384, torch.float32, tp=2)["variant"] < 100     # 64 KB rows: register
     assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 200         # 128 MiB, TP 1: local
     assert rtp.plan(262144, 1024, torch.bfloat16)["variant"] in bulk        # 512 MiB, TP 1: bulk
     rtp.set_kernel_family("register")
@@ -89,16 +135,37 @@ def test_kernel_family_switch():
         assert rtp.plan(65536, 1024, torch.bfloat16, tp=4)["variant"] < 100
         rtp.set_kernel_family("bulk")
         assert rtp.plan(10, 1024, torch.bfloat16)["variant"] in bulk
+        assert rtp.plan(10, 1024, torch.bfloat16, tp=4)["variant"] in bulk
+        rtp.set_kernel_family("batch")
+        assert rtp.plan(10, 1024, torch.bfloat16)["variant"] in batch      # TP 1 too when forced
+        assert rtp.plan(10, 1024, torch.bfloat16, tp=8)["variant"] in batch
     finally:
         rtp.set_kernel_family("auto")
 
 
+def test_push_mode_switch():
+    assert rtp.get_push_mode() == "packed"
+    try:
+        rtp.set_push_mode("release")
+        assert rtp.get_push_mode() == "release"
+    finally:
+        rtp.set_push_mode("packed")
+    from rmsnorm_tp_b200 import _lib
+    assert _lib.LIB.rmsnorm_tp_set_push_mode(2) == _lib.ERR_INVALID
+    assert rtp.get_push_mode() == "packed"
+
+
+@pytest.mark.parametrize("family", ["auto", "batch", "register"])
 @pytest.mark.parametrize("rows", [0, 1, 2, 3, 7, 255, 256, 1000, 4097, 65536])
 @pytest.mark.parametrize("hl", [64, 1024, 4096, 37])
 @pytest.mark.parametrize("resident", [1, 7, 148, 1184])
 @pytest.mark.parametrize("tp", [1, 3, 8])
-def test_every_row_is_visited_exactly_once(rows, hl, resident, tp):
-    p = rtp.plan(rows, hl, torch.bfloat16, tp=tp, resident_ctas=resident)
+def test_every_row_is_visited_exactly_once(rows, hl, resident, tp, family):
+    rtp.set_kernel_family(family)
+    try:
+        p = rtp.plan(rows, hl, torch.bfloat16, tp=tp, resident_ctas=resident)
+    finally:
+        rtp.set_kernel_family("auto")
     assert p["grid"] <= max(1, resident)
     counts = rtp.plan_coverage(p, rows)
     assert len(counts) == rows and all(c == 1 for c in counts)
@@ -108,7 +175,7 @@ def test_grid_never_exceeds_one_resident_wave():
     p = rtp.plan(65536, 1024, torch.bfloat16, tp=8, resident_ctas=148)
     assert p["grid"] == 148 and p["tiles"] == 65536 // p["rows_per_tile"]
     p = rtp.plan(3, 1024, torch.bfloat16, tp=8, resident_ctas=148)
-    assert p["grid"] == 1
+    assert p["grid"] == p["tiles"] <= 3                  # a tiny call: one CTA per batch
 
 
 def test_tp1_module_keeps_reference_attributes():

@@ -9,7 +9,8 @@ import pytest
 
 from conftest import ROOT
 
-SCRIPTS = ["bench.py", "__graft_entry__.py", os.path.join("tests", "mp_tp_worker.py")]
+SCRIPTS = ["bench.py", "__graft_entry__.py", os.path.join("tests", "mp_tp_worker.py"),
+           os.path.join("tests", "mp_stress_worker.py")]
 
 
 def _undefined_globals(path):
