@@ -83,6 +83,9 @@ def parse_args(argv=None):
                          "its fused kernel (oracle/_ref) or its NCCL path")
     ap.add_argument("--family", choices=["auto", "register", "bulk", "batch"], default="auto",
                     help="kernel family of our arm (comparisons)")
+    ap.add_argument("--push-mode", choices=["packed", "release"], default="packed",
+                    help="exchange encoding of our arm: one 64-bit {tag, partial} store (packed) "
+                         "or the reference's value + release-stored flag (comparisons)")
     ap.add_argument("--no-dependent-launch", action="store_true",
                     help="launch our kernels without programmatic dependent launch (comparisons)")
     ap.add_argument("--residual", action="store_true",
@@ -620,6 +623,7 @@ def run_our_arm(args):
     import rmsnorm_tp_b200 as rtp
 
     rtp.set_kernel_family(args.family)
+    rtp.set_push_mode(args.push_mode)
     rtp.set_dependent_launch(not args.no_dependent_launch)
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -740,6 +744,7 @@ def run_our_arm(args):
             "config": bench_config(w, tp),
             "method": {"launch": "CUDA graph of forward() calls, one kernel each",
                        "dependent_launch": rtp.get_dependent_launch(),
+                       "push_mode": rtp.get_push_mode(), "family": rtp.get_kernel_family(),
                        "rotation": f"{nsets} rotating x/out sets of {set_bytes / 2**20:.1f} MiB "
                                    f"({nsets * set_bytes / 2**20:.0f} MiB > {l2 / 2**20:.0f} MiB "
                                    "L2)"},
@@ -803,6 +808,7 @@ class OursImpl:
 
         self.m = rtp.FusedTPRMSNorm(hidden, eps=eps, tp_group=group, num_max_rows=nmax)
         self.family = rtp.get_kernel_family()
+        self.push_mode = rtp.get_push_mode()
         self.dependent_launch = rtp.get_dependent_launch()
 
     def __call__(self, x, w, out, res=None):
@@ -967,7 +973,8 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
         b = algorithmic_bytes(rows, hl, elem) + (2 * rows * hl * elem if use_res else 0)
         if use_bwd:
             b = 3 * rows * hl * elem + 2 * hl * elem
-        return {"impl": impl.name, "family": getattr(impl, "family", None), "rows": rows,
+        return {"impl": impl.name, "family": getattr(impl, "family", None),
+                "push_mode": getattr(impl, "push_mode", None), "rows": rows,
                 "residual": use_res, "backward": use_bwd,
                 "dependent_launch": getattr(impl, "dependent_launch", None), "profile": prof,
                 "local_hidden": hl, "tp": tp, "dtype": str(dtype).split(".")[-1],

@@ -796,7 +796,8 @@ int rmsnorm_tp_plan(int64_t rows, int64_t hl, int dtype, int aligned, int tp, in
   if (rows < 0 || hl < 1 || resident_ctas < 1 || tp < 1 || tp > rtp::kMaxTP)
     return fail(RMSNORM_TP_ERR_INVALID, "plan: rows %lld, local_hidden %lld, tp %d, resident %d",
                 (long long)rows, (long long)hl, tp, resident_ctas);
-  const rtp::VariantDesc v = rtp::choose_variant(hl, dtype, aligned != 0, tp, rows);
+  const rtp::VariantDesc v = rtp::finalize_variant(
+      rtp::choose_variant(hl, dtype, aligned != 0, tp, rows), tp, rows, resident_ctas);
   const rtp::Plan p = rtp::plan_for(v, rows, resident_ctas);
   out->variant = p.variant;
   out->vec_per_lane = p.vec_per_lane;
@@ -815,7 +816,7 @@ int rmsnorm_tp_plan_coverage(const rmsnorm_tp_plan_info* p, int64_t rows, int32_
   if (p->grid < 1 || p->teams_per_cta < 1 || p->rows_per_tile < 1)
     return fail(RMSNORM_TP_ERR_INVALID, "plan_coverage: malformed plan");
   for (int64_t i = 0; i < rows; ++i) counts[i] = 0;
-  if (p->variant >= rtp::kBatchBase) {
+  if (p->variant >= rtp::kBatchBase && p->variant < rtp::kResidentBase) {
     // Batch kernels: CTA c owns batches [B c / G, B (c + 1) / G) of rows_per_tile rows.
     const int64_t B = (rows + p->rows_per_tile - 1) / p->rows_per_tile;
     const int64_t G = p->grid;

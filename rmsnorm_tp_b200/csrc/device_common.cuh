@@ -206,8 +206,11 @@ __device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankP
   uint32_t fail = kStatusOk;
   const unsigned long long t0 = ptx::globaltimer();
   unsigned long long now = t0;
-  for (;;) {
+  // the abort flag and the timer are looked at every 8 probes: each is a
+  // dependent round trip that would otherwise delay seeing the slot arrive
+  for (unsigned n = 1;; ++n) {
     if (probe_slot(a, src, tag, &w)) break;
+    if ((n & 7u) != 0u) continue;
     if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
       fail = kStatusAborted;
       break;

@@ -85,6 +85,13 @@ constexpr int kLocalResBase = 300;
 constexpr int kBulkResBase = 400;
 constexpr int kGenericRes = -2;
 constexpr int kBatchBase = 500;   // batch kernels: base + index of the warp count
+// resident register kernels (TP > 1, at most kResidentDepth tiles per team):
+// base + register shape
+constexpr int kResidentBase = 600;
+constexpr int kResidentDepth = 4;
+// The register plan `v` (TP > 1) becomes the resident register kernel when every
+// team of a grid of `resident_ctas` CTAs holds at most kResidentDepth tiles.
+VariantDesc finalize_variant(const VariantDesc& v, int tp, int64_t rows, int resident_ctas);
 
 int elem_bytes(int dtype);
 
@@ -121,6 +128,69 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
 // dw[j] = sum over parts c of ws[c][j], rounded to the dtype (fixed order).
 cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, int dtype,
                              cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Fused row-parallel linear -> reduce-scatter -> TP RMSNorm (linear.cu).
+//
+// Rank r holds A_r [rows, k_local] and the linear weight W_r [hidden, k_local]
+// (nn.Linear layout: out x in, K contiguous). Its partial product
+// P_r = A_r W_r^T [rows, hidden] is scattered by column block: the columns
+// [o * hl, (o + 1) * hl) (hl = hidden / tp) go to rank o's receive buffer,
+// slot [src = r]; rank o sums the tp slots in rank order (fp32), rounds to the
+// dtype (x), optionally adds the residual, and normalises its hl columns with
+// the one-scalar-per-row exchange of the forward kernels.
+//
+// Receive region of a rank (inside its IPC-mapped mailbox allocation, after
+// the slots and the probe area): flags u32 [2 buffers][tp src][mblocks][nblocks]
+// (a tile of 128 rows x 128 columns from src has landed when its flag equals the
+// call's tag), then partials T [tp src][num_max_rows][hl].
+// ---------------------------------------------------------------------------
+constexpr int kLinTileM = 128;
+constexpr int kLinTileN = 128;
+constexpr int kLinTileK = 64;
+
+struct LinearLayout {
+  int64_t flags_off;    // bytes from the region base
+  int64_t recv_off;
+  int64_t mblocks;      // ceil(num_max_rows / 128)
+  int64_t nblocks;      // hl / 128
+  int64_t bytes;        // end of the receive region
+};
+// Layout of the receive region for (tp, num_max_rows, hidden) after `base` bytes
+// (the slots and probe area); 2-byte elements.
+LinearLayout linear_layout(int tp, int64_t nmax, int64_t hidden, int64_t base);
+
+struct LinRank {
+  const void* tmap_a;        // device copies are in LArgs::tmaps; these index them
+  void* out;                 // y [rows, hl]
+  void* res;                 // residual [rows, hl] (read, rewritten with z) or null
+  const void* gamma;         // norm weight [hl]
+  DeviceState* state;
+  unsigned int* host_flag;
+};
+
+struct alignas(64) LArgs {
+  unsigned char tmaps[2 * kMaxTP][128];   // CUtensorMap of A_r then W_r per rank, 64-aligned
+  LinRank rk[kMaxTP];                     // [0] normal launch, [blockIdx.y] when emulated
+  unsigned char* region[kMaxTP];          // every rank's mailbox region as this process maps it
+  int64_t rows;
+  int64_t k;                              // k_local
+  int64_t hidden;
+  int64_t hl;
+  int64_t nmax;
+  int64_t flags_off, recv_off, mblocks, nblocks;
+  float eps;
+  int rank;
+  int tp;
+  int emulated;
+  int push_mode;
+  unsigned long long timeout_ns;
+};
+
+// Encodes the tensor maps and launches the fused kernel (cooperative when
+// grid_y > 1: emulated ranks on one GPU). `as`/`ws`: per rank A_r and W_r.
+cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws, int dtype,
+                          int device, int grid_y, cudaStream_t stream);
 
 cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,
                          unsigned long long seq, int iters, int initiator,

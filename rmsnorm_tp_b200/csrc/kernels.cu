@@ -239,6 +239,155 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 }
 
 // ---------------------------------------------------------------------------
+// Resident register kernel (TP > 1, calls of at most kDepth tiles per team):
+// the same teams, tiles, column mapping and exchange as the register kernel
+// above, but every tile of a team is held in registers at once. All of a
+// team's loads are issued first (every byte of the call is in flight at once),
+// then each tile is reduced and its partials pushed as its data arrives, then
+// each tile's peers' partials are polled and the tile normalised and stored.
+// The NVLink round trip of a tile overlaps the loads and reductions of the
+// team's later tiles instead of waiting behind a three-buffer rotation.
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kRows, int kBlock, int kMinBlocks, int kDepth>
+__global__ void __launch_bounds__(kBlock, kMinBlocks)
+    tp_rmsnorm_vec_resident_kernel(const __grid_constant__ KArgs a) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  static_assert(kRows * kMaxTP <= 32, "one warp serves every (row, rank) pair of a tile");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const int64_t V = a.hl / Pack<T>::kE;
+  // x and out may be the same memory (in place): no __restrict__ on either
+  const uint4* xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  uint4* yg = reinterpret_cast<uint4*>(rp.out);
+  const int tp = a.tp;
+  const int lr = lane / tp;      // exchange lane -> (row, rank)
+  const int lq = lane - lr * tp;
+
+  __shared__ float s_part[kTeams][kDepth][kW][kRows];
+  __shared__ float s_sum[kTeams][kDepth][kRows];
+  __shared__ int s_ok[kTeams][kDepth];
+
+  const int64_t tiles = (a.rows + kRows - 1) / kRows;
+  const int64_t stride = (int64_t)gridDim.x * kTeams;
+  const int64_t first = (int64_t)blockIdx.x * kTeams + team;
+  WaitStats ws;
+  auto nrows_of = [&](int64_t tt) { return (int)min((int64_t)kRows, a.rows - tt * kRows); };
+  auto mine_of = [&](const float (&ss)[kRows]) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (i == lr) m = ss[i];
+    return m;
+  };
+
+  uint4 xv[kDepth][kRows][kVec];
+  float ss[kDepth][kRows];
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d) {
+    const int64_t tt = first + d * stride;
+    const int nr = tt < tiles ? nrows_of(tt) : 0;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const uint4* xr = xg + (tt * kRows + r) * V;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        xv[d][r][j] = (r < nr && c < V) ? ptx::ld_stream_v4(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
+  const unsigned long long call = read_generation(rp.state);
+  const uint32_t buf = buffer_of(call), tag = tag_of(call);
+
+  // reduce and push every tile as its loads complete
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d) {
+    const int64_t tt = first + d * stride;
+    if (tt >= tiles) break;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) s += sumsq16<T>(xv[d][r][j]);
+      ss[d][r] = warp_allreduce_sum(s);
+    }
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) s_part[team][d][wit][r] = ss[d][r];
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) s += s_part[team][d][w][r];
+        ss[d][r] = s;
+      }
+    }
+    if (kW == 1 || wit == 0)
+      push_slot(a, rank, buf, tag, tt * kRows + lr, lq, lr < nrows_of(tt), mine_of(ss[d]));
+  }
+
+  // poll, normalise and store every tile
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d) {
+    const int64_t tt = first + d * stride;
+    if (tt >= tiles) break;
+    float S[kRows];
+    bool ok = true;
+    if (kW == 1 || wit == 0) {
+      bool failed = false;
+      const float val = poll_slot(a, rank, rp, buf, tag, call, tt * kRows + lr, lq,
+                                  lr < nrows_of(tt), mine_of(ss[d]), failed, ws);
+      ok = !__any_sync(0xFFFFFFFFu, failed);
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        float s = 0.f;
+        for (int p = 0; p < tp; ++p) s += __shfl_sync(0xFFFFFFFFu, val, i * tp + p);
+        S[i] = s;
+      }
+    }
+    if constexpr (kW > 1) {
+      if (wit == 0 && lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) s_sum[team][d][r] = S[r];
+        s_ok[team][d] = ok ? 1 : 0;
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) S[r] = s_sum[team][d][r];
+      ok = s_ok[team][d] != 0;
+    }
+    const int nr = nrows_of(tt);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (r < nr) {
+        const float inv = ok ? rsqrtf(S[r] / a.hidden_f + a.eps) : quiet_nan();
+        uint4* yr = yg + (tt * kRows + r) * V;
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int c = (j * kW + wit) * 32 + lane;
+          if (c < V) ptx::st_v4(yr + c, normalize16<T>(xv[d][r][j], ptx::ld_cached_v4(wg + c), inv));
+        }
+      }
+    }
+  }
+  finish_launch(rp.state, call);
+  flush_stats(a, ws, t_start);
+}
+
+// ---------------------------------------------------------------------------
 // Local register kernel (TP = 1, no exchange). Same teams, tiles and column
 // mapping as the register kernel above, but without the exchange there is no
 // tile waiting for peers, so every buffer holds loads in flight: a team keeps
@@ -1052,7 +1201,8 @@ constexpr int kSlotLocalRes = kNumShapes + 1 + kNumBulk + kNumLocal;
 constexpr int kSlotBulkRes = kSlotLocalRes + kNumShapes;
 constexpr int kSlotGenericRes = kSlotBulkRes + kNumRowBounds;
 constexpr int kSlotBatch = kSlotGenericRes + 1;
-constexpr int kSlots = kSlotBatch + kNumBatch;
+constexpr int kSlotResident = kSlotBatch + kNumBatch;
+constexpr int kSlots = kSlotResident + kNumShapes;
 
 using KernelFn = void (*)(const KArgs);
 
@@ -1097,9 +1247,17 @@ struct KernelTable {
   static constexpr KernelFn generic_res = tp_rmsnorm_generic_kernel<T, kGenericBlock, true>;
   static constexpr KernelFn batch[kNumBatch] = {tp_rmsnorm_batch_kernel<T, 8>,
                                                 tp_rmsnorm_batch_kernel<T, 16>};
+#define RTP_RESIDENT(V, W, R, B, M) tp_rmsnorm_vec_resident_kernel<T, V, W, R, B, M, kResidentDepth>
+  static constexpr KernelFn resident[kNumShapes] = {
+      RTP_RESIDENT(1, 1, 4, 256, 2), RTP_RESIDENT(2, 1, 2, 256, 2), RTP_RESIDENT(4, 1, 1, 256, 2),
+      RTP_RESIDENT(4, 2, 1, 256, 2), RTP_RESIDENT(4, 4, 1, 256, 2), RTP_RESIDENT(4, 8, 1, 256, 2),
+      RTP_RESIDENT(4, 16, 1, 512, 1),
+  };
+#undef RTP_RESIDENT
   static KernelFn get(int variant) {
     if (variant == kGenericRes) return generic_res;
     if (variant < 0) return generic;
+    if (variant >= kResidentBase) return resident[variant - kResidentBase];
     if (variant >= kBatchBase) return batch[variant - kBatchBase];
     if (variant >= kBulkResBase) return bulk_res[variant - kBulkResBase];
     if (variant >= kLocalResBase) return local_res[variant - kLocalResBase];
@@ -1122,6 +1280,7 @@ KernelFn kernel_for(int dtype, int variant) {
 
 int slot_of(int variant) {
   if (variant == kGenericRes) return kSlotGenericRes;
+  if (variant >= kResidentBase) return kSlotResident + (variant - kResidentBase);
   if (variant >= kBatchBase) return kSlotBatch + (variant - kBatchBase);
   if (variant < 0) return kNumShapes;
   if (variant >= kBulkResBase) return kSlotBulkRes + (variant - kBulkResBase);
@@ -1170,6 +1329,11 @@ int resident_ctas(int device, int dtype, const VariantDesc& v, cudaError_t* err)
   if (v.smem_bytes > 48u * 1024u && (!cacheable || g_attr_set[device][dtype][slot].load() == 0u)) {
     *err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kBulkSmemBudget);
+    if (*err != cudaSuccess) return 0;
+    // the whole unified L1/shared array as shared memory, so that the occupancy
+    // the grid is sized by (one resident wave) is the occupancy the launch gets
+    *err = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
     if (*err != cudaSuccess) return 0;
     if (cacheable) g_attr_set[device][dtype][slot].store(1u);
   }
@@ -1336,10 +1500,8 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
     if (family == kFamilyBatch) family = kFamilyAuto;   // no batch kernel with a residual
     return choose_residual_variant(hl, dtype, vec_ok, tp, rows, family);
   }
-  // batch kernels: every aligned call with an exchange whose rows fit a slot
-  // (and any aligned call when the family is forced)
-  if (vec_ok && (uint64_t)hl * eb <= kBatchMaxRowBytes &&
-      (family == kFamilyBatch || (family == kFamilyAuto && tp > 1))) {
+  // batch kernels: when the family is forced (aligned rows that fit a slot)
+  if (vec_ok && (uint64_t)hl * eb <= kBatchMaxRowBytes && family == kFamilyBatch) {
     const VariantDesc v = batch_variant((uint32_t)(hl * eb), rows, sms);
     if (v.depth >= 3) return v;
   }
@@ -1402,6 +1564,18 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
   return VariantDesc{-1, 0, kGenericBlock / 32, 1, kGenericBlock, 0u, 0u, 0, 0, 1};
 }
 
+VariantDesc finalize_variant(const VariantDesc& v, int tp, int64_t rows, int resident_ctas) {
+  if (tp < 2 || v.id < 0 || v.id >= kNumShapes || get_family() == kFamilyRegister) return v;
+  const int64_t teams = (int64_t)resident_ctas * (v.block_threads / 32 / v.team_warps);
+  const int64_t tiles = (rows + v.rows_per_tile - 1) / v.rows_per_tile;
+  if (tiles > teams * kResidentDepth) return v;
+  VariantDesc r = v;
+  r.id = kResidentBase + v.id;
+  r.depth = (int)((tiles + teams - 1) / (teams > 0 ? teams : 1));
+  if (r.depth < 1) r.depth = 1;
+  return r;
+}
+
 Plan plan_for(const VariantDesc& v, int64_t rows, int resident_ctas) {
   Plan p{};
   p.variant = v.id;
@@ -1440,7 +1614,14 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   if (err != cudaSuccess) return err;
   if (grid_y > 1) resident /= grid_y;
   if (resident < 1) return cudaErrorCooperativeLaunchTooLarge;
-  const Plan p = plan_for(v, a_in.rows, resident);
+  VariantDesc v2 = finalize_variant(v, a_in.tp, a_in.rows, resident);
+  if (v2.id != v.id) {   // the resident kernel's own occupancy sizes its grid
+    int r2 = resident_ctas(device, dtype, v2, &err);
+    if (err != cudaSuccess) return err;
+    if (grid_y > 1) r2 /= grid_y;
+    if (r2 < resident) v2 = v;   // fewer resident CTAs: keep the rotating kernel
+  }
+  const Plan p = plan_for(v2, a_in.rows, resident);
   if (plan_out) *plan_out = p;
   KArgs a = a_in;
   a.tile_rows = v.rows_per_tile;
@@ -1449,7 +1630,7 @@ cudaError_t launch_forward(const KArgs& a_in, int dtype, int device, int grid_y,
   a.schedule = v.schedule;
   a.depth = v.depth;
   a.push_mode = get_push_mode();
-  const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v.id));
+  const void* fn = reinterpret_cast<const void*>(kernel_for(dtype, v2.id));
   void* args[] = {&a};
   const dim3 grid((unsigned)p.grid, (unsigned)grid_y);
   const dim3 block((unsigned)p.block_threads);

@@ -1,0 +1,412 @@
+// Fused row-parallel linear -> reduce-scatter -> (residual add) -> TP RMSNorm
+// for B200 (sm_100a), one persistent kernel per call.
+//
+// In a Megatron-style tensor-parallel block the row-parallel linear (attention
+// output projection, MLP down projection) leaves every rank with a partial
+// product P_r = A_r W_r^T of the full hidden width, which an all-reduce (or a
+// reduce-scatter when the norm is itself tensor parallel) sums before the
+// norm. Here rank r:
+//   phase 1 -- computes P_r tile by tile on the tensor cores (128 x 128 tiles,
+//              tcgen05.mma with fp32 accumulators in tensor memory, operands
+//              staged by TMA from this GPU's own memory) and stores each tile,
+//              rounded to the dtype, straight into the receive buffer of the
+//              rank that owns its columns (peer memory over NVLink, or local),
+//              then raises that tile's flag there: the transfer of tile t
+//              overlaps the math of the next tiles;
+//   phase 2 -- once every rank's tiles of a 128-row block have landed, sums the
+//              tp partials of each of its rows in rank order (fp32), rounds
+//              to the dtype (x), adds the residual (z = x + residual, written
+//              back), and normalises its hl = hidden / tp columns with the
+//              one-scalar-per-row exchange of the forward kernels
+//              (y = (z * rsqrt(S / hidden + eps)) * gamma, S summed in rank
+//              order).
+// The reference leaves this step to torch: the partial output goes through
+// NCCL, then its AllReduce TP RMSNorm (bench_rmsnorm_tp.py:16-22) normalises.
+//
+// Roles in phase 1 (192 threads): warp 0 lane 0 issues TMA loads into a ring of
+// 4 stages (A and W tiles of 128 x 64); warp 1 allocates tensor memory (two
+// 128-column fp32 accumulators) and its lane 0 issues the MMAs; warps 2-5
+// (one per 32-lane quarter of tensor memory) read an accumulator, convert it,
+// stage it in shared memory and store it to the owner with 16-byte stores
+// (512 contiguous bytes per warp instruction). All CTAs are resident (one per
+// SM) and phase 1 waits on nothing outside the CTA, so every phase-2 wait on
+// another rank's flags or partial sums ends.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+
+#include "device_common.cuh"
+#include "internal.h"
+#include "ptx.cuh"
+#include "rtp_common.h"
+#include "sm100.cuh"
+
+namespace rtp {
+
+namespace {
+constexpr int kLinStages = 4;
+constexpr int kLinThreads = 192;
+constexpr uint32_t kLinTileBytes = kLinTileM * kLinTileK * 2;       // 16 KB (A); W the same
+constexpr uint32_t kLinStageBytes = 2 * kLinTileBytes;
+constexpr uint32_t kLinPitch = kLinTileN * 2 + 16;                  // staging row: 256 + 16 bytes
+constexpr uint32_t kLinStagingBytes = kLinTileM * kLinPitch;
+constexpr uint32_t kLinSmem = 1024 + kLinStages * kLinStageBytes + kLinStagingBytes;
+constexpr uint32_t kLinTmemCols = 2 * kLinTileN;
+constexpr unsigned long long kLinWaitNs = 2000000000ull;           // an internal wait that never ends
+
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (;;) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (ptx::globaltimer() - t0 > kLinWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void record_failure(DeviceState* st, unsigned int* host_flag,
+                                               unsigned code, unsigned long long call) {
+  if (st == nullptr) return;
+  if (atomicCAS(&st->err_code, 0u, code) == 0u) {
+    st->err_call = call;
+    if (host_flag != nullptr) {
+      *reinterpret_cast<volatile unsigned int*>(host_flag) = code;
+      __threadfence_system();
+    }
+  }
+  atomicExch(&st->abort, 1u);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  return bf16x2_pack(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  return f16x2_pack(lo, hi);
+}
+}  // namespace
+
+template <typename T>
+__global__ void __launch_bounds__(kLinThreads, 1)
+    tp_linear_rmsnorm_kernel(const __grid_constant__ LArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ __align__(8) unsigned long long s_full[kLinStages];
+  __shared__ __align__(8) unsigned long long s_empty[kLinStages];
+  __shared__ __align__(8) unsigned long long s_accf[2];
+  __shared__ __align__(8) unsigned long long s_acce[2];
+  __shared__ __align__(8) unsigned long long s_drain;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  __shared__ unsigned long long s_call;
+
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const LinRank& rk = a.rk[ri];
+  const int tp = a.tp;
+  const bool exchange = tp > 1;
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
+  const uint32_t sbase = ptx::smem_addr(smem);
+  unsigned char* staging = smem + kLinStages * kLinStageBytes;
+  const uint32_t bar_full = ptx::smem_addr(&s_full[0]);
+  const uint32_t bar_empty = ptx::smem_addr(&s_empty[0]);
+  const uint32_t bar_accf = ptx::smem_addr(&s_accf[0]);
+  const uint32_t bar_acce = ptx::smem_addr(&s_acce[0]);
+  const uint32_t bar_drain = ptx::smem_addr(&s_drain);
+
+  const int64_t mt = (a.rows + kLinTileM - 1) / kLinTileM;
+  const int64_t nt = a.hidden / kLinTileN;
+  const int64_t nbl = a.nblocks;                       // column tiles per owner
+  const int64_t tiles = mt * nt;
+  const int kbs = (int)(a.k / kLinTileK);
+  const int64_t hl = a.hl;
+  // tile t -> (m block, n block); consecutive tiles go to different owners
+  auto tile_mn = [&](int64_t t, int64_t& mb, int64_t& nb) {
+    mb = t / nt;
+    const int64_t j = t - mb * nt;
+    nb = (j % tp) * nbl + j / tp;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLinStages; ++s) {
+      ptx::mbar_init(bar_full + 8u * s, 1u);
+      ptx::mbar_init(bar_empty + 8u * s, 1u);
+    }
+    for (int c = 0; c < 2; ++c) {
+      ptx::mbar_init(bar_accf + 8u * c, 1u);
+      ptx::mbar_init(bar_acce + 8u * c, 4u);           // one arrive per epilogue warp
+    }
+    ptx::mbar_init(bar_drain, 1u);
+    ptx::fence_mbar_init();
+    s_abort = 0;
+    s_call = exchange ? read_generation(rk.state) : 0ull;
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(ptx::smem_addr(&s_tmem), kLinTmemCols);
+    sm100::tmem_relinquish();
+    sm100::fence_before_sync();
+  }
+  __syncthreads();
+  sm100::fence_after_sync();
+  const uint32_t tmem = s_tmem;
+  const unsigned long long call = s_call;
+  const uint32_t buf = buffer_of(call), tag = tag_of(call);
+
+  // ------------------------------------------------------------------ phase 1
+  if (warp == 0 && lane == 0) {
+    // TMA producer
+    const void* tma = a.tmaps[2 * ri];
+    const void* tmb = a.tmaps[2 * ri + 1];
+    sm100::tma_prefetch_desc(tma);
+    sm100::tma_prefetch_desc(tmb);
+    int64_t it = 0;
+    int issued[kLinStages] = {0, 0, 0, 0};
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      int64_t mb, nb;
+      tile_mn(t, mb, nb);
+      for (int kb = 0; kb < kbs; ++kb, ++it) {
+        const int s = (int)(it % kLinStages);
+        const uint32_t ph = (uint32_t)((it / kLinStages) & 1);
+        if (!wait_bounded(bar_empty + 8u * s, ph ^ 1u) || s_abort) {
+          ok = false;
+          break;
+        }
+        const uint32_t sa = sbase + (uint32_t)s * kLinStageBytes;
+        ptx::mbar_arrive_expect_tx(bar_full + 8u * s, kLinStageBytes);
+        sm100::tma_load_2d(sa, tma, kb * kLinTileK, (int32_t)(mb * kLinTileM), bar_full + 8u * s);
+        sm100::tma_load_2d(sa + kLinTileBytes, tmb, kb * kLinTileK, (int32_t)(nb * kLinTileN),
+                           bar_full + 8u * s);
+        issued[s] += 1;
+      }
+    }
+    if (!ok) {
+      s_abort = 1;
+      record_failure(rk.state, rk.host_flag, kStatusLoadTimeout, call);
+      // the copies already issued land before shared memory is released
+      for (int s = 0; s < kLinStages; ++s)
+        if (issued[s] > 0) wait_bounded(bar_full + 8u * s, (uint32_t)((issued[s] - 1) & 1));
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    const uint32_t idesc = sm100::idesc_f16(sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value,
+                                            kLinTileM, kLinTileN);
+    int64_t it = 0, tc = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+      const int acc = (int)(tc & 1);
+      const uint32_t aph = (uint32_t)((tc >> 1) & 1);
+      if (!wait_bounded(bar_acce + 8u * acc, aph ^ 1u) || s_abort) {
+        ok = false;
+        break;
+      }
+      sm100::fence_after_sync();
+      const uint32_t d = tmem + (uint32_t)(acc * kLinTileN);
+      for (int kb = 0; kb < kbs; ++kb, ++it) {
+        const int s = (int)(it % kLinStages);
+        const uint32_t ph = (uint32_t)((it / kLinStages) & 1);
+        if (!wait_bounded(bar_full + 8u * s, ph) || s_abort) {
+          ok = false;
+          break;
+        }
+        sm100::fence_after_sync();
+        const uint32_t sa = sbase + (uint32_t)s * kLinStageBytes;
+        const uint64_t da = sm100::desc_k_sw128(sa);
+        const uint64_t db = sm100::desc_k_sw128(sa + kLinTileBytes);
+#pragma unroll
+        for (int k = 0; k < kLinTileK / 16; ++k)   // 16 elements = 32 bytes per MMA
+          sm100::mma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                         (kb | k) != 0 ? 1u : 0u);
+        sm100::mma_commit(bar_empty + 8u * s);     // stage s is free once these complete
+      }
+      if (!ok) break;
+      sm100::mma_commit(bar_accf + 8u * acc);      // accumulator ready for the epilogue
+    }
+    if (!ok) {
+      s_abort = 1;
+      record_failure(rk.state, rk.host_flag, kStatusLoadTimeout, call);
+    }
+    // every MMA issued has completed before tensor memory is released
+    sm100::mma_commit(bar_drain);
+    wait_bounded(bar_drain, 0u);
+  } else if (warp >= 2) {
+    // epilogue: tensor memory -> dtype -> staging -> owner's receive buffer
+    const int q4 = warp & 3;                   // tensor-memory lane quarter of this warp
+    const int et = (int)threadIdx.x - 64;      // 0..127
+    const int row = q4 * 32 + lane;            // tile row this thread reads
+    int64_t tc = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+      int64_t mb, nb;
+      tile_mn(t, mb, nb);
+      const int owner = (int)(nb / nbl);
+      const int64_t nbo = nb - (int64_t)owner * nbl;
+      const int acc = (int)(tc & 1);
+      const uint32_t aph = (uint32_t)((tc >> 1) & 1);
+      const bool ok = wait_bounded(bar_accf + 8u * acc, aph) && !s_abort;
+      if (!ok) {
+        s_abort = 1;
+        record_failure(rk.state, rk.host_flag, kStatusLoadTimeout, call);
+      }
+      // every epilogue thread takes the same branch: s_abort is read after the barrier
+      ptx::team_bar(1, 128);
+      if (s_abort) break;
+      sm100::fence_after_sync();
+      unsigned char* srow = staging + (size_t)row * kLinPitch;
+#pragma unroll
+      for (int c = 0; c < kLinTileN / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld_32x32(tmem + (uint32_t)(acc * kLinTileN + c * 32) + ((uint32_t)(q4 * 32) << 16),
+                             r);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 v;
+          v.x = pack2<T>(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+          v.y = pack2<T>(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+          v.z = pack2<T>(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+          v.w = pack2<T>(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+          *reinterpret_cast<uint4*>(srow + c * 64 + j * 16) = v;
+        }
+      }
+      sm100::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_acce + 8u * acc);   // accumulator free
+      ptx::team_bar(1, 128);                                  // staging tile complete
+      // 128 rows x 256 bytes into owner's partials [src = rank][row][col]
+      unsigned char* dst = a.region[owner] + a.recv_off +
+                           (((int64_t)rank * a.nmax + mb * kLinTileM) * hl + nbo * kLinTileN) *
+                               (int64_t)sizeof(T);
+      for (int idx = et; idx < kLinTileM * 16; idx += 128) {
+        const int i = idx >> 4, ch = idx & 15;
+        if (mb * kLinTileM + i < a.rows) {
+          const uint4 v = *reinterpret_cast<const uint4*>(staging + (size_t)i * kLinPitch + ch * 16);
+          ptx::st_v4(dst + (int64_t)i * hl * (int64_t)sizeof(T) + ch * 16, v);
+        }
+      }
+      ptx::team_bar(1, 128);   // every store of the tile issued (and the staging free)
+      if (et == 0) {
+        __threadfence_system();   // the CTA's stores of the tile before its flag
+        unsigned int* flag = reinterpret_cast<unsigned int*>(a.region[owner] + a.flags_off) +
+                             (((int64_t)buf * tp + rank) * a.mblocks + mb) * a.nblocks + nbo;
+        ptx::st_relaxed_sys_u32(flag, tag);
+      }
+    }
+  }
+  __syncthreads();   // phase 1 done on this CTA
+  if (warp == 1) {
+    sm100::fence_after_sync();
+    sm100::tmem_dealloc(tmem, kLinTmemCols);
+  }
+
+  // ------------------------------------------------------------------ phase 2
+  // Rows [rows * c / G, rows * (c + 1) / G) of this rank's columns; warps take
+  // rows round-robin. Pass A: x = sum of the tp partials (rank order), z = x +
+  // residual, z -> out (scratch), this rank's sum of z^2 pushed to every peer
+  // and kept in its own slot. Pass B: every rank's partial -> S, y from z.
+  WaitStats ws;
+  const int nwarps = kLinThreads / 32;
+  const int64_t r_lo = a.rows * (int64_t)blockIdx.x / gridDim.x;
+  const int64_t r_hi = a.rows * ((int64_t)blockIdx.x + 1) / gridDim.x;
+  const int V = (int)(hl * (int64_t)sizeof(T) / 16);          // 16-byte vectors per row
+  T* out = reinterpret_cast<T*>(rk.out);
+  T* res = reinterpret_cast<T*>(rk.res);
+  const uint4* gam = reinterpret_cast<const uint4*>(rk.gamma);
+  const unsigned char* recv = a.region[rank] + a.recv_off;
+  const unsigned int* flags = reinterpret_cast<const unsigned int*>(a.region[rank] + a.flags_off);
+  unsigned long long* mine = reinterpret_cast<unsigned long long*>(a.region[rank]);
+  const bool aborted = s_abort != 0;
+  int64_t ready_mb = -1;
+  bool flags_ok = !aborted;
+  for (int64_t i = r_lo + warp; i < r_hi && !aborted; i += nwarps) {
+    const int64_t mb = i / kLinTileM;
+    if (mb != ready_mb) {   // every rank's tiles of this 128-row block have landed
+      const int nflags = tp * (int)a.nblocks;
+      const unsigned long long t0 = ptx::globaltimer();
+      for (;;) {
+        bool all = true;
+        for (int f = lane; f < nflags; f += 32) {
+          const int src = f / (int)a.nblocks, nbo = f - src * (int)a.nblocks;
+          const unsigned int* fl = flags + (((int64_t)buf * tp + src) * a.mblocks + mb) * a.nblocks + nbo;
+          if (ptx::ld_acquire_sys_u32(fl) != tag) all = false;
+        }
+        if (__all_sync(0xFFFFFFFFu, all)) break;
+        if (ptx::globaltimer() - t0 > a.timeout_ns ||
+            (rk.state && ptx::ld_relaxed_gpu_u32(&rk.state->abort) != 0u)) {
+          if (lane == 0) record_failure(rk.state, rk.host_flag, kStatusTimeout, call);
+          flags_ok = false;
+          break;
+        }
+      }
+      ready_mb = mb;
+    }
+    float ss = 0.f;
+    for (int v = lane; v < V; v += 32) {
+      float accf[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) accf[e] = 0.f;
+      for (int src = 0; src < tp; ++src) {
+        const uint4 p = ptx::ld_stream_v4(recv + (((int64_t)src * a.nmax + i) * hl) * (int64_t)sizeof(T) +
+                                          (int64_t)v * 16);
+        float pf[8];
+        Pack<T>::unpack(p, pf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) accf[e] += pf[e];
+      }
+      uint4 z = Pack<T>::pack(accf);                       // x, rounded to the dtype
+      uint4* res_v = res ? reinterpret_cast<uint4*>(res + i * hl) + v : nullptr;
+      if (res_v) {
+        z = add16<T>(z, ptx::ld_stream_v4(res_v));         // z = x + residual, rounded
+        ptx::st_v4(res_v, z);
+      }
+      ptx::st_v4(reinterpret_cast<uint4*>(out + i * hl) + v, z);
+      ss += sumsq16<T>(z);
+    }
+    ss = warp_allreduce_sum(ss);
+    if (lane < tp) {
+      unsigned long long* slot = (lane == rank ? mine : a.region[lane] ? reinterpret_cast<unsigned long long*>(a.region[lane]) : mine) +
+                                 slot_index(buf, rank, tp, a.nmax, i);
+      if (lane == rank) {
+        *reinterpret_cast<volatile unsigned long long*>(slot) = pack_slot(ss, tag);
+      } else {
+        store_slot_lin(a.push_mode, slot, ss, tag);
+      }
+    }
+    if (!flags_ok) break;
+  }
+  __syncthreads();   // this CTA's own partials (plain stores) are visible to pass B
+  for (int64_t i = r_lo + warp; i < r_hi && !aborted; i += nwarps) {
+    bool failed = !flags_ok;
+    float val = 0.f;
+    if (lane < tp) {
+      const unsigned long long* src = mine + slot_index(buf, lane, tp, a.nmax, i);
+      if (lane == rank) {
+        val = slot_value(*reinterpret_cast<const volatile unsigned long long*>(src));
+      } else if (!failed) {
+        val = poll_slot_lin(a.push_mode, src, tag, a.timeout_ns, rk.state, failed, ws);
+        if (failed) record_failure(rk.state, rk.host_flag, kStatusTimeout, call);
+      }
+    }
+    failed = __any_sync(0xFFFFFFFFu, failed);
+    float S = 0.f;
+    for (int q = 0; q < tp; ++q) S += __shfl_sync(0xFFFFFFFFu, val, q);
+    const float inv = failed ? quiet_nan() : rsqrtf(S / (float)a.hidden + a.eps);
+    for (int v = lane; v < V; v += 32) {
+      uint4* yv = reinterpret_cast<uint4*>(out + i * hl) + v;
+      ptx::st_v4(yv, normalize16<T>(ptx::ld_stream_v4(yv), ptx::ld_cached_v4(gam + v), inv));
+    }
+  }
+  if (exchange) finish_launch(rk.state, call);
+}
+
+}  // namespace rtp

@@ -47,9 +47,11 @@ def _require_cuda_for_gpu_tests(request):
         assert torch.cuda.is_available(), "GPU test run without a CUDA device"
 
 
-@pytest.fixture(params=["bulk", "register", "batch"])
+@pytest.fixture(params=["auto", "bulk", "register", "batch"])
 def family(request):
-    """Run a test once per kernel family (bulk-copy, register and batch kernels)."""
+    """Run a test once per kernel family: the automatic choice (which includes the
+    resident register kernels with an exchange), bulk-copy, rotating register and
+    batch kernels."""
     import rmsnorm_tp_b200 as rtp
 
     rtp.set_kernel_family(request.param)

@@ -94,13 +94,18 @@ def test_bulk_plan_for_large_calls(dtype, hl, tp):
 @pytest.mark.parametrize("tp", [2, 3, 4, 8])
 @pytest.mark.parametrize("rows", [1, 7, 256, 4096, 65536])
 def test_batch_plan_with_an_exchange(dtype, hl, tp, rows):
-    """Aligned rows of up to 16 KB with an exchange take the batch kernels: batches
+    """Aligned rows of up to 16 KB with an exchange take the batch kernels (when that
+    family is chosen): batches
     of at most 32 rows (one lane per row in the exchange), a ring of at least 3
     slots in the shared-memory budget of 2 CTAs per SM, a grid of at most one
     resident wave."""
     es = torch.tensor([], dtype=dtype).element_size()
     row = hl * es
-    p = rtp.plan(rows, hl, dtype, tp=tp, resident_ctas=296)
+    rtp.set_kernel_family("batch")
+    try:
+        p = rtp.plan(rows, hl, dtype, tp=tp, resident_ctas=296)
+    finally:
+        rtp.set_kernel_family("auto")
     if row % 16 or row > 16384:
         assert not 500 <= p["variant"] < 600
         return
@@ -122,11 +127,15 @@ def test_unaligned_pointers_use_generic_kernel():
 def test_kernel_family_switch():
     assert rtp.get_kernel_family() == "auto"
     bulk, batch = range(100, 200), range(500, 600)
+    resident = range(600, 700)
     assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 200          # small call: register (TP 1)
-    assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] in batch  # with an exchange: batch
-    assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in batch
-    assert rtp.plan(10, 1000, torch.float32, tp=2)["variant"] in batch   # 4000-byte rows
-    assert rtp.plan(10, 16384, torch.float32, tp=2)["variant"] < 100     # 64 KB rows: register
+    assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] in resident   # with an exchange
+    assert rtp.plan(4096, 2048, torch.bfloat16, tp=2)["variant"] in resident  # the bench call at N=2
+    assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in bulk    # 128 MiB: bulk
+    assert rtp.plan(10, 1000, torch.float32, tp=2)["variant"] in resident    # 4000-byte rows
+    assert rtp.plan(10, 16384, torch.float32, tp=2)["variant"] == -1         # 64 KB rows: generic
+    # more tiles than 4 per team: the rotating register kernel
+    assert rtp.plan(6000, 2048, torch.bfloat16, tp=2, resident_ctas=296)["variant"] < 100
     assert rtp.plan(65536, 1024, torch.bfloat16)["variant"] >= 200         # 128 MiB, TP 1: local
     assert rtp.plan(262144, 1024, torch.bfloat16)["variant"] in bulk        # 512 MiB, TP 1: bulk
     rtp.set_kernel_family("register")
@@ -175,7 +184,7 @@ def test_grid_never_exceeds_one_resident_wave():
     p = rtp.plan(65536, 1024, torch.bfloat16, tp=8, resident_ctas=148)
     assert p["grid"] == 148 and p["tiles"] == 65536 // p["rows_per_tile"]
     p = rtp.plan(3, 1024, torch.bfloat16, tp=8, resident_ctas=148)
-    assert p["grid"] == p["tiles"] <= 3                  # a tiny call: one CTA per batch
+    assert p["grid"] == 1                                # a tiny call: one CTA
 
 
 def test_tp1_module_keeps_reference_attributes():
@@ -233,3 +242,19 @@ def test_protocol_simulation_catches_an_early_second_push(tmp_path):
                     "-I", inc, src, "-o", str(exe)], check=True)
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert res.returncode != 0 and "FAIL" in res.stdout, res.stdout
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+@pytest.mark.parametrize("hl", [64, 512, 1000, 1024, 2048, 4096, 8192])
+@pytest.mark.parametrize("rows", [1, 300, 4096, 9000])
+def test_resident_plan_holds_at_most_four_tiles_per_team(tp, hl, rows):
+    """With an exchange, a register plan whose teams would hold at most 4 tiles
+    each runs the resident register kernel (every tile's loads in flight at once);
+    its depth is the tiles per team."""
+    p = rtp.plan(rows, hl, torch.float32, tp=tp, resident_ctas=296)
+    teams = 296 * p["teams_per_cta"]
+    if 600 <= p["variant"] < 700:
+        assert p["tiles"] <= teams * 4 and p["depth"] == -(-p["tiles"] // teams)
+        assert p["grid"] == min(296, -(-p["tiles"] // p["teams_per_cta"]))
+    elif 0 <= p["variant"] < 100:
+        assert p["tiles"] > teams * 4
