@@ -158,6 +158,41 @@ int rmsnorm_local_forward_residual(void* out, void* residual, const void* x,
                                    const void* weight, int64_t rows, int64_t hidden,
                                    int dtype, float eps, void* stream);
 
+/* ---- fused row-parallel linear -> reduce-scatter -> TP RMSNorm ------------
+ * No counterpart in the reference, which leaves the step before its norm to
+ * torch: the partial output of a row-parallel linear goes through an NCCL
+ * all-reduce / reduce-scatter, then its AllReduce TP RMSNorm normalises
+ * (bench_rmsnorm_tp.py:16-22). Here one kernel per call does all of it.
+ *
+ * Rank r holds a [rows, k_local] (its slice of the linear's input) and
+ * linear_weight [hidden, k_local] (nn.Linear layout, its slice of the input
+ * features); its partial product a @ linear_weight^T [rows, hidden] is computed
+ * on the tensor cores and each 128-column block goes straight into the
+ * receive buffer of the rank that owns those columns (rank o owns columns
+ * [o * hidden / tp, (o + 1) * hidden / tp)). Rank o sums the tp partials of its
+ * columns in rank order (fp32) and rounds to the dtype (x), adds the residual
+ * when one is given (z = x + residual, written back into residual), and
+ * normalises: out = z * rsqrt(S / hidden + eps) * norm_weight, S = sum over the
+ * group of sum(z^2). out and residual are [rows, hidden / tp]; norm_weight is
+ * [hidden / tp]. bf16 or fp16; k_local a multiple of 64; hidden a multiple of
+ * 128 * tp; every pointer 16-byte aligned. A collective like rmsnorm_tp_forward
+ * (one generation per call), on a communicator made by rmsnorm_tp_create_linear,
+ * whose mailbox allocation also holds the receive buffer
+ * (num_max_rows * hidden * 2 bytes) and its flags; the same export / open /
+ * finalize / destroy calls set it up. */
+int rmsnorm_tp_create_linear(int rank, int tp_size, int64_t num_max_rows, int64_t hidden,
+                             int device, rmsnorm_tp_comm** out);
+int rmsnorm_tp_linear_forward(rmsnorm_tp_comm* comm, void* out, void* residual, const void* a,
+                              const void* linear_weight, const void* norm_weight, int64_t rows,
+                              int64_t k_local, int dtype, float eps, void* stream);
+/* Every rank of the group in one cooperative launch on one GPU (comms[r] are
+ * rank r of a group attached to each other's mailboxes); residuals may be NULL. */
+int rmsnorm_tp_linear_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
+                                       void* const* residuals, const void* const* as,
+                                       const void* const* linear_weights,
+                                       const void* const* norm_weights, int64_t rows,
+                                       int64_t k_local, int dtype, float eps, void* stream);
+
 /* ---- backward (no reference counterpart: the reference is forward-only) --- */
 
 /* Gradients of out = x * rsqrt(S / hidden + eps) * weight (S over the TP group):
@@ -326,7 +361,8 @@ const char* rmsnorm_tp_last_error(void);
 /* ABI version (major * 100 + minor). 1.01 added the residual, backward and
  * dependent-launch entry points and named the plan's last field `depth`; 1.02
  * added rmsnorm_tp_forward_group_static_status, the batch kernel family
- * (rmsnorm_tp_set_kernel_family(3)) and the push encodings. */
+ * (rmsnorm_tp_set_kernel_family(3)), the push encodings and the fused
+ * row-parallel linear entry points. */
 int rmsnorm_tp_abi_version(void);
 
 #ifdef __cplusplus

@@ -69,3 +69,26 @@ def backward_dist(x: torch.Tensor, dy: torch.Tensor, w: torch.Tensor, eps: float
     dx = inv * g - xf * (inv ** 3) * (D / hidden)
     dw = (dyf * xf * inv).sum(dim=0)
     return dx, dw
+
+
+def linear_rs_norm_group(as_: Sequence[torch.Tensor], lws: Sequence[torch.Tensor],
+                         gammas: Sequence[torch.Tensor], eps: float,
+                         residuals: Sequence[torch.Tensor] = None) -> List[torch.Tensor]:
+    """The unfused pipeline of a Megatron-style block, every rank in one process:
+    rank r's partial a_r @ lw_r^T (fp32 GEMM, rounded to the dtype as a reduce-scatter
+    in that dtype receives it), the sum of every rank's column block in rank order,
+    the residual add, then the reference's AllReduce TP RMSNorm
+    (bench_rmsnorm_tp.py:16-22)."""
+    tp = len(as_)
+    dt = as_[0].dtype
+    partials = [(a.float() @ w.float().t()).to(dt) for a, w in zip(as_, lws)]
+    hl = partials[0].shape[1] // tp
+    xs = []
+    for o in range(tp):
+        acc = partials[0][:, o * hl:(o + 1) * hl].float()
+        for p in partials[1:]:
+            acc = acc + p[:, o * hl:(o + 1) * hl].float()
+        xs.append(acc.to(dt))
+    if residuals is not None:
+        xs = [(x.float() + r.float()).to(dt) for x, r in zip(xs, residuals)]
+    return allreduce_path_group(xs, gammas, eps)

@@ -21,6 +21,11 @@ the fused residual add, which the reference does not have: the updated residual
 is z_k = (x_k + r_k).to(dtype) (an fp32 add rounded once, as torch computes
 ``x + r`` for bf16/fp16), and the norm is either path above applied to z_k.
 
+``linear_rs_norm_path`` covers the fused row-parallel linear: each rank's
+partial product rounded to the dtype (what an NCCL reduce-scatter in that dtype
+is given), summed over ranks per column block in rank order, rounded, then the
+AllReduce path above (with the residual add when given).
+
 Arrays: fp32 values are np.float32; bf16 values are carried as np.uint16 bit
 patterns; fp16 values as np.float16. Sums are taken in float64 and rounded to
 fp32 once, which is within an ulp or two of torch's fp32 reductions.
@@ -155,6 +160,44 @@ def fused_path_residual(xs: Sequence[np.ndarray], rs: Sequence[np.ndarray],
     """(outputs, updated residuals): the fused-kernel formula on z_k = x_k + r_k."""
     zs = [residual_add(x, r, dtype) for x, r in zip(xs, rs)]
     return fused_path(zs, ws, eps, dtype), zs
+
+
+def linear_partials(as_: Sequence[np.ndarray], lws: Sequence[np.ndarray],
+                    dtype: str) -> List[np.ndarray]:
+    """Rank r's partial product of a row-parallel linear, a_r @ lw_r^T, accumulated
+    in float64, rounded to fp32 and then to `dtype` (what the rank sends)."""
+    outs = []
+    for a, w in zip(as_, lws):
+        p = to_f32(dtype, a).astype(np.float64) @ to_f32(dtype, w).astype(np.float64).T
+        outs.append(round_to(dtype, p.astype(np.float32)))
+    return outs
+
+
+def linear_reduce_scatter(partials: Sequence[np.ndarray], dtype: str) -> List[np.ndarray]:
+    """Reduce-scatter by column block: rank o gets the rank-order fp32 sum of every
+    rank's columns [o * hl, (o + 1) * hl), rounded to `dtype` (stored representation)."""
+    tp = len(partials)
+    hl = partials[0].shape[1] // tp
+    xs = []
+    for o in range(tp):
+        acc = np.zeros((partials[0].shape[0], hl), dtype=np.float32)
+        for p in partials:
+            acc = (acc + p[:, o * hl:(o + 1) * hl]).astype(np.float32)
+        xs.append(from_f32(dtype, acc))
+    return xs
+
+
+def linear_rs_norm_path(as_: Sequence[np.ndarray], lws: Sequence[np.ndarray],
+                        gammas: Sequence[np.ndarray], eps: float, dtype: str,
+                        residuals: Sequence[np.ndarray] = None):
+    """Row-parallel linear -> reduce-scatter -> (residual add) -> the reference's
+    AllReduce TP RMSNorm (bench_rmsnorm_tp.py:16-22), the unfused pipeline a
+    Megatron-style block runs. Returns (every rank's fp32 output, every rank's
+    normalised input z in `dtype`'s stored representation)."""
+    xs = linear_reduce_scatter(linear_partials(as_, lws, dtype), dtype)
+    if residuals is not None:
+        return allreduce_path_residual(xs, residuals, gammas, eps, dtype)
+    return allreduce_path(xs, gammas, eps, dtype), xs
 
 
 def backward_path(xs: Sequence[np.ndarray], dys: Sequence[np.ndarray], ws: Sequence[np.ndarray],

@@ -9,7 +9,9 @@ package fails if that library has not been built.
 from ._lib import RMSNormTPDeviceError, RMSNormTPError
 from .api import (
     EmulatedTPGroup,
+    EmulatedTPLinearGroup,
     exchange_handles,
+    FusedTPLinearRMSNorm,
     FusedTPRMSNorm,
     IpcHandle,
     TPCommBuffer,
@@ -31,6 +33,8 @@ from .api import (
 
 __all__ = [
     "FusedTPRMSNorm",
+    "FusedTPLinearRMSNorm",
+    "EmulatedTPLinearGroup",
     "TPCommBuffer",
     "IpcHandle",
     "EmulatedTPGroup",

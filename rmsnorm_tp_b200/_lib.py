@@ -112,6 +112,20 @@ SIGNATURES = {
             _c_void_p,
         ],
     ),
+    "rmsnorm_tp_create_linear": (_i32, [_i32, _i32, _i64, _i64, _i32, ctypes.POINTER(_c_void_p)]),
+    "rmsnorm_tp_linear_forward": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32,
+         ctypes.c_float, _c_void_p],
+    ),
+    "rmsnorm_tp_linear_forward_emulated": (
+        _i32,
+        [
+            ctypes.POINTER(_c_void_p), _i32, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+            ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), _i64,
+            _i64, _i32, ctypes.c_float, _c_void_p,
+        ],
+    ),
     "rmsnorm_tp_backward_workspace_bytes": (_sz, [_i64, _i64]),
     "rmsnorm_tp_backward": (
         _i32,

@@ -154,11 +154,15 @@ class TPCommBuffer:
     reference's API.
     """
 
-    def __init__(self, rank: int, tp_size: int, num_max_rows: int, device: Optional[int] = None):
+    def __init__(self, rank: int, tp_size: int, num_max_rows: int, device: Optional[int] = None,
+                 linear_hidden: int = 0):
         self.rank = rank
         self.tp_size = tp_size
         self.num_max_rows = num_max_rows
         self.device = torch.cuda.current_device() if device is None else int(device)
+        # > 0: the mailbox allocation also holds the receive buffer of the fused
+        # row-parallel linear for this hidden width (FusedTPLinearRMSNorm)
+        self.linear_hidden = int(linear_hidden)
         self._comm = ctypes.c_void_p()
         self._generation = 0
 
@@ -166,6 +170,14 @@ class TPCommBuffer:
     def allocate(self) -> None:
         if self._comm.value:
             raise RuntimeError("TPCommBuffer.allocate: already allocated")
+        if self.linear_hidden > 0:
+            check(
+                LIB.rmsnorm_tp_create_linear(self.rank, self.tp_size, self.num_max_rows,
+                                             self.linear_hidden, self.device,
+                                             ctypes.byref(self._comm)),
+                "rmsnorm_tp_create_linear",
+            )
+            return
         check(
             LIB.rmsnorm_tp_create(self.rank, self.tp_size, self.num_max_rows, self.device,
                                   ctypes.byref(self._comm)),
@@ -443,6 +455,159 @@ class FusedTPRMSNorm:
                 dist.barrier(group=self.tp_group)
             self.comm_buf.destroy()
             self.comm_buf = None
+
+
+def _check_linear_operands(a: torch.Tensor, linear_weight: torch.Tensor,
+                           norm_weight: torch.Tensor, hidden: int, tp: int) -> None:
+    for name, t in (("a", a), ("linear_weight", linear_weight), ("norm_weight", norm_weight)):
+        if not t.is_contiguous():
+            raise AssertionError(f"{name} must be contiguous")
+        if not t.is_cuda or t.device != a.device:
+            raise AssertionError(f"{name} must be a CUDA tensor on a's device")
+        if t.dtype != a.dtype:
+            raise AssertionError(f"{name} must have a's dtype ({a.dtype}), got {t.dtype}")
+    if a.dtype not in (torch.bfloat16, torch.float16):
+        raise AssertionError(f"the tensor-core path takes bfloat16 or float16, got {a.dtype}")
+    if a.dim() != 2 or linear_weight.dim() != 2 or linear_weight.shape != (hidden, a.shape[1]):
+        raise AssertionError(
+            f"a must be [rows, k_local] and linear_weight [hidden={hidden}, k_local], got "
+            f"{tuple(a.shape)} and {tuple(linear_weight.shape)}")
+    if norm_weight.shape != (hidden // tp,):
+        raise AssertionError(f"norm_weight must be [{hidden // tp}], got {tuple(norm_weight.shape)}")
+
+
+class FusedTPLinearRMSNorm:
+    """Row-parallel linear -> reduce-scatter -> (residual add) -> TP RMSNorm, one
+    kernel per call (no reference counterpart: the reference normalises the
+    output of an NCCL reduction with its AllReduce path, bench_rmsnorm_tp.py:16-22).
+
+    ``FusedTPLinearRMSNorm(hidden_dim, eps=1e-6, tp_group=None, num_max_rows=4096)``;
+    ``forward(a, linear_weight, norm_weight, residual=None, out=None)`` with ``a``
+    ``[rows, k_local]`` (this rank's slice of the linear's input features),
+    ``linear_weight`` ``[hidden_dim, k_local]`` (nn.Linear layout), ``norm_weight``
+    ``[hidden_dim / tp]``; returns this rank's ``[rows, hidden_dim / tp]`` columns of
+    ``rmsnorm(sum over ranks of a_r @ linear_weight_r^T (+ residual))``. ``residual``
+    (``[rows, hidden_dim / tp]``) is updated in place with the sum. bf16 or fp16;
+    k_local a multiple of 64, hidden_dim a multiple of 128 * tp. A collective:
+    every rank calls it in the same order with the same number of rows.
+    """
+
+    def __init__(self, hidden_dim: int, eps: float = 1e-6, tp_group=None,
+                 num_max_rows: int = 4096, timeout_s: Optional[float] = None):
+        self.hidden_dim = int(hidden_dim)
+        self.eps = eps
+        self.tp_group = tp_group
+        self.num_max_rows = int(num_max_rows)
+        self.tp_size = dist.get_world_size(tp_group) if tp_group else 1
+        self.rank = dist.get_rank(tp_group) if tp_group else 0
+        local_device = torch.cuda.current_device()
+        self.comm_buf = TPCommBuffer(self.rank, self.tp_size, self.num_max_rows, local_device,
+                                     linear_hidden=self.hidden_dim)
+        self.comm_buf.allocate()
+        if timeout_s is not None:
+            self.comm_buf.set_timeout(timeout_s)
+        if self.tp_size > 1:
+            handle = self.comm_buf.get_ipc_handle()
+            _, handles = exchange_handles(tp_group, local_device, handle)
+            for i in range(self.tp_size):
+                if i != self.rank:
+                    self.comm_buf.open_remote_handle(i, handles[i])
+        self.comm_buf.finalize_setup()
+        if self.tp_size > 1:
+            dist.barrier(group=tp_group)
+
+    def forward(self, a: torch.Tensor, linear_weight: torch.Tensor, norm_weight: torch.Tensor,
+                residual: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        _check_linear_operands(a, linear_weight, norm_weight, self.hidden_dim, self.tp_size)
+        rows = a.shape[0]
+        if rows > self.num_max_rows:
+            raise AssertionError(f"num_rows {rows} > num_max_rows {self.num_max_rows}")
+        hl = self.hidden_dim // self.tp_size
+        if out is None:
+            out = torch.empty(rows, hl, dtype=a.dtype, device=a.device)
+        elif out.shape != (rows, hl) or out.dtype != a.dtype or not out.is_contiguous():
+            raise AssertionError(f"out must be contiguous [{rows}, {hl}] of a's dtype")
+        if residual is not None and (residual.shape != (rows, hl) or residual.dtype != a.dtype
+                                     or not residual.is_contiguous()):
+            raise AssertionError(f"residual must be contiguous [{rows}, {hl}] of a's dtype")
+        self.comm_buf.next_generation()
+        check(
+            LIB.rmsnorm_tp_linear_forward(self.comm_buf._comm, out.data_ptr(),
+                                          None if residual is None else residual.data_ptr(),
+                                          a.data_ptr(), linear_weight.data_ptr(),
+                                          norm_weight.data_ptr(), rows, a.shape[1],
+                                          _DTYPES[a.dtype], float(self.eps),
+                                          _stream_of(a.device.index)),
+            "rmsnorm_tp_linear_forward",
+        )
+        return out
+
+    __call__ = forward
+
+    def status(self) -> dict:
+        return self.comm_buf.status()
+
+    def destroy(self) -> None:
+        if self.comm_buf is not None:
+            torch.cuda.synchronize()
+            if self.tp_size > 1 and dist.is_available() and dist.is_initialized():
+                dist.barrier(group=self.tp_group)
+            self.comm_buf.destroy()
+            self.comm_buf = None
+
+
+class EmulatedTPLinearGroup:
+    """Every rank of a FusedTPLinearRMSNorm group on ONE GPU (one cooperative
+    launch, rank = blockIdx.y), for tests without several GPUs."""
+
+    def __init__(self, tp_size: int, hidden_dim: int, eps: float = 1e-6,
+                 num_max_rows: int = 4096, device: Optional[int] = None,
+                 timeout_s: Optional[float] = None):
+        if not 2 <= tp_size <= _lib.MAX_TP:
+            raise ValueError(f"tp_size {tp_size} outside [2, {_lib.MAX_TP}]")
+        self.tp_size, self.hidden_dim, self.eps = tp_size, int(hidden_dim), eps
+        self.num_max_rows = int(num_max_rows)
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        self.bufs = [TPCommBuffer(r, tp_size, self.num_max_rows, self.device,
+                                  linear_hidden=self.hidden_dim) for r in range(tp_size)]
+        for b in self.bufs:
+            b.allocate()
+            if timeout_s is not None:
+                b.set_timeout(timeout_s)
+        boxes = [b.mailbox()[0] for b in self.bufs]
+        for b in self.bufs:
+            for q in range(tp_size):
+                if q != b.rank:
+                    b.attach_peer(q, boxes[q])
+            b.finalize_setup()
+
+    def forward(self, as_: Sequence[torch.Tensor], linear_weights: Sequence[torch.Tensor],
+                norm_weights: Sequence[torch.Tensor],
+                residuals: Optional[Sequence[torch.Tensor]] = None) -> List[torch.Tensor]:
+        tp = self.tp_size
+        for a, w, g in zip(as_, linear_weights, norm_weights):
+            _check_linear_operands(a, w, g, self.hidden_dim, tp)
+        rows, k = as_[0].shape
+        hl = self.hidden_dim // tp
+        outs = [torch.empty(rows, hl, dtype=as_[0].dtype, device=as_[0].device) for _ in range(tp)]
+        P = ctypes.c_void_p * tp
+        for b in self.bufs:
+            b.next_generation()
+        rptr = None if residuals is None else P(*[r.data_ptr() for r in residuals])
+        check(
+            LIB.rmsnorm_tp_linear_forward_emulated(
+                P(*[b._comm.value for b in self.bufs]), tp, P(*[o.data_ptr() for o in outs]), rptr,
+                P(*[a.data_ptr() for a in as_]), P(*[w.data_ptr() for w in linear_weights]),
+                P(*[g.data_ptr() for g in norm_weights]), rows, k, _DTYPES[as_[0].dtype],
+                float(self.eps), _stream_of(as_[0].device.index)),
+            "rmsnorm_tp_linear_forward_emulated",
+        )
+        return outs
+
+    def destroy(self) -> None:
+        for b in self.bufs:
+            b.destroy()
 
 
 class EmulatedTPGroup:

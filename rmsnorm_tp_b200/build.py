@@ -2,7 +2,8 @@
 
 The library is plain CUDA C++ (no torch, no pybind11): kernels.cu holds the
 forward kernels and their launcher, backward.cu the backward kernels,
-noalloc.cu the allocation-free group entry point, comm.cpp the extern "C" entry points declared in
+noalloc.cu the allocation-free group entry point, linear.cu the fused row-parallel linear
+(tcgen05 GEMM) -> reduce-scatter -> TP RMSNorm kernel, comm.cpp the extern "C" entry points declared in
 include/rmsnorm_tp_b200.h. The CUDA runtime is linked statically, so the
 library loads (and its symbols can be listed) on a machine without a GPU.
 
@@ -27,12 +28,14 @@ LIB_NAME = "librmsnorm_tp_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
 SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "backward.cu"),
-           os.path.join(CSRC, "comm.cpp"), os.path.join(CSRC, "noalloc.cu")]
+           os.path.join(CSRC, "comm.cpp"), os.path.join(CSRC, "noalloc.cu"),
+           os.path.join(CSRC, "linear.cu")]
 HEADERS = [
     os.path.join(CSRC, "device_common.cuh"),
     os.path.join(CSRC, "rtp_common.h"),
     os.path.join(CSRC, "internal.h"),
     os.path.join(CSRC, "ptx.cuh"),
+    os.path.join(CSRC, "sm100.cuh"),
     os.path.join(ROOT_DIR, "include", "rmsnorm_tp_b200.h"),
 ]
 

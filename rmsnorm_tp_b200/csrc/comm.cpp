@@ -95,7 +95,8 @@ struct HandleBytes {
   int64_t nmax;
   uint64_t mailbox_bytes;
   unsigned char uuid[16];
-  unsigned char reserved[16];
+  int64_t linear_hidden;        // hidden width of the fused linear's receive region (0: none)
+  unsigned char reserved[8];
 };
 static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t is 64 bytes");
 static_assert(sizeof(HandleBytes) == rtp::kHandleBytes, "handle is 128 bytes");
@@ -129,6 +130,8 @@ struct rmsnorm_tp_comm {
   unsigned long long probe_seq = 0;
   unsigned char uuid[16] = {};
   unsigned long long* prof = nullptr;      // optional device counters (5 x u64)
+  int64_t linear_hidden = 0;               // fused linear: hidden width of the receive region
+  rtp::LinearLayout lin{};                 // fused linear: layout of the receive region
 };
 
 static void release(rmsnorm_tp_comm* c) {
@@ -155,8 +158,8 @@ int rmsnorm_tp_abi_version(void) { return 102; }
 uint32_t rmsnorm_tp_tag_of(uint64_t generation) { return rtp::tag_of(generation); }
 uint32_t rmsnorm_tp_buffer_of(uint64_t generation) { return rtp::buffer_of(generation); }
 
-int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
-                      rmsnorm_tp_comm** out) {
+static int create_impl(int rank, int tp_size, int64_t num_max_rows, int64_t linear_hidden,
+                       int device, rmsnorm_tp_comm** out) {
   if (!out) return fail(RMSNORM_TP_ERR_INVALID, "create: out is NULL");
   *out = nullptr;
   if (tp_size < 1 || tp_size > rtp::kMaxTP)
@@ -181,6 +184,11 @@ int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
   c->device = device;
   c->nmax = num_max_rows;
   c->mailbox_bytes = slots_bytes(tp_size, num_max_rows) + kProbeBytes;
+  if (linear_hidden > 0) {
+    c->linear_hidden = linear_hidden;
+    c->lin = rtp::linear_layout(tp_size, num_max_rows, linear_hidden, (int64_t)c->mailbox_bytes);
+    c->mailbox_bytes = (size_t)c->lin.bytes;
+  }
   if (const char* env = std::getenv("RMSNORM_TP_TIMEOUT_MS")) {
     const long long ms = std::atoll(env);
     if (ms > 0) c->timeout_ns = (unsigned long long)ms * 1000000ull;
@@ -212,6 +220,24 @@ int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
   return RMSNORM_TP_OK;
 }
 
+int rmsnorm_tp_create(int rank, int tp_size, int64_t num_max_rows, int device,
+                      rmsnorm_tp_comm** out) {
+  return create_impl(rank, tp_size, num_max_rows, 0, device, out);
+}
+
+int rmsnorm_tp_create_linear(int rank, int tp_size, int64_t num_max_rows, int64_t hidden,
+                             int device, rmsnorm_tp_comm** out) {
+  if (out) *out = nullptr;
+  if (tp_size < 1 || tp_size > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "create_linear: tp_size %d outside [1, %d]", tp_size,
+                rtp::kMaxTP);
+  if (hidden < 1 || hidden % ((int64_t)tp_size * rtp::kLinTileN) != 0 || hidden > (int64_t(1) << 20))
+    return fail(RMSNORM_TP_ERR_INVALID,
+                "create_linear: hidden %lld must be a positive multiple of tp * %d (<= 2^20)",
+                (long long)hidden, rtp::kLinTileN);
+  return create_impl(rank, tp_size, num_max_rows, hidden, device, out);
+}
+
 int rmsnorm_tp_export_handle(const rmsnorm_tp_comm* c, void* out, size_t cap, size_t* len) {
   if (!c || !out) return fail(RMSNORM_TP_ERR_INVALID, "export_handle: NULL argument");
   if (cap < sizeof(HandleBytes))
@@ -228,6 +254,7 @@ int rmsnorm_tp_export_handle(const rmsnorm_tp_comm* c, void* out, size_t cap, si
   h.tp = c->tp;
   h.nmax = c->nmax;
   h.mailbox_bytes = c->mailbox_bytes;
+  h.linear_hidden = c->linear_hidden;
   std::memcpy(h.uuid, c->uuid, 16);
   std::memcpy(out, &h, sizeof(h));
   if (len) *len = sizeof(h);
@@ -249,11 +276,13 @@ int rmsnorm_tp_open_peer(rmsnorm_tp_comm* c, int peer, const void* bytes, size_t
   if (h.magic != rtp::kHandleMagic || h.version != rtp::kHandleVersion)
     return fail(RMSNORM_TP_ERR_HANDLE, "open_peer: not a mailbox handle (magic %08x version %u)",
                 h.magic, h.version);
-  if (h.rank != peer || h.tp != c->tp || h.nmax != c->nmax || h.mailbox_bytes != c->mailbox_bytes)
+  if (h.rank != peer || h.tp != c->tp || h.nmax != c->nmax || h.mailbox_bytes != c->mailbox_bytes ||
+      h.linear_hidden != c->linear_hidden)
     return fail(RMSNORM_TP_ERR_HANDLE,
-                "open_peer: handle of rank %d (tp %d, num_max_rows %lld) does not match peer %d "
-                "(tp %d, num_max_rows %lld)",
-                h.rank, h.tp, (long long)h.nmax, peer, c->tp, (long long)c->nmax);
+                "open_peer: handle of rank %d (tp %d, num_max_rows %lld, linear hidden %lld) does "
+                "not match peer %d (tp %d, num_max_rows %lld, linear hidden %lld)",
+                h.rank, h.tp, (long long)h.nmax, (long long)h.linear_hidden, peer, c->tp,
+                (long long)c->nmax, (long long)c->linear_hidden);
   if (std::memcmp(h.uuid, c->uuid, 16) == 0)
     return fail(RMSNORM_TP_ERR_HANDLE,
                 "open_peer: peer %d is on this rank's GPU; one GPU per rank is required", peer);
@@ -519,6 +548,127 @@ int rmsnorm_tp_forward_emulated_residual(rmsnorm_tp_comm* const* comms, int tp, 
   if (!residuals) return fail(RMSNORM_TP_ERR_INVALID, "forward_emulated_residual: NULL residuals");
   return forward_emulated_impl("forward_emulated_residual", comms, tp, outs, residuals, xs, ws, rows,
                                hl, dtype, eps, stream);
+}
+
+// ---- fused row-parallel linear -> reduce-scatter -> TP RMSNorm ---------------
+
+static int check_linear(const char* who, const rmsnorm_tp_comm* c, int64_t rows, int64_t k,
+                        int dtype, const void* out, const void* res, const void* a, const void* w,
+                        const void* gamma) {
+  if (!c->finalized) return fail(RMSNORM_TP_ERR_STATE, "%s: communicator not finalized", who);
+  if (c->linear_hidden == 0)
+    return fail(RMSNORM_TP_ERR_STATE, "%s: communicator made without a linear receive region "
+                "(use rmsnorm_tp_create_linear)", who);
+  if (dtype != RMSNORM_TP_BF16 && dtype != RMSNORM_TP_F16)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: dtype %d; the tensor-core path takes bf16 or fp16",
+                who, dtype);
+  if (rows < 0 || rows > c->nmax)
+    return fail(rows < 0 ? RMSNORM_TP_ERR_INVALID : RMSNORM_TP_ERR_ROWS,
+                "%s: rows %lld outside [0, num_max_rows %lld]", who, (long long)rows,
+                (long long)c->nmax);
+  if (k < rtp::kLinTileK || k % rtp::kLinTileK != 0 || k > (int64_t(1) << 20))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: k_local %lld must be a positive multiple of %d",
+                who, (long long)k, rtp::kLinTileK);
+  if (rows > 0 && (!out || !a || !w || !gamma))
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL tensor pointer", who);
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(res) |
+                         reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
+                         reinterpret_cast<uintptr_t>(gamma);
+  if (bits & 15u)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: every tensor must be 16-byte aligned", who);
+  if (res != nullptr) {
+    const int rc = check_residual(who, rows, c->linear_hidden / c->tp, dtype, res, out);
+    if (rc != RMSNORM_TP_OK) return rc;
+  }
+  if (*reinterpret_cast<volatile unsigned*>(c->host_flag) != 0u)
+    return fail(RMSNORM_TP_ERR_DEVICE,
+                "%s: an earlier launch recorded a device failure; reset the communicator on "
+                "every rank", who);
+  return RMSNORM_TP_OK;
+}
+
+static void fill_linear(rtp::LArgs& L, const rmsnorm_tp_comm* c, int64_t rows, int64_t k,
+                        float eps) {
+  L.rows = rows;
+  L.k = k;
+  L.hidden = c->linear_hidden;
+  L.hl = c->linear_hidden / c->tp;
+  L.nmax = c->nmax;
+  L.flags_off = c->lin.flags_off;
+  L.recv_off = c->lin.recv_off;
+  L.mblocks = c->lin.mblocks;
+  L.nblocks = c->lin.nblocks;
+  L.eps = eps;
+  L.tp = c->tp;
+  L.timeout_ns = c->timeout_ns;
+}
+
+int rmsnorm_tp_linear_forward(rmsnorm_tp_comm* c, void* out, void* residual, const void* a,
+                              const void* linear_weight, const void* norm_weight, int64_t rows,
+                              int64_t k_local, int dtype, float eps, void* stream) {
+  const char* who = "linear_forward";
+  if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL communicator", who);
+  int rc = check_linear(who, c, rows, k_local, dtype, out, residual, a, linear_weight, norm_weight);
+  if (rc != RMSNORM_TP_OK) return rc;
+  if (rows == 0) return RMSNORM_TP_OK;
+  rtp::LArgs* L = new (std::nothrow) rtp::LArgs();
+  if (!L) return fail(RMSNORM_TP_ERR_INVALID, "%s: out of host memory", who);
+  fill_linear(*L, c, rows, k_local, eps);
+  L->rk[0] = rtp::LinRank{out, residual, norm_weight, c->state, c->host_flag_dev};
+  for (int q = 0; q < c->tp; ++q) L->region[q] = reinterpret_cast<unsigned char*>(c->peers[q]);
+  L->rank = c->rank;
+  L->emulated = 0;
+  const void* as[1] = {a};
+  const void* ws[1] = {linear_weight};
+  DeviceGuard guard(c->device);
+  cudaError_t e = guard.err;
+  if (e == cudaSuccess)
+    e = rtp::launch_linear(*L, as, ws, dtype, c->device, 1, reinterpret_cast<cudaStream_t>(stream));
+  delete L;
+  if (e != cudaSuccess) return cuda_fail(e, who, "kernel launch");
+  return RMSNORM_TP_OK;
+}
+
+int rmsnorm_tp_linear_forward_emulated(rmsnorm_tp_comm* const* comms, int tp, void* const* outs,
+                                       void* const* residuals, const void* const* as,
+                                       const void* const* linear_weights,
+                                       const void* const* norm_weights, int64_t rows,
+                                       int64_t k_local, int dtype, float eps, void* stream) {
+  const char* who = "linear_forward_emulated";
+  if (!comms || !outs || !as || !linear_weights || !norm_weights)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: NULL argument", who);
+  if (tp < 2 || tp > rtp::kMaxTP)
+    return fail(RMSNORM_TP_ERR_INVALID, "%s: tp %d outside [2, %d]", who, tp, rtp::kMaxTP);
+  for (int r = 0; r < tp; ++r) {
+    const rmsnorm_tp_comm* c = comms[r];
+    if (!c) return fail(RMSNORM_TP_ERR_INVALID, "%s: comms[%d] is NULL", who, r);
+    if (c->rank != r || c->tp != tp || c->device != comms[0]->device ||
+        c->nmax != comms[0]->nmax || c->linear_hidden != comms[0]->linear_hidden)
+      return fail(RMSNORM_TP_ERR_INVALID, "%s: comms[%d] is not rank %d of one group", who, r, r);
+    const int rc = check_linear(who, c, rows, k_local, dtype, outs[r],
+                                residuals ? residuals[r] : nullptr, as[r], linear_weights[r],
+                                norm_weights[r]);
+    if (rc != RMSNORM_TP_OK) return rc;
+  }
+  if (rows == 0) return RMSNORM_TP_OK;
+  rtp::LArgs* L = new (std::nothrow) rtp::LArgs();
+  if (!L) return fail(RMSNORM_TP_ERR_INVALID, "%s: out of host memory", who);
+  fill_linear(*L, comms[0], rows, k_local, eps);
+  for (int r = 0; r < tp; ++r) {
+    L->rk[r] = rtp::LinRank{outs[r], residuals ? residuals[r] : nullptr, norm_weights[r],
+                            comms[r]->state, comms[r]->host_flag_dev};
+    L->region[r] = reinterpret_cast<unsigned char*>(comms[r]->mailbox);
+  }
+  L->rank = 0;
+  L->emulated = 1;
+  DeviceGuard guard(comms[0]->device);
+  cudaError_t e = guard.err;
+  if (e == cudaSuccess)
+    e = rtp::launch_linear(*L, as, linear_weights, dtype, comms[0]->device, tp,
+                           reinterpret_cast<cudaStream_t>(stream));
+  delete L;
+  if (e != cudaSuccess) return cuda_fail(e, who, "cooperative launch");
+  return RMSNORM_TP_OK;
 }
 
 // ---- backward ---------------------------------------------------------------

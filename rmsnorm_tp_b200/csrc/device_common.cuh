@@ -155,9 +155,9 @@ struct WaitStats {          // optional per-lane counters (KArgs::prof)
 // Stores {mine, tag} into a slot: one 64-bit system-scope store (packed encoding,
 // the default), or the value and then the tag with a release store (the
 // reference's flag scheme, KArgs::push_mode == kPushRelease).
-__device__ __forceinline__ void store_slot(const KArgs& a, unsigned long long* dst, float mine,
+__device__ __forceinline__ void store_slot(int push_mode, unsigned long long* dst, float mine,
                                            uint32_t tag) {
-  if (a.push_mode == kPushRelease) {
+  if (push_mode == kPushRelease) {
     unsigned int* w = reinterpret_cast<unsigned int*>(dst);   // [0] value, [1] tag
     ptx::st_relaxed_sys_u32(w, f32_bits(mine));
     ptx::st_release_sys_u32(w + 1, tag);
@@ -167,9 +167,9 @@ __device__ __forceinline__ void store_slot(const KArgs& a, unsigned long long* d
 }
 
 // One look at a local slot: true if it carries `tag`; *word gets {tag seen, value}.
-__device__ __forceinline__ bool probe_slot(const KArgs& a, const unsigned long long* src,
+__device__ __forceinline__ bool probe_slot(int push_mode, const unsigned long long* src,
                                            uint32_t tag, unsigned long long* word) {
-  if (a.push_mode == kPushRelease) {
+  if (push_mode == kPushRelease) {
     const unsigned int* w = reinterpret_cast<const unsigned int*>(src);
     const unsigned int t = ptx::ld_acquire_sys_u32(w + 1);
     if (t != tag) {
@@ -187,8 +187,40 @@ __device__ __forceinline__ void push_slot(const KArgs& a, int rank, uint32_t buf
                                           int64_t row, int q, bool active, float mine) {
   if (active && q != rank) {
     unsigned long long* dst = a.mbox[q] + slot_index(buf, rank, a.tp, a.nmax, row);
-    store_slot(a, dst, mine, tag);
+    store_slot(a.push_mode, dst, mine, tag);
   }
+}
+
+// Bounded wait until the local slot `src` carries `tag`: kStatusOk, or
+// kStatusTimeout after timeout_ns, or kStatusAborted once *abort_flag is set
+// (another wait of this GPU gave up). *word gets the last word seen.
+__device__ __forceinline__ uint32_t wait_slot(int push_mode, const unsigned long long* src,
+                                              uint32_t tag, unsigned long long timeout_ns,
+                                              const unsigned int* abort_flag,
+                                              unsigned long long* word, WaitStats& ws) {
+  if (probe_slot(push_mode, src, tag, word)) {
+    ws.fast += 1;
+    return kStatusOk;
+  }
+  uint32_t fail = kStatusOk;
+  const unsigned long long t0 = ptx::globaltimer();
+  // the abort flag and the timer are looked at every 8 probes: each is a
+  // dependent round trip that would otherwise delay seeing the slot arrive
+  for (unsigned n = 1;; ++n) {
+    if (probe_slot(push_mode, src, tag, word)) break;
+    if ((n & 7u) != 0u) continue;
+    if (abort_flag != nullptr && ptx::ld_relaxed_gpu_u32(abort_flag) != 0u) {
+      fail = kStatusAborted;
+      break;
+    }
+    if (ptx::globaltimer() - t0 > timeout_ns) {
+      fail = kStatusTimeout;
+      break;
+    }
+  }
+  ws.slow += 1;
+  ws.ns += ptx::globaltimer() - t0;
+  return fail;
 }
 
 __device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankPtrs& rp,
@@ -199,30 +231,7 @@ __device__ __forceinline__ float poll_slot(const KArgs& a, int rank, const RankP
   if (!active || q == rank) return mine;
   const unsigned long long* src = a.mbox[rank] + slot_index(buf, q, a.tp, a.nmax, row);
   unsigned long long w = 0ull;
-  if (probe_slot(a, src, tag, &w)) {
-    ws.fast += 1;
-    return slot_value(w);
-  }
-  uint32_t fail = kStatusOk;
-  const unsigned long long t0 = ptx::globaltimer();
-  unsigned long long now = t0;
-  // the abort flag and the timer are looked at every 8 probes: each is a
-  // dependent round trip that would otherwise delay seeing the slot arrive
-  for (unsigned n = 1;; ++n) {
-    if (probe_slot(a, src, tag, &w)) break;
-    if ((n & 7u) != 0u) continue;
-    if (ptx::ld_relaxed_gpu_u32(&rp.state->abort) != 0u) {
-      fail = kStatusAborted;
-      break;
-    }
-    now = ptx::globaltimer();
-    if (now - t0 > a.timeout_ns) {
-      fail = kStatusTimeout;
-      break;
-    }
-  }
-  ws.slow += 1;
-  ws.ns += ptx::globaltimer() - t0;
+  const uint32_t fail = wait_slot(a.push_mode, src, tag, a.timeout_ns, &rp.state->abort, &w, ws);
   if (fail == kStatusTimeout) {
     DeviceState* st = rp.state;
     if (atomicCAS(&st->err_code, 0u, (unsigned)kStatusTimeout) == 0u) {

@@ -161,7 +161,6 @@ struct LinearLayout {
 LinearLayout linear_layout(int tp, int64_t nmax, int64_t hidden, int64_t base);
 
 struct LinRank {
-  const void* tmap_a;        // device copies are in LArgs::tmaps; these index them
   void* out;                 // y [rows, hl]
   void* res;                 // residual [rows, hl] (read, rewritten with z) or null
   const void* gamma;         // norm weight [hl]

@@ -1051,7 +1051,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
       } else {
         unsigned long long* dst =
             a.mbox[warp] + slot_index(buf, rank, tp, a.nmax, row0_of(b) + lane);
-        store_slot(a, dst, part, tag);
+        store_slot(a.push_mode, dst, part, tag);
       }
     }
     if (f >= 0 && warp < tp) {   // poll batch f: warp q <- rank q (lanes = rows)

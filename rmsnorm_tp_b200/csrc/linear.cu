@@ -37,8 +37,10 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "device_common.cuh"
 #include "internal.h"
@@ -311,90 +313,97 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 
   // ------------------------------------------------------------------ phase 2
   // Rows [rows * c / G, rows * (c + 1) / G) of this rank's columns; warps take
-  // rows round-robin. Pass A: x = sum of the tp partials (rank order), z = x +
-  // residual, z -> out (scratch), this rank's sum of z^2 pushed to every peer
-  // and kept in its own slot. Pass B: every rank's partial -> S, y from z.
+  // rows round-robin. Pass A: x = sum of the tp partials in rank order,
+  // z = x + residual, z -> out (scratch), this rank's sum of z^2 kept in its own
+  // slot and pushed to every peer. Pass B: every rank's partial -> S, y from z.
   WaitStats ws;
-  const int nwarps = kLinThreads / 32;
+  constexpr int kWarps = kLinThreads / 32;
   const int64_t r_lo = a.rows * (int64_t)blockIdx.x / gridDim.x;
   const int64_t r_hi = a.rows * ((int64_t)blockIdx.x + 1) / gridDim.x;
   const int V = (int)(hl * (int64_t)sizeof(T) / 16);          // 16-byte vectors per row
-  T* out = reinterpret_cast<T*>(rk.out);
-  T* res = reinterpret_cast<T*>(rk.res);
+  unsigned char* outb = reinterpret_cast<unsigned char*>(rk.out);
+  unsigned char* resb = reinterpret_cast<unsigned char*>(rk.res);
   const uint4* gam = reinterpret_cast<const uint4*>(rk.gamma);
   const unsigned char* recv = a.region[rank] + a.recv_off;
   const unsigned int* flags = reinterpret_cast<const unsigned int*>(a.region[rank] + a.flags_off);
-  unsigned long long* mine = reinterpret_cast<unsigned long long*>(a.region[rank]);
-  const bool aborted = s_abort != 0;
+  const unsigned long long* own = reinterpret_cast<const unsigned long long*>(a.region[rank]);
+  const unsigned int* abort_flag = rk.state ? &rk.state->abort : nullptr;
+  const int64_t row_bytes = hl * (int64_t)sizeof(T);
+  bool ok = s_abort == 0;
   int64_t ready_mb = -1;
-  bool flags_ok = !aborted;
-  for (int64_t i = r_lo + warp; i < r_hi && !aborted; i += nwarps) {
+  for (int64_t i = r_lo + warp; i < r_hi && ok; i += kWarps) {
     const int64_t mb = i / kLinTileM;
     if (mb != ready_mb) {   // every rank's tiles of this 128-row block have landed
       const int nflags = tp * (int)a.nblocks;
       const unsigned long long t0 = ptx::globaltimer();
-      for (;;) {
+      for (unsigned n = 0;; ++n) {
         bool all = true;
         for (int f = lane; f < nflags; f += 32) {
           const int src = f / (int)a.nblocks, nbo = f - src * (int)a.nblocks;
-          const unsigned int* fl = flags + (((int64_t)buf * tp + src) * a.mblocks + mb) * a.nblocks + nbo;
+          const unsigned int* fl =
+              flags + (((int64_t)buf * tp + src) * a.mblocks + mb) * a.nblocks + nbo;
           if (ptx::ld_acquire_sys_u32(fl) != tag) all = false;
         }
         if (__all_sync(0xFFFFFFFFu, all)) break;
-        if (ptx::globaltimer() - t0 > a.timeout_ns ||
-            (rk.state && ptx::ld_relaxed_gpu_u32(&rk.state->abort) != 0u)) {
+        bool give_up = false;
+        if ((n & 7u) == 7u)
+          give_up = ptx::globaltimer() - t0 > a.timeout_ns ||
+                    (abort_flag && ptx::ld_relaxed_gpu_u32(abort_flag) != 0u);
+        if (__any_sync(0xFFFFFFFFu, give_up)) {
           if (lane == 0) record_failure(rk.state, rk.host_flag, kStatusTimeout, call);
-          flags_ok = false;
+          ok = false;
           break;
         }
       }
       ready_mb = mb;
+      if (!ok) break;
     }
     float ss = 0.f;
     for (int v = lane; v < V; v += 32) {
-      float accf[8];
+      float acc[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) accf[e] = 0.f;
-      for (int src = 0; src < tp; ++src) {
-        const uint4 p = ptx::ld_stream_v4(recv + (((int64_t)src * a.nmax + i) * hl) * (int64_t)sizeof(T) +
-                                          (int64_t)v * 16);
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int src = 0; src < tp; ++src) {   // rank order: the same sum on every element
+        const uint4 p =
+            ptx::ld_stream_v4(recv + ((int64_t)src * a.nmax + i) * row_bytes + (int64_t)v * 16);
         float pf[8];
         Pack<T>::unpack(p, pf);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) accf[e] += pf[e];
+        for (int e = 0; e < 8; ++e) acc[e] += pf[e];
       }
-      uint4 z = Pack<T>::pack(accf);                       // x, rounded to the dtype
-      uint4* res_v = res ? reinterpret_cast<uint4*>(res + i * hl) + v : nullptr;
-      if (res_v) {
-        z = add16<T>(z, ptx::ld_stream_v4(res_v));         // z = x + residual, rounded
-        ptx::st_v4(res_v, z);
+      uint4 z = Pack<T>::pack(acc);                          // x, rounded to the dtype
+      if (resb) {
+        uint4* rv = reinterpret_cast<uint4*>(resb + i * row_bytes) + v;
+        z = add16<T>(z, ptx::ld_stream_v4(rv));              // z = x + residual, rounded
+        ptx::st_v4(rv, z);
       }
-      ptx::st_v4(reinterpret_cast<uint4*>(out + i * hl) + v, z);
+      ptx::st_v4(reinterpret_cast<uint4*>(outb + i * row_bytes) + v, z);
       ss += sumsq16<T>(z);
     }
     ss = warp_allreduce_sum(ss);
-    if (lane < tp) {
-      unsigned long long* slot = (lane == rank ? mine : a.region[lane] ? reinterpret_cast<unsigned long long*>(a.region[lane]) : mine) +
-                                 slot_index(buf, rank, tp, a.nmax, i);
-      if (lane == rank) {
-        *reinterpret_cast<volatile unsigned long long*>(slot) = pack_slot(ss, tag);
-      } else {
-        store_slot_lin(a.push_mode, slot, ss, tag);
-      }
+    if (lane < tp) {   // lane q: this rank's partial of row i into rank q's slot [buf][rank][i]
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(a.region[lane]) + slot_index(buf, rank, tp, a.nmax, i);
+      if (lane == rank)
+        *reinterpret_cast<volatile unsigned long long*>(dst) = pack_slot(ss, tag);
+      else
+        store_slot(a.push_mode, dst, ss, tag);
     }
-    if (!flags_ok) break;
   }
-  __syncthreads();   // this CTA's own partials (plain stores) are visible to pass B
-  for (int64_t i = r_lo + warp; i < r_hi && !aborted; i += nwarps) {
-    bool failed = !flags_ok;
+  for (int64_t i = r_lo + warp; i < r_hi; i += kWarps) {
+    // the same warp wrote row i in pass A (its own slot: program order)
+    bool failed = !ok || s_abort != 0;
     float val = 0.f;
-    if (lane < tp) {
-      const unsigned long long* src = mine + slot_index(buf, lane, tp, a.nmax, i);
+    if (lane < tp && !failed) {
+      const unsigned long long* src = own + slot_index(buf, lane, tp, a.nmax, i);
       if (lane == rank) {
         val = slot_value(*reinterpret_cast<const volatile unsigned long long*>(src));
-      } else if (!failed) {
-        val = poll_slot_lin(a.push_mode, src, tag, a.timeout_ns, rk.state, failed, ws);
-        if (failed) record_failure(rk.state, rk.host_flag, kStatusTimeout, call);
+      } else {
+        unsigned long long w = 0ull;
+        const uint32_t f = wait_slot(a.push_mode, src, tag, a.timeout_ns, abort_flag, &w, ws);
+        if (f == kStatusTimeout) record_failure(rk.state, rk.host_flag, kStatusTimeout, call);
+        if (f != kStatusOk) failed = true;
+        val = slot_value(w);
       }
     }
     failed = __any_sync(0xFFFFFFFFu, failed);
@@ -402,11 +411,125 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     for (int q = 0; q < tp; ++q) S += __shfl_sync(0xFFFFFFFFu, val, q);
     const float inv = failed ? quiet_nan() : rsqrtf(S / (float)a.hidden + a.eps);
     for (int v = lane; v < V; v += 32) {
-      uint4* yv = reinterpret_cast<uint4*>(out + i * hl) + v;
+      uint4* yv = reinterpret_cast<uint4*>(outb + i * row_bytes) + v;
       ptx::st_v4(yv, normalize16<T>(ptx::ld_stream_v4(yv), ptx::ld_cached_v4(gam + v), inv));
     }
   }
   if (exchange) finish_launch(rk.state, call);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+LinearLayout linear_layout(int tp, int64_t nmax, int64_t hidden, int64_t base) {
+  LinearLayout L{};
+  L.mblocks = (nmax + kLinTileM - 1) / kLinTileM;
+  L.nblocks = hidden / tp / kLinTileN;
+  L.flags_off = (base + 1023) & ~(int64_t)1023;
+  const int64_t flag_bytes = 2 * (int64_t)tp * L.mblocks * L.nblocks * 4;
+  L.recv_off = (L.flags_off + flag_bytes + 1023) & ~(int64_t)1023;
+  L.bytes = L.recv_off + (int64_t)tp * nmax * (hidden / tp) * 2;
+  return L;
+}
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+EncodeTiledFn encode_tiled(cudaError_t* err) {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  static cudaError_t e0 = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    e0 = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e0 == cudaSuccess && (q != cudaDriverEntryPointSuccess || p == nullptr))
+      e0 = cudaErrorNotSupported;
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  *err = e0;
+  return fn;
+}
+
+// Row-major [outer][inner] 16-bit matrix, boxes of box_outer rows x 64 elements
+// (128 bytes, the 128-byte swizzle); zeros outside the matrix.
+cudaError_t encode_2d(EncodeTiledFn fn, unsigned char* out, const void* base, int dtype,
+                      uint64_t inner, uint64_t outer, uint32_t box_outer) {
+  CUtensorMap* m = reinterpret_cast<CUtensorMap*>(out);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kLinTileK, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_lin_attr[kMaxDevices][2];
+}  // namespace
+
+static_assert(sizeof(CUtensorMap) == 128, "a tensor map is 128 bytes");
+static_assert(offsetof(LArgs, tmaps) % 64 == 0, "tensor maps 64-byte aligned in the parameters");
+
+cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws, int dtype,
+                          int device, int grid_y, cudaStream_t stream) {
+  cudaError_t err = cudaSuccess;
+  const EncodeTiledFn fn = encode_tiled(&err);
+  if (err != cudaSuccess) return err;
+  const int nranks = a.emulated ? grid_y : 1;
+  for (int r = 0; r < nranks; ++r) {
+    err = encode_2d(fn, a.tmaps[2 * r], as[r], dtype, (uint64_t)a.k, (uint64_t)a.rows, kLinTileM);
+    if (err != cudaSuccess) return err;
+    err = encode_2d(fn, a.tmaps[2 * r + 1], ws[r], dtype, (uint64_t)a.k, (uint64_t)a.hidden,
+                    kLinTileN);
+    if (err != cudaSuccess) return err;
+  }
+  const void* kfn = dtype == kBF16
+                        ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half>);
+  const int ti = dtype == kBF16 ? 0 : 1;
+  const bool cacheable = device >= 0 && device < kMaxDevices;
+  if (!cacheable || g_lin_attr[device][ti].load() == 0) {
+    err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLinSmem);
+    if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared);
+    if (err != cudaSuccess) return err;
+    if (cacheable) g_lin_attr[device][ti].store(1);
+  }
+  int per_sm = 0, sms = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kLinThreads, kLinSmem);
+  if (err != cudaSuccess) return err;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return err;
+  const int64_t resident = (int64_t)per_sm * sms / (grid_y > 1 ? grid_y : 1);
+  const int64_t tiles = ((a.rows + kLinTileM - 1) / kLinTileM) * (a.hidden / kLinTileN);
+  int64_t grid = tiles < resident ? tiles : resident;
+  if (grid < 1) return cudaErrorCooperativeLaunchTooLarge;
+  a.push_mode = get_push_mode();
+  void* args[] = {&a};
+  const dim3 g3((unsigned)grid, (unsigned)grid_y), blk(kLinThreads);
+  if (grid_y > 1) return cudaLaunchCooperativeKernel(kfn, g3, blk, args, kLinSmem, stream);
+  if (!get_dependent_launch()) return cudaLaunchKernel(kfn, g3, blk, args, kLinSmem, stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g3;
+  cfg.blockDim = blk;
+  cfg.dynamicSmemBytes = kLinSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kfn, args);
 }
 
 }  // namespace rtp

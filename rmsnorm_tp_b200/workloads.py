@@ -89,3 +89,24 @@ def algorithmic_bytes(rows: int, local_hidden: int, dtype: torch.dtype) -> int:
     """HBM bytes one rank must move per call: read x, write y, read the weight once."""
     s = torch.tensor([], dtype=dtype).element_size()
     return 2 * rows * local_hidden * s + local_hidden * s
+
+
+def make_linear_group(rows: int, k_local: int, hidden: int, tp: int, dtype: torch.dtype,
+                      seed: int, *, device: str = "cpu"):
+    """Inputs of the fused row-parallel linear for every rank: a_r [rows, k_local]
+    ~ N(0, 1), the linear weight slice lw_r [hidden, k_local] ~ N(0, 1 / (k_local * tp))
+    (unit-variance outputs after the sum over ranks), and the norm weight slice
+    g_r [hidden / tp] ~ 1 + 0.1 N(0, 1); each rank from a generator seeded seed + rank."""
+    if hidden % tp:
+        raise ValueError(f"hidden {hidden} is not divisible by tp {tp}")
+    as_, lws, gs = [], [], []
+    scale = (k_local * tp) ** -0.5
+    for r in range(tp):
+        g = torch.Generator(device=device).manual_seed(seed + r)
+        a = torch.randn(rows, k_local, generator=g, device=device, dtype=torch.float32)
+        w = scale * torch.randn(hidden, k_local, generator=g, device=device, dtype=torch.float32)
+        gm = 1.0 + 0.1 * torch.randn(hidden // tp, generator=g, device=device, dtype=torch.float32)
+        as_.append(a.to(dtype))
+        lws.append(w.to(dtype))
+        gs.append(gm.to(dtype))
+    return as_, lws, gs
