@@ -97,6 +97,10 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the untimed parity check (profiling runs)")
+    ap.add_argument("--op", choices=["norm", "linear"], default="norm",
+                    help="linear: the fused row-parallel linear -> reduce-scatter -> TP RMSNorm "
+                         "(Llama-70B o_proj rows: hidden 8192, in-features 8192 split over N), "
+                         "one JSON line per row count, beside the unfused torch + NCCL pipeline")
     ap.add_argument("--sweep", choices=["none", "decode", "prefill", "llama", "all"], default="none")
     ap.add_argument("--out", default=None, help="JSON-lines file for sweep points")
     ap.add_argument("--rows", type=int, default=None,
@@ -470,6 +474,9 @@ def kernel_name(rtp, rows, hl, tp, dtype=torch.bfloat16):
     p = rtp.plan(rows, hl, dtype, tp=tp)
     v = p["variant"]
     dt = DTYPE_NAME[dtype]
+    if v >= 600:
+        return (f"tp_rmsnorm_vec_resident_kernel<{dt},{p['vec_per_lane']},{p['team_warps']},"
+                f"{p['rows_per_tile']},{p['block_threads']}> up to {p['depth']} tiles per team")
     if v >= 500:
         return (f"tp_rmsnorm_batch_kernel<{dt},{p['block_threads'] // 32} warps> "
                 f"{p['rows_per_tile']} rows/batch, {p['vec_per_lane']} slots")
@@ -1049,10 +1056,108 @@ def probe_roundtrip(mod, rank, tp, iters=2000):
     return v if rank == 0 and v > 0 else (None if rank == 0 else v)
 
 
+LINEAR_PEAK_NVLINK_GBS = 770.0   # measured peer-copy bandwidth per direction per GPU on this pool
+
+
+def measured_peak_tflops():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_linear_bench(args):
+    """--op linear: the fused row-parallel linear -> reduce-scatter -> TP RMSNorm
+    at TP = N on Llama-70B o_proj rows (in-features 8192 split over the ranks,
+    hidden 8192, bf16), per row count: our one kernel (CUDA graph and eager) and
+    the unfused pipeline a Megatron-style block runs (cuBLAS GEMM, NCCL
+    reduce-scatter of the column blocks, the reference's AllReduce norm), with a
+    parity check of our output against that pipeline's on the first rows."""
+    import rmsnorm_tp_b200 as rtp
+    from oracle import torch_port
+
+    rtp.set_push_mode(args.push_mode)
+    world, rank, local = dist_env()
+    group = setup_group(world, local)
+    dev = torch.device("cuda", local)
+    wl = load_workloads()
+    tp, hidden, k_total, dtype, eps = world, args.hidden or 8192, 8192, torch.bfloat16, 1e-5
+    k = k_total // tp
+    hl = hidden // tp
+    rows_list = [args.rows] if args.rows else [1, 16, 128, 1024, 4096, 8192]
+    m = rtp.FusedTPLinearRMSNorm(hidden, eps=eps, tp_group=group, num_max_rows=max(rows_list))
+    peak_tf, peak_kind = measured_peak_tflops()
+    for rows in rows_list:
+        as_, lws, gs = wl.make_linear_group(rows, k, hidden, tp, dtype, 3000 + rows)
+        a, w, g = as_[rank].to(dev), lws[rank].to(dev), gs[rank].to(dev)
+        out = torch.empty(rows, hl, dtype=dtype, device=dev)
+
+        def ours(_i):
+            m.forward(a, w, g, out=out)
+
+        def unfused(_i):
+            p = a @ w.t()                                         # cuBLAS
+            if tp > 1:
+                blocks = p.view(rows, tp, hl).transpose(0, 1).contiguous()
+                x = torch.empty(rows, hl, dtype=dtype, device=dev)
+                dist.reduce_scatter_tensor(x, blocks, group=group)
+                return torch_port.allreduce_path_dist(x, g, eps, group)
+            return torch_port.allreduce_path_group([p], [g], eps)[0]
+
+        steps = 200 if rows <= 1024 else 50
+        for i in range(5):
+            ours(i)
+            unfused(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        eager_ms = max_over_ranks([time_steps(ours, steps)], world)[0] / steps
+        graph_ms, _ = time_graph(ours, min(steps, 50), steps, world)
+        if world > 1:
+            dist.barrier()
+        unf_ms = max_over_ranks([time_steps(unfused, steps)], world)[0] / steps
+        # parity: our output against the unfused pipeline's on this rank's columns
+        ours(0)
+        ref = unfused(0).to(dtype)
+        torch.cuda.synchronize()
+        diff = (out.float() - ref.float()).abs()
+        bad = int((diff > 1e-2 + 1.6e-2 * ref.float().abs()).sum())
+        bad = int(max_over_ranks([float(bad)], world)[0])
+        flops = 2.0 * rows * k * hidden
+        nvl = (tp - 1) / tp * rows * hidden * 2
+        t_gemm = flops / (peak_tf * 1e12)
+        t_nvl = nvl / (LINEAR_PEAK_NVLINK_GBS * 1e9)
+        bound = max(t_gemm, t_nvl)
+        rec = {"op": "linear_rs_rmsnorm", "tp": tp, "rows": rows, "k_local": k, "hidden": hidden,
+               "dtype": "bf16", "push_mode": rtp.get_push_mode(),
+               "graph_us_per_call": round(graph_ms * 1e3, 3),
+               "eager_us_per_call": round(eager_ms * 1e3, 3),
+               "unfused_eager_us_per_call": round(unf_ms * 1e3, 3),
+               "speedup_vs_unfused": round(unf_ms / graph_ms, 3),
+               "tflops_per_rank": round(flops / (graph_ms * 1e-3) / 1e12, 1),
+               "nvlink_GBps_per_rank": round(nvl / (graph_ms * 1e-3) / 1e9, 1),
+               "roofline": {"bound": "tensor" if t_gemm >= t_nvl else "nvlink",
+                            "floor_us": round(bound * 1e6, 3),
+                            "frac": round(bound / (graph_ms * 1e-3), 4),
+                            "peak_tflops": peak_tf, "peak_kind": peak_kind,
+                            "nvlink_GBps": LINEAR_PEAK_NVLINK_GBS},
+               "parity_vs_unfused": {"bad": bad, "max_abs": round(float(diff.max()), 5)}}
+        emit(args, rank, rec)
+    m.destroy()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.op == "linear":
+        return run_linear_bench(args)
     return run_our_arm(args)
 
 
