@@ -339,7 +339,30 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
       push_slot(a, rank, buf, tag, tt * kRows + lr, lq, lr < nrows_of(tt), mine_of(ss[d]));
   }
 
-  // poll, normalise and store every tile
+  // one look at every tile's slot, all loads issued back to back (independent
+  // round trips), so that partials that have already arrived cost one round
+  // trip for the whole team instead of one per tile
+  // (packed encoding: the raw words first, the tag tests after, so that no test
+  // waits between two loads; the release encoding's acquire must precede its
+  // value read, so it polls tile by tile)
+  unsigned long long seen[kDepth];
+  bool have[kDepth];
+  if (kW == 1 || wit == 0) {
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) {
+      const int64_t tt = first + d * stride;
+      const bool remote = tt < tiles && lr < nrows_of(tt) && lq != rank;
+      seen[d] = remote && a.push_mode == kPushPacked
+                    ? ptx::ld_relaxed_sys_u64(a.mbox[rank] +
+                                              slot_index(buf, lq, tp, a.nmax, tt * kRows + lr))
+                    : 0ull;
+      have[d] = !remote;
+    }
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d)
+      if (!have[d] && a.push_mode == kPushPacked) have[d] = slot_tag(seen[d]) == tag;
+  }
+  // poll (what has not arrived yet), normalise and store every tile
 #pragma unroll
   for (int d = 0; d < kDepth; ++d) {
     const int64_t tt = first + d * stride;
@@ -348,8 +371,16 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
     bool ok = true;
     if (kW == 1 || wit == 0) {
       bool failed = false;
-      const float val = poll_slot(a, rank, rp, buf, tag, call, tt * kRows + lr, lq,
-                                  lr < nrows_of(tt), mine_of(ss[d]), failed, ws);
+      const bool active = lr < nrows_of(tt);
+      float val;
+      if (!active || lq == rank) {
+        val = mine_of(ss[d]);
+      } else if (have[d]) {
+        ws.fast += 1;
+        val = slot_value(seen[d]);
+      } else {
+        val = poll_slot(a, rank, rp, buf, tag, call, tt * kRows + lr, lq, true, 0.f, failed, ws);
+      }
       ok = !__any_sync(0xFFFFFFFFu, failed);
 #pragma unroll
       for (int i = 0; i < kRows; ++i) {
@@ -803,6 +834,18 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   };
 
   // poll tile kk's remote partials, normalise and store it, refill its stage
+  // the slot word of the next tile to finish, loaded one reduction ahead of its
+  // use (packed encoding), so that its round trip overlaps that reduction
+  unsigned long long pre_word = 0ull;
+  int64_t pre_tile = -1;
+  auto prefetch = [&](int64_t kk) {
+    pre_tile = kk;
+    const bool remote = lr < nrows_of(kk) && lq != rank && a.push_mode == kPushPacked;
+    pre_word = remote ? ptx::ld_relaxed_sys_u64(a.mbox[rank] +
+                                                slot_index(buf, lq, tp, a.nmax, row0_of(kk) + lr))
+                      : 0ull;
+  };
+
   auto finish = [&](int64_t kk) {
     const int64_t row0 = row0_of(kk);
     const int nr = nrows_of(kk);
@@ -810,8 +853,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if (exchange) {
       const bool active = lr < nr;
       bool failed = false;
-      const float val = poll_slot(a, rank, rp, buf, tag, call, row0 + lr, lq, active,
-                                  active ? s_part[warp][kk % kStages][lr] : 0.f, failed, ws);
+      float val;
+      if (active && lq != rank && pre_tile == kk && a.push_mode == kPushPacked &&
+          slot_tag(pre_word) == tag) {
+        ws.fast += 1;
+        val = slot_value(pre_word);
+      } else {
+        val = poll_slot(a, rank, rp, buf, tag, call, row0 + lr, lq, active,
+                        active ? s_part[warp][kk % kStages][lr] : 0.f, failed, ws);
+      }
       ok = !__any_sync(0xFFFFFFFFu, failed);
       float S = 0.f;
       for (int p = 0; p < tp; ++p) S += __shfl_sync(0xFFFFFFFFu, val, lr * tp + p);
@@ -861,6 +911,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       load_ok = false;
       break;
     }
+    if (exchange && k + 1 - f > lag) prefetch(f);   // f is finished in this iteration
     reduce(k);
     if (exchange) push(k);
     // finish tiles only `lag` tiles behind: their NVLink round trips (TP > 1)
