@@ -101,6 +101,10 @@ def parse_args(argv=None):
                     help="linear: the fused row-parallel linear -> reduce-scatter -> TP RMSNorm "
                          "(Llama-70B o_proj rows: hidden 8192, in-features 8192 split over N), "
                          "one JSON line per row count, beside the unfused torch + NCCL pipeline")
+    ap.add_argument("--emulated-tp", type=int, default=0,
+                    help="profiling on one GPU: every rank of a TP group of this size in one "
+                         "cooperative launch (the workload's rows, hidden split over the ranks), "
+                         "--steps calls, one line with the per-call time (not a bench line)")
     ap.add_argument("--sweep", choices=["none", "decode", "prefill", "llama", "all"], default="none")
     ap.add_argument("--out", default=None, help="JSON-lines file for sweep points")
     ap.add_argument("--rows", type=int, default=None,
@@ -1152,12 +1156,46 @@ def run_linear_bench(args):
     return 0
 
 
+def run_emulated(args):
+    """--emulated-tp N: every rank of a TP group of N on one GPU in one cooperative
+    launch, the workload's rows and hidden split over the ranks; for ncu captures
+    of the exchange kernels without several GPUs (not a bench line: the ranks
+    share one GPU's SMs and HBM, and the exchange never crosses NVLink)."""
+    import rmsnorm_tp_b200 as rtp
+
+    rtp.set_kernel_family(args.family)
+    rtp.set_push_mode(args.push_mode)
+    torch.cuda.set_device(0)
+    w = workload_of(args)
+    tp = args.emulated_tp
+    wl = load_workloads()
+    xs, ws = wl.make_group(w["rows"], w["hidden"], tp, w["dtype"], w["seed_base"], device="cuda")
+    g = rtp.EmulatedTPGroup(tp, eps=w["eps"], num_max_rows=w["rows"], timeout_s=5.0)
+    outs = [torch.empty_like(x) for x in xs]
+    try:
+        for _ in range(max(args.warmup, 1)):
+            g.forward(xs, ws, outs=outs)
+        torch.cuda.synchronize()
+        ms = time_steps(lambda i: g.forward(xs, ws, outs=outs), args.steps)
+        ok = all(b.poll_error() == 0 for b in g.bufs)
+    finally:
+        g.destroy()
+    print(json.dumps({"emulated_tp": tp, "rows": w["rows"], "hidden": w["hidden"],
+                      "dtype": DTYPE_NAME[w["dtype"]], "steps": args.steps,
+                      "us_per_call": round(ms * 1e3 / args.steps, 3),
+                      "kernel": kernel_name(rtp, w["rows"], w["hidden"] // tp, tp, w["dtype"]),
+                      "device_errors": not ok}), flush=True)
+    return 0 if ok else 1
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference_arm(args)
     if args.op == "linear":
         return run_linear_bench(args)
+    if args.emulated_tp:
+        return run_emulated(args)
     return run_our_arm(args)
 
 

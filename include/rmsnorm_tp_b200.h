@@ -310,8 +310,9 @@ int rmsnorm_tp_probe_roundtrip(rmsnorm_tp_comm* comm, int peer, int iters,
  * <= 16 KB; at TP = 1: the local register kernels, bulk-copy kernels from
  * 256 MiB of x), 1 = register kernels only, 2 = bulk-copy kernels wherever
  * eligible (aligned rows of <= 16 KB), 3 = batch kernels wherever eligible
- * (aligned rows of <= 16 KB, TP = 1 included). For tests and benchmarks that
- * compare the implementations. */
+ * (aligned rows of <= 16 KB, TP = 1 included). Family 2 also makes the backward
+ * use its one-CTA-per-row kernel instead of the register kernel. For tests and
+ * benchmarks that compare the implementations. */
 int rmsnorm_tp_set_kernel_family(int family);
 int rmsnorm_tp_get_kernel_family(void);
 

@@ -180,6 +180,235 @@ __global__ void __launch_bounds__(kBlock)
   flush_stats(a, wst, t_start);
 }
 
+// ---------------------------------------------------------------------------
+// Register backward (aligned rows of up to 2048 16-byte vectors): the forward's
+// teams and column mapping. A team of kW warps owns whole rows; lane l of warp
+// wit holds the row's vectors c = (j * kW + wit) * 32 + l, j < kVec, of x and dy
+// in registers, for kChunk rows at a time (all their loads in flight at once).
+// Per chunk: S and D of every row in one pass (team reduction), the exchange
+// (every row's S pushed, every S polled, then every D pushed and polled --
+// a row's D is pushed only after its S exchange completed), then dx from the
+// registers and dw accumulated per lane in fp32 registers (the lane's own
+// columns, every row of the team). At the end the teams of a CTA add their dw
+// partials into shared memory in team order, and the CTA writes its row of the
+// workspace; backward_dw_reduce_kernel sums the rows in order (deterministic).
+// x and dy are read once from HBM.
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kBlock, int kMinBlocks, int kChunk>
+__global__ void __launch_bounds__(kBlock, kMinBlocks)
+    tp_rmsnorm_backward_vec_kernel(const __grid_constant__ BArgs b) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  constexpr int kE = Pack<T>::kE;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const KArgs& a = b.k;
+  extern __shared__ float s_dw[];                    // [hl]: the CTA's dw partial
+  __shared__ float s_red[kTeams][kChunk][kW][2];
+  __shared__ float s_tot[kTeams][kChunk][3];         // S, D, ok
+  const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
+  WaitStats wst;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const int ri = a.emulated ? (int)blockIdx.y : 0;
+  const int rank = a.emulated ? (int)blockIdx.y : a.rank;
+  const RankPtrs& rp = a.rp[ri];
+  const int64_t V = a.hl / kE;
+  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  const uint4* __restrict__ dyg = ptx::launder(reinterpret_cast<const uint4*>(b.dy[ri]));
+  uint4* __restrict__ dxg = reinterpret_cast<uint4*>(rp.out);
+  const bool exchange = a.tp > 1;
+  const int tp = a.tp;
+
+  unsigned long long call = 0ull;
+  uint32_t buf0 = 0u, tag0 = 0u, buf1 = 0u, tag1 = 0u;
+  if (exchange) {
+    call = read_generation(rp.state);
+    buf0 = buffer_of(call);
+    tag0 = tag_of(call);
+    buf1 = buffer_of(call + 1ull);
+    tag1 = tag_of(call + 1ull);
+  }
+
+  float dw[kVec][kE];
+#pragma unroll
+  for (int j = 0; j < kVec; ++j)
+#pragma unroll
+    for (int e = 0; e < kE; ++e) dw[j][e] = 0.f;
+
+  const int64_t teams_total = (int64_t)gridDim.x * kTeams;
+  const int64_t tg = (int64_t)blockIdx.x * kTeams + team;
+  bool all_ok = true;
+  // the team's rows: tg, tg + TT, tg + 2 TT, ... in chunks of kChunk
+  for (int64_t base = tg; base < a.rows; base += (int64_t)kChunk * teams_total) {
+    uint4 xv[kChunk][kVec], dv[kChunk][kVec];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const int64_t row = base + i * teams_total;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        const bool in = row < a.rows && c < V;
+        xv[i][j] = in ? ptx::ld_stream_v4(xg + row * V + c) : make_uint4(0u, 0u, 0u, 0u);
+        dv[i][j] = in ? ptx::ld_stream_v4(dyg + row * V + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    // S = sum x^2 and D = sum dy * w * x of every row of the chunk
+    float S[kChunk], D[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      float s = 0.f, d = 0.f;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        if (c < V) {
+          float xf[kE], df[kE], wf[kE];
+          Pack<T>::unpack(xv[i][j], xf);
+          Pack<T>::unpack(dv[i][j], df);
+          Pack<T>::unpack(ptx::ld_cached_v4(wg + c), wf);
+#pragma unroll
+          for (int e = 0; e < kE; ++e) {
+            s = fmaf(xf[e], xf[e], s);
+            d = fmaf(df[e] * wf[e], xf[e], d);
+          }
+        }
+      }
+      S[i] = warp_allreduce_sum(s);
+      D[i] = warp_allreduce_sum(d);
+    }
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          s_red[team][i][wit][0] = S[i];
+          s_red[team][i][wit][1] = D[i];
+        }
+      }
+      ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        float s = 0.f, d = 0.f;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) {
+          s += s_red[team][i][w][0];
+          d += s_red[team][i][w][1];
+        }
+        S[i] = s;
+        D[i] = d;
+      }
+    }
+    bool ok[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) ok[i] = true;
+    if (exchange) {
+      if (kW == 1 || wit == 0) {
+        // lane q < tp serves rank q: every row's S, then every row's D
+        const bool lq = lane < tp;
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const int64_t row = base + i * teams_total;
+          push_slot(a, rank, buf0, tag0, row, lane, lq && row < a.rows, S[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const int64_t row = base + i * teams_total;
+          bool failed = false;
+          const float v = poll_slot(a, rank, rp, buf0, tag0, call, row, lane, lq && row < a.rows,
+                                    S[i], failed, wst);
+          ok[i] = !__any_sync(0xFFFFFFFFu, failed);   // every S poll ended before any D push
+          float t = 0.f;
+          for (int p = 0; p < tp; ++p) t += __shfl_sync(0xFFFFFFFFu, v, p);
+          S[i] = t;
+        }
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const int64_t row = base + i * teams_total;
+          push_slot(a, rank, buf1, tag1, row, lane, lq && row < a.rows, D[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const int64_t row = base + i * teams_total;
+          bool failed = false;
+          const float v = poll_slot(a, rank, rp, buf1, tag1, call + 1ull, row, lane,
+                                    lq && row < a.rows, D[i], failed, wst);
+          ok[i] = !__any_sync(0xFFFFFFFFu, failed) && ok[i];
+          float t = 0.f;
+          for (int p = 0; p < tp; ++p) t += __shfl_sync(0xFFFFFFFFu, v, p);
+          D[i] = t;
+        }
+      }
+      if constexpr (kW > 1) {
+        if (wit == 0 && lane == 0) {
+#pragma unroll
+          for (int i = 0; i < kChunk; ++i) {
+            s_tot[team][i][0] = S[i];
+            s_tot[team][i][1] = D[i];
+            s_tot[team][i][2] = ok[i] ? 1.f : 0.f;
+          }
+        }
+        ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          S[i] = s_tot[team][i][0];
+          D[i] = s_tot[team][i][1];
+          ok[i] = s_tot[team][i][2] != 0.f;
+        }
+      }
+    }
+    // dx from the registers; dw partial of the lane's columns
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const int64_t row = base + i * teams_total;
+      if (row >= a.rows) break;
+      if (!ok[i]) all_ok = false;
+      const float inv = ok[i] ? rsqrtf(S[i] / a.hidden_f + a.eps) : quiet_nan();
+      const float coef = (inv * inv * inv) * (D[i] / a.hidden_f);
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        if (c < V) {
+          float xf[kE], df[kE], wf[kE], o[kE];
+          Pack<T>::unpack(xv[i][j], xf);
+          Pack<T>::unpack(dv[i][j], df);
+          Pack<T>::unpack(ptx::ld_cached_v4(wg + c), wf);
+#pragma unroll
+          for (int e = 0; e < kE; ++e) {
+            o[e] = inv * (df[e] * wf[e]) - xf[e] * coef;
+            dw[j][e] += (df[e] * xf[e]) * inv;
+          }
+          ptx::st_v4(dxg + row * V + c, Pack<T>::pack(o));
+        }
+      }
+    }
+  }
+  (void)all_ok;
+  // the teams' dw partials into shared memory in team order, then the CTA's row
+  // of the workspace
+  for (int t = 0; t < kTeams; ++t) {
+    if (team == t) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int c = (j * kW + wit) * 32 + lane;
+        if (c < V) {
+#pragma unroll
+          for (int e = 0; e < kE; ++e) {
+            float* p = s_dw + (int64_t)c * kE + e;
+            *p = (t == 0 ? 0.f : *p) + dw[j][e];
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  float* wsr = b.ws[ri] + (int64_t)blockIdx.x * a.hl;
+  for (int64_t i = threadIdx.x; i < a.hl; i += kBlock) wsr[i] = s_dw[i];
+  if (exchange) finish_launch(rp.state, call, 2ull);
+  flush_stats(a, wst, t_start);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
     backward_dw_reduce_kernel(const float* __restrict__ ws, int parts, int64_t hl,
@@ -214,6 +443,43 @@ BwdFn backward_fn(int dtype, bool vec16) {
 constexpr int kMaxDevices = 64;
 std::atomic<unsigned int> g_smem_set[kMaxDevices][3][2];   // max dynamic smem raised to this
 
+// Register backward shapes by 16-byte vectors per row V: the first whose capacity
+// 32 * kW * kVec >= V (kVec, kW, block, CTAs per SM), two rows in flight per team.
+struct BwdShape {
+  int vec, w, block;
+};
+constexpr BwdShape kBwdShapes[] = {{1, 1, 256}, {2, 1, 256}, {4, 1, 256}, {4, 2, 256},
+                                   {4, 4, 256}, {4, 8, 256}, {4, 16, 512}};
+constexpr int kNumBwdShapes = sizeof(kBwdShapes) / sizeof(kBwdShapes[0]);
+// rows in flight per team: two, but one for 16-bit rows of 4 vectors per lane,
+// whose 32 fp32 dw accumulators and two rows of x and dy exceed 128 registers
+template <typename T, int kVec>
+constexpr int bwd_chunk() {
+  return (sizeof(T) == 2 && kVec == 4) ? 1 : 2;
+}
+
+template <typename T>
+struct BwdVecTable {
+#define RTP_BWD(V, W, B, M) tp_rmsnorm_backward_vec_kernel<T, V, W, B, M, bwd_chunk<T, V>()>
+  static constexpr BwdFn fn[kNumBwdShapes] = {
+      RTP_BWD(1, 1, 256, 2), RTP_BWD(2, 1, 256, 2), RTP_BWD(4, 1, 256, 2), RTP_BWD(4, 2, 256, 2),
+      RTP_BWD(4, 4, 256, 2), RTP_BWD(4, 8, 256, 2), RTP_BWD(4, 16, 512, 1),
+  };
+#undef RTP_BWD
+};
+
+BwdFn backward_vec_fn(int dtype, int shape) {
+  switch (dtype) {
+    case kF32:
+      return BwdVecTable<float>::fn[shape];
+    case kBF16:
+      return BwdVecTable<__nv_bfloat16>::fn[shape];
+    default:
+      return BwdVecTable<__half>::fn[shape];
+  }
+}
+std::atomic<unsigned int> g_vec_smem_set[kMaxDevices][3][kNumBwdShapes];
+
 }  // namespace
 
 cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, cudaStream_t stream,
@@ -229,20 +495,30 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
                            reinterpret_cast<uintptr_t>(b.dy[r]);
     if (bits & 15u) vec16 = false;
   }
-  const BwdFn fn = backward_fn(dtype, vec16);
+  // the register kernel for aligned rows of up to 2048 vectors (unless the
+  // bulk family is forced, which keeps the one-CTA-per-row kernel for comparison)
+  const int64_t V = vec16 ? a.hl * eb / 16 : 0;
+  int shape = -1;
+  if (vec16 && get_family() != kFamilyBulk)
+    for (int i = 0; i < kNumBwdShapes && shape < 0; ++i)
+      if (V <= 32ll * kBwdShapes[i].w * kBwdShapes[i].vec) shape = i;
+  const BwdFn fn = shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
+  const int block = shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
   const void* fp = reinterpret_cast<const void*>(fn);
   const size_t smem = (size_t)a.hl * sizeof(float);
   cudaError_t err;
   if (smem > 48u * 1024u) {
     const bool cacheable = device >= 0 && device < kMaxDevices;
-    if (!cacheable || g_smem_set[device][dtype][vec16 ? 1 : 0].load() < smem) {
+    std::atomic<unsigned int>& set = shape >= 0 ? g_vec_smem_set[device][dtype][shape]
+                                                : g_smem_set[device][dtype][vec16 ? 1 : 0];
+    if (!cacheable || set.load() < smem) {
       err = cudaFuncSetAttribute(fp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (err != cudaSuccess) return err;
-      if (cacheable) g_smem_set[device][dtype][vec16 ? 1 : 0].store((unsigned)smem);
+      if (cacheable) set.store((unsigned)smem);
     }
   }
   int per_sm = 0, sms = 0;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp, kBwdBlock, smem);
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp, block, smem);
   if (err != cudaSuccess) return err;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return err;
@@ -254,7 +530,7 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   BArgs bb = b;
   bb.k.push_mode = get_push_mode();
   void* args[] = {&bb};
-  const dim3 g3((unsigned)grid, (unsigned)grid_y), blk(kBwdBlock);
+  const dim3 g3((unsigned)grid, (unsigned)grid_y), blk((unsigned)block);
   if (grid_y > 1) return cudaLaunchCooperativeKernel(fp, g3, blk, args, smem, stream);
   if (!get_dependent_launch()) return cudaLaunchKernel(fp, g3, blk, args, smem, stream);
   cudaLaunchAttribute attr[1];

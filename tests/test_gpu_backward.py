@@ -35,10 +35,19 @@ def _check(dtype, xs, ws, dys, dxs, dws, eps):
         assert r["ok"], f"dw rank {k}: {r}"
 
 
+@pytest.fixture(params=["auto", "bulk"])
+def bwd_family(request):
+    """The register backward kernel (automatic choice for aligned rows) and the
+    one-CTA-per-row kernel (kept under the bulk family)."""
+    rtp.set_kernel_family(request.param)
+    yield request.param
+    rtp.set_kernel_family("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("hidden", [37, 96, 512, 4096, 8192])
+@pytest.mark.parametrize("hidden", [37, 96, 512, 4096, 8192, 16384])
 @pytest.mark.parametrize("rows", [1, 7, 300, 2500])
-def test_local_backward(dtype, hidden, rows):
+def test_local_backward(bwd_family, dtype, hidden, rows):
     xs, ws, dys = _inputs(rows, hidden, 1, dtype, 13)
     dx, dw = rtp.local_rmsnorm_backward(dys[0], xs[0], ws[0], 1e-6)
     torch.cuda.synchronize()
@@ -51,7 +60,7 @@ def test_local_backward(dtype, hidden, rows):
 @pytest.mark.parametrize("tp", [2, 4, 8])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("hl,rows", [(64, 5), (512, 300), (2048, 1), (37, 40), (1024, 129)])
-def test_emulated_group_backward_between_forwards(tp, dtype, hl, rows):
+def test_emulated_group_backward_between_forwards(bwd_family, tp, dtype, hl, rows):
     """forward, backward, forward on one group: the backward takes two
     generations and the calls around it still meet their peers."""
     xs, ws, dys = _inputs(rows, hl * tp, tp, dtype, 23)
