@@ -66,9 +66,15 @@ DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"
 # forward kernel on the benchmark workload, from ncu captures of this bench
 # command: several consecutive launches over the rotating sets with
 # --cache-control none, summed and divided by the launches, so that each
-# launch is charged the write-back of its y. Key: (workload, TP, dtype).
-# Absent keys are reported as null.
-TRAFFIC = {}
+# launch is charged the write-back of its y. Key: (workload, TP, dtype) ->
+# (bytes, source). Absent keys are reported as null.
+TRAFFIC = {
+    # 5 launches of rmsnorm_local_vec_kernel<bf16,4,4,1,256,2,3>: read 33562010 B,
+    # write 31476326 B per launch (algorithmic 67117056 B: 0.97)
+    ("llama3_8b", 1, "bf16"): (65038336, "ncu, 5 consecutive launches of this bench command "
+                               "(--steps 20 --warmup 5), --cache-control none, mean of "
+                               "dram__bytes_read.sum + dram__bytes_write.sum"),
+}
 
 
 def parse_args(argv=None):

@@ -51,15 +51,24 @@
 namespace rtp {
 
 namespace {
-constexpr int kLinStages = 4;
 constexpr int kLinThreads = 192;
-constexpr uint32_t kLinTileBytes = kLinTileM * kLinTileK * 2;       // 16 KB (A); W the same
-constexpr uint32_t kLinStageBytes = 2 * kLinTileBytes;
-constexpr uint32_t kLinPitch = kLinTileN * 2 + 16;                  // staging row: 256 + 16 bytes
-constexpr uint32_t kLinStagingBytes = kLinTileM * kLinPitch;
-constexpr uint32_t kLinSmem = 1024 + kLinStages * kLinStageBytes + kLinStagingBytes;
-constexpr uint32_t kLinTmemCols = 2 * kLinTileN;
+constexpr uint32_t kLinPitch = 128 * 2 + 16;                        // staging row: 256 + 16 bytes
+constexpr uint32_t kLinStagingBytes = kLinTileM * kLinPitch;        // 128 columns at a time
 constexpr unsigned long long kLinWaitNs = 2000000000ull;           // an internal wait that never ends
+
+// Tile shapes: 128 rows x kBN columns (128 or 256) per tile, 64-element K steps.
+// 256-column tiles load 48 KB per K step for 4.2 MFLOP (128-column: 32 KB for
+// 2.1 MFLOP), so they need less L2 bandwidth per FLOP; they take the whole
+// tensor memory (two 256-column fp32 accumulators) and 3 ring stages.
+template <int kBN>
+struct LinCfg {
+  static constexpr int kStages = kBN == 256 ? 3 : 4;
+  static constexpr uint32_t kABytes = kLinTileM * kLinTileK * 2;    // 16 KB
+  static constexpr uint32_t kBBytes = kBN * kLinTileK * 2;          // 16 or 32 KB
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kSmem = 1024 + kStages * kStageBytes + kLinStagingBytes;
+  static constexpr uint32_t kTmemCols = 2 * kBN;
+};
 
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -95,9 +104,12 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 }
 }  // namespace
 
-template <typename T>
+template <typename T, int kBN>
 __global__ void __launch_bounds__(kLinThreads, 1)
     tp_linear_rmsnorm_kernel(const __grid_constant__ LArgs a) {
+  using Cfg = LinCfg<kBN>;
+  constexpr int kLinStages = Cfg::kStages;
+  constexpr uint32_t kLinStageBytes = Cfg::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) unsigned long long s_full[kLinStages];
   __shared__ __align__(8) unsigned long long s_empty[kLinStages];
@@ -128,7 +140,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const uint32_t bar_drain = ptx::smem_addr(&s_drain);
 
   const int64_t mt = (a.rows + kLinTileM - 1) / kLinTileM;
-  const int64_t nt = a.hidden / kLinTileN;
+  const int64_t nt = a.hidden / kBN;
   const int64_t nbl = a.nblocks;                       // column tiles per owner
   const int64_t tiles = mt * nt;
   const int kbs = (int)(a.k / kLinTileK);
@@ -155,7 +167,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     s_call = exchange ? read_generation(rk.state) : 0ull;
   }
   if (warp == 1) {
-    sm100::tmem_alloc(ptx::smem_addr(&s_tmem), kLinTmemCols);
+    sm100::tmem_alloc(ptx::smem_addr(&s_tmem), Cfg::kTmemCols);
     sm100::tmem_relinquish();
     sm100::fence_before_sync();
   }
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     sm100::tma_prefetch_desc(tma);
     sm100::tma_prefetch_desc(tmb);
     int64_t it = 0;
-    int issued[kLinStages] = {0, 0, 0, 0};
+    int issued[kLinStages] = {};
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       int64_t mb, nb;
@@ -188,7 +200,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         const uint32_t sa = sbase + (uint32_t)s * kLinStageBytes;
         ptx::mbar_arrive_expect_tx(bar_full + 8u * s, kLinStageBytes);
         sm100::tma_load_2d(sa, tma, kb * kLinTileK, (int32_t)(mb * kLinTileM), bar_full + 8u * s);
-        sm100::tma_load_2d(sa + kLinTileBytes, tmb, kb * kLinTileK, (int32_t)(nb * kLinTileN),
+        sm100::tma_load_2d(sa + Cfg::kABytes, tmb, kb * kLinTileK, (int32_t)(nb * kBN),
                            bar_full + 8u * s);
         issued[s] += 1;
       }
@@ -203,7 +215,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // MMA issuer
     const uint32_t idesc = sm100::idesc_f16(sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value,
-                                            kLinTileM, kLinTileN);
+                                            kLinTileM, kBN);
     int64_t it = 0, tc = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         break;
       }
       sm100::fence_after_sync();
-      const uint32_t d = tmem + (uint32_t)(acc * kLinTileN);
+      const uint32_t d = tmem + (uint32_t)(acc * kBN);
       for (int kb = 0; kb < kbs; ++kb, ++it) {
         const int s = (int)(it % kLinStages);
         const uint32_t ph = (uint32_t)((it / kLinStages) & 1);
@@ -225,7 +237,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         sm100::fence_after_sync();
         const uint32_t sa = sbase + (uint32_t)s * kLinStageBytes;
         const uint64_t da = sm100::desc_k_sw128(sa);
-        const uint64_t db = sm100::desc_k_sw128(sa + kLinTileBytes);
+        const uint64_t db = sm100::desc_k_sw128(sa + Cfg::kABytes);
 #pragma unroll
         for (int k = 0; k < kLinTileK / 16; ++k)   // 16 elements = 32 bytes per MMA
           sm100::mma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
@@ -265,38 +277,46 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       if (s_abort) break;
       sm100::fence_after_sync();
       unsigned char* srow = staging + (size_t)row * kLinPitch;
-#pragma unroll
-      for (int c = 0; c < kLinTileN / 32; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32(tmem + (uint32_t)(acc * kLinTileN + c * 32) + ((uint32_t)(q4 * 32) << 16),
-                             r);
-        sm100::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 v;
-          v.x = pack2<T>(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-          v.y = pack2<T>(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-          v.z = pack2<T>(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-          v.w = pack2<T>(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
-          *reinterpret_cast<uint4*>(srow + c * 64 + j * 16) = v;
-        }
-      }
-      sm100::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_acce + 8u * acc);   // accumulator free
-      ptx::team_bar(1, 128);                                  // staging tile complete
-      // 128 rows x 256 bytes into owner's partials [src = rank][row][col]
+      // owner's partials [src = rank][row][col] of this tile
       unsigned char* dst = a.region[owner] + a.recv_off +
-                           (((int64_t)rank * a.nmax + mb * kLinTileM) * hl + nbo * kLinTileN) *
+                           (((int64_t)rank * a.nmax + mb * kLinTileM) * hl + nbo * kBN) *
                                (int64_t)sizeof(T);
-      for (int idx = et; idx < kLinTileM * 16; idx += 128) {
-        const int i = idx >> 4, ch = idx & 15;
-        if (mb * kLinTileM + i < a.rows) {
-          const uint4 v = *reinterpret_cast<const uint4*>(staging + (size_t)i * kLinPitch + ch * 16);
-          ptx::st_v4(dst + (int64_t)i * hl * (int64_t)sizeof(T) + ch * 16, v);
+#pragma unroll 1
+      for (int h = 0; h < kBN / 128; ++h) {   // 128 columns at a time through the staging
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32(tmem + (uint32_t)(acc * kBN + h * 128 + c * 32) +
+                                   ((uint32_t)(q4 * 32) << 16),
+                               r);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 v;
+            v.x = pack2<T>(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+            v.y = pack2<T>(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+            v.z = pack2<T>(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+            v.w = pack2<T>(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+            *reinterpret_cast<uint4*>(srow + c * 64 + j * 16) = v;
+          }
         }
+        if (h == kBN / 128 - 1) {   // the whole accumulator has been read
+          sm100::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar_acce + 8u * acc);
+        }
+        ptx::team_bar(1, 128);   // staging complete
+        // 128 rows x 256 bytes; a warp instruction stores 2 rows x 256 contiguous bytes
+        for (int idx = et; idx < kLinTileM * 16; idx += 128) {
+          const int i = idx >> 4, ch = idx & 15;
+          if (mb * kLinTileM + i < a.rows) {
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(staging + (size_t)i * kLinPitch + ch * 16);
+            ptx::st_v4(dst + (int64_t)i * hl * (int64_t)sizeof(T) + h * 256 + ch * 16, v);
+          }
+        }
+        ptx::team_bar(1, 128);   // every store issued (and the staging free)
       }
-      ptx::team_bar(1, 128);   // every store of the tile issued (and the staging free)
       if (et == 0) {
         __threadfence_system();   // the CTA's stores of the tile before its flag
         unsigned int* flag = reinterpret_cast<unsigned int*>(a.region[owner] + a.flags_off) +
@@ -308,7 +328,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   __syncthreads();   // phase 1 done on this CTA
   if (warp == 1) {
     sm100::fence_after_sync();
-    sm100::tmem_dealloc(tmem, kLinTmemCols);
+    sm100::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 
   // ------------------------------------------------------------------ phase 2
@@ -424,7 +444,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 LinearLayout linear_layout(int tp, int64_t nmax, int64_t hidden, int64_t base) {
   LinearLayout L{};
   L.mblocks = (nmax + kLinTileM - 1) / kLinTileM;
-  L.nblocks = hidden / tp / kLinTileN;
+  L.nblocks = hidden / tp / kLinTileN;   // flags for the narrowest tiles (128 columns)
   L.flags_off = (base + 1023) & ~(int64_t)1023;
   const int64_t flag_bytes = 2 * (int64_t)tp * L.mblocks * L.nblocks * 4;
   L.recv_off = (L.flags_off + flag_bytes + 1023) & ~(int64_t)1023;
@@ -473,7 +493,15 @@ cudaError_t encode_2d(EncodeTiledFn fn, unsigned char* out, const void* base, in
 }
 
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_lin_attr[kMaxDevices][2];
+std::atomic<int> g_lin_attr[kMaxDevices][2][2];
+
+const void* linear_kernel(int dtype, int bn) {
+  if (dtype == kBF16)
+    return bn == 256 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16, 256>)
+                     : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16, 128>);
+  return bn == 256 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half, 256>)
+                   : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half, 128>);
+}
 }  // namespace
 
 static_assert(sizeof(CUtensorMap) == 128, "a tensor map is 128 bytes");
@@ -485,47 +513,49 @@ cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws
   const EncodeTiledFn fn = encode_tiled(&err);
   if (err != cudaSuccess) return err;
   const int nranks = a.emulated ? grid_y : 1;
+  // 256-column tiles whenever every owner's columns are whole 256-column tiles
+  const int bn = (a.hl % 256 == 0) ? 256 : 128;
+  a.nblocks = a.hl / bn;
+  const uint32_t smem = bn == 256 ? LinCfg<256>::kSmem : LinCfg<128>::kSmem;
   for (int r = 0; r < nranks; ++r) {
     err = encode_2d(fn, a.tmaps[2 * r], as[r], dtype, (uint64_t)a.k, (uint64_t)a.rows, kLinTileM);
     if (err != cudaSuccess) return err;
     err = encode_2d(fn, a.tmaps[2 * r + 1], ws[r], dtype, (uint64_t)a.k, (uint64_t)a.hidden,
-                    kLinTileN);
+                    (uint32_t)bn);
     if (err != cudaSuccess) return err;
   }
-  const void* kfn = dtype == kBF16
-                        ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half>);
-  const int ti = dtype == kBF16 ? 0 : 1;
+  const void* kfn = linear_kernel(dtype, bn);
+  const int ti = dtype == kBF16 ? 0 : 1, bi = bn == 256 ? 1 : 0;
   const bool cacheable = device >= 0 && device < kMaxDevices;
-  if (!cacheable || g_lin_attr[device][ti].load() == 0) {
-    err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLinSmem);
+  if (!cacheable || g_lin_attr[device][ti][bi].load() == 0) {
+    err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     err = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                (int)cudaSharedmemCarveoutMaxShared);
     if (err != cudaSuccess) return err;
-    if (cacheable) g_lin_attr[device][ti].store(1);
+    if (cacheable) g_lin_attr[device][ti][bi].store(1);
   }
   int per_sm = 0, sms = 0;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kLinThreads, kLinSmem);
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kLinThreads, smem);
   if (err != cudaSuccess) return err;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return err;
   const int64_t resident = (int64_t)per_sm * sms / (grid_y > 1 ? grid_y : 1);
-  const int64_t tiles = ((a.rows + kLinTileM - 1) / kLinTileM) * (a.hidden / kLinTileN);
+  const int64_t tiles = ((a.rows + kLinTileM - 1) / kLinTileM) * (a.hidden / bn);
   int64_t grid = tiles < resident ? tiles : resident;
   if (grid < 1) return cudaErrorCooperativeLaunchTooLarge;
   a.push_mode = get_push_mode();
   void* args[] = {&a};
   const dim3 g3((unsigned)grid, (unsigned)grid_y), blk(kLinThreads);
-  if (grid_y > 1) return cudaLaunchCooperativeKernel(kfn, g3, blk, args, kLinSmem, stream);
-  if (!get_dependent_launch()) return cudaLaunchKernel(kfn, g3, blk, args, kLinSmem, stream);
+  if (grid_y > 1) return cudaLaunchCooperativeKernel(kfn, g3, blk, args, smem, stream);
+  if (!get_dependent_launch()) return cudaLaunchKernel(kfn, g3, blk, args, smem, stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = g3;
   cfg.blockDim = blk;
-  cfg.dynamicSmemBytes = kLinSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
