@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   ptx::grid_dep_wait();
   ptx::grid_dep_launch_dependents();
   const KArgs& a = b.k;
-  extern __shared__ float s_dw[];                    // [hl]: the CTA's dw partial
+  extern __shared__ float s_dw[];                    // [kTeams][hl]: each team's dw partial
   __shared__ float s_red[kTeams][kChunk][kW][2];
   __shared__ float s_tot[kTeams][kChunk][3];         // S, D, ok
   const unsigned long long t_start = a.prof ? ptx::globaltimer() : 0ull;
@@ -233,11 +233,17 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
     tag1 = tag_of(call + 1ull);
   }
 
-  float dw[kVec][kE];
+  // this lane's columns of the team's dw partial (no other thread touches them)
+  float* tdw = s_dw + (int64_t)team * a.hl;
 #pragma unroll
-  for (int j = 0; j < kVec; ++j)
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    if (c < V) {
 #pragma unroll
-    for (int e = 0; e < kE; ++e) dw[j][e] = 0.f;
+      for (int e = 0; e < kE; e += 4)
+        *reinterpret_cast<float4*>(tdw + (int64_t)c * kE + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
 
   const int64_t teams_total = (int64_t)gridDim.x * kTeams;
   const int64_t tg = (int64_t)blockIdx.x * kTeams + team;
@@ -374,51 +380,61 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
           Pack<T>::unpack(xv[i][j], xf);
           Pack<T>::unpack(dv[i][j], df);
           Pack<T>::unpack(ptx::ld_cached_v4(wg + c), wf);
+          float* dwp = tdw + (int64_t)c * kE;
 #pragma unroll
-          for (int e = 0; e < kE; ++e) {
-            o[e] = inv * (df[e] * wf[e]) - xf[e] * coef;
-            dw[j][e] += (df[e] * xf[e]) * inv;
+          for (int e = 0; e < kE; e += 4) {
+            float4 acc = *reinterpret_cast<float4*>(dwp + e);
+            acc.x += (df[e + 0] * xf[e + 0]) * inv;
+            acc.y += (df[e + 1] * xf[e + 1]) * inv;
+            acc.z += (df[e + 2] * xf[e + 2]) * inv;
+            acc.w += (df[e + 3] * xf[e + 3]) * inv;
+            *reinterpret_cast<float4*>(dwp + e) = acc;
           }
+#pragma unroll
+          for (int e = 0; e < kE; ++e) o[e] = inv * (df[e] * wf[e]) - xf[e] * coef;
           ptx::st_v4(dxg + row * V + c, Pack<T>::pack(o));
         }
       }
     }
   }
   (void)all_ok;
-  // the teams' dw partials into shared memory in team order, then the CTA's row
-  // of the workspace
-  for (int t = 0; t < kTeams; ++t) {
-    if (team == t) {
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        const int c = (j * kW + wit) * 32 + lane;
-        if (c < V) {
-#pragma unroll
-          for (int e = 0; e < kE; ++e) {
-            float* p = s_dw + (int64_t)c * kE + e;
-            *p = (t == 0 ? 0.f : *p) + dw[j][e];
-          }
-        }
-      }
-    }
-    __syncthreads();
-  }
+  // the CTA's row of the workspace: the teams' partials added in team order
+  __syncthreads();
   float* wsr = b.ws[ri] + (int64_t)blockIdx.x * a.hl;
-  for (int64_t i = threadIdx.x; i < a.hl; i += kBlock) wsr[i] = s_dw[i];
+  for (int64_t i = threadIdx.x; i < a.hl; i += kBlock) {
+    float acc = s_dw[i];
+#pragma unroll
+    for (int t = 1; t < kTeams; ++t) acc += s_dw[(int64_t)t * a.hl + i];
+    wsr[i] = acc;
+  }
   if (exchange) finish_launch(rp.state, call, 2ull);
   flush_stats(a, wst, t_start);
 }
 
+// dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 8 warps
+// each sum a contiguous range of parts (lane = column, coalesced), and warp 0
+// adds the 8 range sums in range order -- the same order on every call.
 template <typename T>
 __global__ void __launch_bounds__(256)
     backward_dw_reduce_kernel(const float* __restrict__ ws, int parts, int64_t hl,
                               T* __restrict__ dw) {
+  __shared__ float s_part[8][32];
   ptx::grid_dep_wait();
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= hl) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t j = (int64_t)blockIdx.x * 32 + lane;
+  const int per = (parts + 7) / 8;
+  const int c0 = warp * per, c1 = min(parts, c0 + per);
   float s = 0.f;
-  for (int c = 0; c < parts; ++c) s += ws[(int64_t)c * hl + j];
-  dw[j] = Pack<T>::from_f(s);
+  if (j < hl)
+    for (int c = c0; c < c1; ++c) s += ws[(int64_t)c * hl + j];
+  s_part[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && j < hl) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += s_part[w][lane];
+    dw[j] = Pack<T>::from_f(t);
+  }
 }
 
 namespace {
@@ -451,11 +467,10 @@ struct BwdShape {
 constexpr BwdShape kBwdShapes[] = {{1, 1, 256}, {2, 1, 256}, {4, 1, 256}, {4, 2, 256},
                                    {4, 4, 256}, {4, 8, 256}, {4, 16, 512}};
 constexpr int kNumBwdShapes = sizeof(kBwdShapes) / sizeof(kBwdShapes[0]);
-// rows in flight per team: two, but one for 16-bit rows of 4 vectors per lane,
-// whose 32 fp32 dw accumulators and two rows of x and dy exceed 128 registers
+// rows in flight per team (x and dy of each in registers; dw lives in shared memory)
 template <typename T, int kVec>
 constexpr int bwd_chunk() {
-  return (sizeof(T) == 2 && kVec == 4) ? 1 : 2;
+  return 2;
 }
 
 template <typename T>
@@ -505,7 +520,9 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   const BwdFn fn = shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
   const int block = shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
   const void* fp = reinterpret_cast<const void*>(fn);
-  const size_t smem = (size_t)a.hl * sizeof(float);
+  // dw partials: one [hl] fp32 slice per team (register kernel) or per CTA
+  const int teams = shape >= 0 ? kBwdShapes[shape].block / 32 / kBwdShapes[shape].w : 1;
+  const size_t smem = (size_t)teams * (size_t)a.hl * sizeof(float);
   cudaError_t err;
   if (smem > 48u * 1024u) {
     const bool cacheable = device >= 0 && device < kMaxDevices;
@@ -548,22 +565,25 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
 
 cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, int dtype,
                              cudaStream_t stream) {
-  const dim3 grid((unsigned)((hl + 255) / 256)), blk(256);
-  switch (dtype) {
-    case kF32:
-      backward_dw_reduce_kernel<float><<<grid, blk, 0, stream>>>(ws, parts, hl,
-                                                                 static_cast<float*>(dw));
-      break;
-    case kBF16:
-      backward_dw_reduce_kernel<__nv_bfloat16><<<grid, blk, 0, stream>>>(
-          ws, parts, hl, static_cast<__nv_bfloat16*>(dw));
-      break;
-    default:
-      backward_dw_reduce_kernel<__half><<<grid, blk, 0, stream>>>(ws, parts, hl,
-                                                                  static_cast<__half*>(dw));
-      break;
-  }
-  return cudaPeekAtLastError();
+  const dim3 grid((unsigned)((hl + 31) / 32)), blk(256);
+  const void* fn = dtype == kF32    ? reinterpret_cast<const void*>(backward_dw_reduce_kernel<float>)
+                   : dtype == kBF16 ? reinterpret_cast<const void*>(
+                                          backward_dw_reduce_kernel<__nv_bfloat16>)
+                                    : reinterpret_cast<const void*>(backward_dw_reduce_kernel<__half>);
+  void* args[] = {&ws, &parts, &hl, &dw};
+  if (!get_dependent_launch()) return cudaLaunchKernel(fn, grid, blk, args, 0, stream);
+  // launched while the backward kernel drains; waits for it in griddepcontrol.wait
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = blk;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace rtp
