@@ -145,12 +145,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const int64_t tiles = mt * nt;
   const int kbs = (int)(a.k / kLinTileK);
   const int64_t hl = a.hl;
-  // tile t -> (m block, n block); consecutive tiles go to different owners
-  auto tile_mn = [&](int64_t t, int64_t& mb, int64_t& nb) {
-    mb = t / nt;
-    const int64_t j = t - mb * nt;
-    nb = (j % tp) * nbl + j / tp;
-  };
+  // tile t -> (m block, n block): grouped m blocks, owners dealt in turn
+  auto tile_mn = [&](int64_t t, int64_t& mb, int64_t& nb) { linear_tile(t, mt, nt, tp, nbl, &mb, &nb); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kLinStages; ++s) {

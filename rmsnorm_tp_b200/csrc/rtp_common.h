@@ -131,4 +131,24 @@ RTP_HD int64_t tile_of(int64_t team_global, int64_t it, int64_t teams_total) {
   return team_global + it * teams_total;
 }
 
+// Output tile t of the fused row-parallel linear -> (m block, n block), for mt x nt
+// tiles, tp owners of nbl column tiles each. Tiles go in groups of up to 16 m
+// blocks: within a group the m block varies fastest, so the CTAs running at the
+// same time share a few column slices of the weight (read once from HBM, then
+// from L2) instead of streaming all of it per m block; the group's column index
+// j is dealt over the owners (owner j % tp), so that consecutive tiles go to
+// different ranks' receive buffers.
+constexpr int64_t kLinGroupM = 16;
+RTP_HD void linear_tile(int64_t t, int64_t mt, int64_t nt, int tp, int64_t nbl, int64_t* mb,
+                        int64_t* nb) {
+  const int64_t per_group = kLinGroupM * nt;
+  const int64_t g = t / per_group;
+  const int64_t left = mt - g * kLinGroupM;
+  const int64_t gm = left < kLinGroupM ? left : kLinGroupM;
+  const int64_t r = t - g * per_group;
+  *mb = g * kLinGroupM + r % gm;
+  const int64_t j = r / gm;
+  *nb = (j % tp) * nbl + j / tp;
+}
+
 }  // namespace rtp

@@ -61,3 +61,20 @@ def test_linear_forward_validates_without_gpu():
                                        None) == _lib.ERR_INVALID
     assert L.rmsnorm_tp_linear_forward_emulated(None, 2, None, None, None, None, None, 4, 64, 1,
                                                 1e-6, None) == _lib.ERR_INVALID
+
+
+def test_linear_tile_order_is_a_bijection(tmp_path):
+    """tests/cpp/test_linear_tiles.cpp: the fused linear's tile order covers every
+    output tile exactly once (compiled against the kernels' header)."""
+    import os
+    import subprocess
+
+    from conftest import ROOT
+
+    exe = tmp_path / "test_linear_tiles"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-I",
+                    os.path.join(ROOT, "rmsnorm_tp_b200", "csrc"),
+                    os.path.join(ROOT, "tests", "cpp", "test_linear_tiles.cpp"), "-o", str(exe)],
+                   check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and "ALL PASS" in res.stdout, res.stdout
