@@ -278,17 +278,20 @@ __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
 }
 
 // Last CTA of the launch advances the rank's generation counter by `step`
-// (one per exchange the launch made: forward 1, backward 2).
+// (one per exchange the launch made: forward 1, backward 2). No fence: nothing
+// in this launch reads the counter after its first read, and the next launch
+// reads it only once this grid has completed (stream order, or its
+// griddepcontrol.wait), when every write of the grid is visible; a fence here
+// would hold each CTA's exit until its outstanding stores, the pushes to peers
+// included, were acknowledged.
 __device__ __forceinline__ void finish_launch(DeviceState* st, unsigned long long call,
                                               unsigned long long step = 1ull) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const unsigned prev = atomicAdd(&st->done, 1u);
     if (prev == gridDim.x - 1) {
       st->done = 0u;
       st->call = call + step;
-      __threadfence();
     }
   }
 }
