@@ -276,6 +276,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   __shared__ float s_part[kTeams][kDepth][kW][kRows];
   __shared__ float s_sum[kTeams][kDepth][kRows];
   __shared__ int s_ok[kTeams][kDepth];
+  __shared__ float s_cpart[kDepth][kTeams * kRows];   // the CTA's partials, per depth
+  static_assert(kTeams * kRows <= 32, "one lane per row of a CTA's depth level");
+  static_assert(kBlock / 32 >= kMaxTP, "one warp per peer");
 
   const int64_t tiles = (a.rows + kRows - 1) / kRows;
   const int64_t stride = (int64_t)gridDim.x * kTeams;
@@ -309,34 +312,53 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   const unsigned long long call = read_generation(rp.state);
   const uint32_t buf = buffer_of(call), tag = tag_of(call);
 
-  // reduce and push every tile as its loads complete
+  // Reduce every tile as its loads complete and push it. At depth d the CTA's
+  // teams hold kTeams consecutive tiles = kTeams * kRows consecutive rows, so
+  // after a CTA barrier warp q writes all of them to rank q as ONE contiguous
+  // store of kTeams * kRows slots (one NVLink write per peer, CTA and depth,
+  // instead of one per peer and team).
+  const int64_t cta_tile0 = (int64_t)blockIdx.x * kTeams;
 #pragma unroll
   for (int d = 0; d < kDepth; ++d) {
+    if (cta_tile0 + d * stride >= tiles) break;   // uniform over the CTA
     const int64_t tt = first + d * stride;
-    if (tt >= tiles) break;
-#pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-      float s = 0.f;
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) s += sumsq16<T>(xv[d][r][j]);
-      ss[d][r] = warp_allreduce_sum(s);
-    }
-    if constexpr (kW > 1) {
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) s_part[team][d][wit][r] = ss[d][r];
-      }
-      ptx::team_bar(1 + team, kW * 32);
+    if (tt < tiles) {
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < kW; ++w) s += s_part[team][d][w][r];
-        ss[d][r] = s;
+        for (int j = 0; j < kVec; ++j) s += sumsq16<T>(xv[d][r][j]);
+        ss[d][r] = warp_allreduce_sum(s);
+      }
+      if constexpr (kW > 1) {
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) s_part[team][d][wit][r] = ss[d][r];
+        }
+        ptx::team_bar(1 + team, kW * 32);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          float s = 0.f;
+#pragma unroll
+          for (int w = 0; w < kW; ++w) s += s_part[team][d][w][r];
+          ss[d][r] = s;
+        }
+      }
+      if ((kW == 1 || wit == 0) && lane < kRows) {
+        float m = 0.f;
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+          if (r == lane) m = ss[d][r];
+        s_cpart[d][team * kRows + lane] = m;
       }
     }
-    if (kW == 1 || wit == 0)
-      push_slot(a, rank, buf, tag, tt * kRows + lr, lq, lr < nrows_of(tt), mine_of(ss[d]));
+    __syncthreads();
+    if (warp < tp && warp != rank && lane < kTeams * kRows) {
+      const int64_t row = (cta_tile0 + d * stride) * kRows + lane;
+      if (row < a.rows)
+        store_slot(a.push_mode, a.mbox[warp] + slot_index(buf, rank, tp, a.nmax, row),
+                   s_cpart[d][lane], tag);
+    }
   }
 
   // one look at every tile's slot, all loads issued back to back (independent
