@@ -414,6 +414,141 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 // dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 8 warps
 // each sum a contiguous range of parts (lane = column, coalesced), and warp 0
 // adds the 8 range sums in range order -- the same order on every call.
+// ---------------------------------------------------------------------------
+// Local register backward (TP = 1: no exchange): the register backward's teams,
+// column mapping and dw slices, one row at a time but double-buffered -- the
+// next row's x and dy loads are issued before the current row is reduced,
+// written and accumulated, so HBM stays busy through the compute and the dx
+// stores (the chunked kernel above waits for each chunk's loads after the
+// previous chunk's stores).
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kBlock, int kMinBlocks>
+__global__ void __launch_bounds__(kBlock, kMinBlocks)
+    rmsnorm_local_backward_vec_kernel(const __grid_constant__ BArgs b) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  constexpr int kE = Pack<T>::kE;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const KArgs& a = b.k;
+  extern __shared__ float s_dw[];                    // [kTeams][hl]: each team's dw partial
+  __shared__ float s_red[kTeams][2][kW][2];          // two slots: rows alternate
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const RankPtrs& rp = a.rp[0];
+  const int64_t V = a.hl / kE;
+  const uint4* __restrict__ xg = ptx::launder(reinterpret_cast<const uint4*>(rp.x));
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  const uint4* __restrict__ dyg = ptx::launder(reinterpret_cast<const uint4*>(b.dy[0]));
+  uint4* __restrict__ dxg = reinterpret_cast<uint4*>(rp.out);
+
+  float* tdw = s_dw + (int64_t)team * a.hl;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    if (c < V) {
+#pragma unroll
+      for (int e = 0; e < kE; e += 4)
+        *reinterpret_cast<float4*>(tdw + (int64_t)c * kE + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+
+  auto load = [&](int64_t row, uint4 (&xv)[kVec], uint4 (&dv)[kVec]) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      const bool in = c < V;
+      xv[j] = in ? ptx::ld_stream_v4(xg + row * V + c) : make_uint4(0u, 0u, 0u, 0u);
+      dv[j] = in ? ptx::ld_stream_v4(dyg + row * V + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // S, D (team), dx from the registers, dw into the team's slice
+  auto process = [&](int64_t row, const uint4 (&xv)[kVec], const uint4 (&dv)[kVec], int slot) {
+    float s = 0.f, d = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      if (c < V) {
+        float xf[kE], df[kE], wf[kE];
+        Pack<T>::unpack(xv[j], xf);
+        Pack<T>::unpack(dv[j], df);
+        Pack<T>::unpack(ptx::ld_cached_v4(wg + c), wf);
+#pragma unroll
+        for (int e = 0; e < kE; ++e) {
+          s = fmaf(xf[e], xf[e], s);
+          d = fmaf(df[e] * wf[e], xf[e], d);
+        }
+      }
+    }
+    float S = warp_allreduce_sum(s), D = warp_allreduce_sum(d);
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+        s_red[team][slot][wit][0] = S;
+        s_red[team][slot][wit][1] = D;
+      }
+      ptx::team_bar(1 + team, kW * 32);
+      S = 0.f;
+      D = 0.f;
+#pragma unroll
+      for (int w = 0; w < kW; ++w) {
+        S += s_red[team][slot][w][0];
+        D += s_red[team][slot][w][1];
+      }
+    }
+    const float inv = rsqrtf(S / a.hidden_f + a.eps);
+    const float coef = (inv * inv * inv) * (D / a.hidden_f);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      if (c < V) {
+        float xf[kE], df[kE], wf[kE], o[kE];
+        Pack<T>::unpack(xv[j], xf);
+        Pack<T>::unpack(dv[j], df);
+        Pack<T>::unpack(ptx::ld_cached_v4(wg + c), wf);
+        float* dwp = tdw + (int64_t)c * kE;
+#pragma unroll
+        for (int e = 0; e < kE; e += 4) {
+          float4 acc = *reinterpret_cast<float4*>(dwp + e);
+          acc.x += (df[e + 0] * xf[e + 0]) * inv;
+          acc.y += (df[e + 1] * xf[e + 1]) * inv;
+          acc.z += (df[e + 2] * xf[e + 2]) * inv;
+          acc.w += (df[e + 3] * xf[e + 3]) * inv;
+          *reinterpret_cast<float4*>(dwp + e) = acc;
+        }
+#pragma unroll
+        for (int e = 0; e < kE; ++e) o[e] = inv * (df[e] * wf[e]) - xf[e] * coef;
+        ptx::st_v4(dxg + row * V + c, Pack<T>::pack(o));
+      }
+    }
+  };
+
+  const int64_t teams_total = (int64_t)gridDim.x * kTeams;
+  int64_t row = (int64_t)blockIdx.x * kTeams + team;
+  uint4 xa[kVec], da[kVec], xb[kVec], db[kVec];
+  if (row < a.rows) load(row, xa, da);
+  while (row < a.rows) {
+    int64_t nxt = row + teams_total;
+    if (nxt < a.rows) load(nxt, xb, db);
+    process(row, xa, da, 0);
+    row = nxt;
+    if (row >= a.rows) break;
+    nxt = row + teams_total;
+    if (nxt < a.rows) load(nxt, xa, da);
+    process(row, xb, db, 1);
+    row = nxt;
+  }
+  __syncthreads();
+  float* wsr = b.ws[0] + (int64_t)blockIdx.x * a.hl;
+  for (int64_t i = threadIdx.x; i < a.hl; i += kBlock) {
+    float acc = s_dw[i];
+#pragma unroll
+    for (int t = 1; t < kTeams; ++t) acc += s_dw[(int64_t)t * a.hl + i];
+    wsr[i] = acc;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
     backward_dw_reduce_kernel(const float* __restrict__ ws, int parts, int64_t hl,
@@ -483,6 +618,27 @@ struct BwdVecTable {
 #undef RTP_BWD
 };
 
+template <typename T>
+struct BwdLocalTable {
+#define RTP_BWDL(V, W, B, M) rmsnorm_local_backward_vec_kernel<T, V, W, B, M>
+  static constexpr BwdFn fn[kNumBwdShapes] = {
+      RTP_BWDL(1, 1, 256, 2), RTP_BWDL(2, 1, 256, 2), RTP_BWDL(4, 1, 256, 2), RTP_BWDL(4, 2, 256, 2),
+      RTP_BWDL(4, 4, 256, 2), RTP_BWDL(4, 8, 256, 2), RTP_BWDL(4, 16, 512, 1),
+  };
+#undef RTP_BWDL
+};
+
+BwdFn backward_local_fn(int dtype, int shape) {
+  switch (dtype) {
+    case kF32:
+      return BwdLocalTable<float>::fn[shape];
+    case kBF16:
+      return BwdLocalTable<__nv_bfloat16>::fn[shape];
+    default:
+      return BwdLocalTable<__half>::fn[shape];
+  }
+}
+
 BwdFn backward_vec_fn(int dtype, int shape) {
   switch (dtype) {
     case kF32:
@@ -494,6 +650,7 @@ BwdFn backward_vec_fn(int dtype, int shape) {
   }
 }
 std::atomic<unsigned int> g_vec_smem_set[kMaxDevices][3][kNumBwdShapes];
+std::atomic<unsigned int> g_local_smem_set[kMaxDevices][3][kNumBwdShapes];
 
 }  // namespace
 
@@ -517,7 +674,10 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   if (vec16 && get_family() != kFamilyBulk)
     for (int i = 0; i < kNumBwdShapes && shape < 0; ++i)
       if (V <= 32ll * kBwdShapes[i].w * kBwdShapes[i].vec) shape = i;
-  const BwdFn fn = shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
+  // TP = 1 (no exchange): the double-buffered local register kernel
+  const bool local = shape >= 0 && a.tp == 1 && !a.emulated;
+  const BwdFn fn = local ? backward_local_fn(dtype, shape)
+                         : shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
   const int block = shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
   const void* fp = reinterpret_cast<const void*>(fn);
   // dw partials: one [hl] fp32 slice per team (register kernel) or per CTA
@@ -526,8 +686,9 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   cudaError_t err;
   if (smem > 48u * 1024u) {
     const bool cacheable = device >= 0 && device < kMaxDevices;
-    std::atomic<unsigned int>& set = shape >= 0 ? g_vec_smem_set[device][dtype][shape]
-                                                : g_smem_set[device][dtype][vec16 ? 1 : 0];
+    std::atomic<unsigned int>& set = local        ? g_local_smem_set[device][dtype][shape]
+                                     : shape >= 0 ? g_vec_smem_set[device][dtype][shape]
+                                                  : g_smem_set[device][dtype][vec16 ? 1 : 0];
     if (!cacheable || set.load() < smem) {
       err = cudaFuncSetAttribute(fp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (err != cudaSuccess) return err;
