@@ -175,7 +175,8 @@ int rmsnorm_local_forward_residual(void* out, void* residual, const void* x,
  * normalises: out = z * rsqrt(S / hidden + eps) * norm_weight, S = sum over the
  * group of sum(z^2). out and residual are [rows, hidden / tp]; norm_weight is
  * [hidden / tp]. bf16 or fp16; k_local a multiple of 64; hidden a multiple of
- * 128 * tp; every pointer 16-byte aligned. A collective like rmsnorm_tp_forward
+ * 128 * tp; every pointer 16-byte aligned; out and residual must not overlap a,
+ * linear_weight or norm_weight. A collective like rmsnorm_tp_forward
  * (one generation per call), on a communicator made by rmsnorm_tp_create_linear,
  * whose mailbox allocation also holds the receive buffer
  * (num_max_rows * hidden * 2 bytes) and its flags; the same export / open /

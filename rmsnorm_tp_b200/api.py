@@ -235,7 +235,6 @@ class TPCommBuffer:
         rows, hl = x.shape
         if residual is not None:
             _check_like("residual", residual, x)
-            self.next_generation()
             check(
                 LIB.rmsnorm_tp_forward_residual(self._comm, out.data_ptr(), residual.data_ptr(),
                                                 x.data_ptr(), weight.data_ptr(), rows, hl, hidden,
@@ -243,14 +242,15 @@ class TPCommBuffer:
                                                 _stream_of(x.device.index)),
                 "rmsnorm_tp_forward_residual",
             )
+            self.next_generation()
             return out
-        self.next_generation()
         check(
             LIB.rmsnorm_tp_forward(self._comm, out.data_ptr(), x.data_ptr(), weight.data_ptr(), rows,
                                    hl, hidden, _DTYPES[x.dtype], float(eps),
                                    _stream_of(x.device.index)),
             "rmsnorm_tp_forward",
         )
+        self.next_generation()
         return out
 
     def launch_backward(self, dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, hidden: int,
@@ -258,8 +258,6 @@ class TPCommBuffer:
         """One backward launch on the current stream (two generations); returns (dx, dw)."""
         dx, dw, ws, nbytes = _backward_operands(dy, x, weight)
         rows, hl = x.shape
-        self.next_generation()
-        self.next_generation()
         check(
             LIB.rmsnorm_tp_backward(self._comm, dx.data_ptr(), dw.data_ptr(), dy.data_ptr(),
                                     x.data_ptr(), weight.data_ptr(), rows, hl, hidden,
@@ -267,6 +265,8 @@ class TPCommBuffer:
                                     _stream_of(x.device.index)),
             "rmsnorm_tp_backward",
         )
+        self.next_generation()
+        self.next_generation()
         return dx, dw
 
     # -- failure detection / recovery
@@ -382,7 +382,6 @@ class FusedTPRMSNorm:
                 f"x is on cuda:{x.device.index}, the communicator on cuda:{self.comm_buf.device}"
             )
         output = torch.empty_like(x) if out is None else out
-        self.comm_buf.next_generation()
         if residual is not None:
             check(
                 LIB.rmsnorm_tp_forward_residual(self.comm_buf._comm, output.data_ptr(),
@@ -392,14 +391,15 @@ class FusedTPRMSNorm:
                                                 float(self.eps), _stream_of(x.device.index)),
                 "rmsnorm_tp_forward_residual",
             )
-            return output
-        check(
-            LIB.rmsnorm_tp_forward(self.comm_buf._comm, output.data_ptr(), x.data_ptr(),
-                                   weight.data_ptr(), num_rows, local_hidden_dim,
-                                   local_hidden_dim * self.tp_size, _DTYPES[x.dtype],
-                                   float(self.eps), _stream_of(x.device.index)),
-            "rmsnorm_tp_forward",
-        )
+        else:
+            check(
+                LIB.rmsnorm_tp_forward(self.comm_buf._comm, output.data_ptr(), x.data_ptr(),
+                                       weight.data_ptr(), num_rows, local_hidden_dim,
+                                       local_hidden_dim * self.tp_size, _DTYPES[x.dtype],
+                                       float(self.eps), _stream_of(x.device.index)),
+                "rmsnorm_tp_forward",
+            )
+        self.comm_buf.next_generation()   # the device advanced its own on the launch
         return output
 
     __call__ = forward
@@ -415,8 +415,6 @@ class FusedTPRMSNorm:
         if num_rows > self.num_max_rows:
             raise AssertionError(f"num_rows {num_rows} > num_max_rows {self.num_max_rows}")
         dx, dw, ws, nbytes = _backward_operands(dy, x, weight)
-        self.comm_buf.next_generation()
-        self.comm_buf.next_generation()
         check(
             LIB.rmsnorm_tp_backward(self.comm_buf._comm, dx.data_ptr(), dw.data_ptr(), dy.data_ptr(),
                                     x.data_ptr(), weight.data_ptr(), num_rows, local_hidden_dim,
@@ -425,6 +423,8 @@ class FusedTPRMSNorm:
                                     _stream_of(x.device.index)),
             "rmsnorm_tp_backward",
         )
+        self.comm_buf.next_generation()
+        self.comm_buf.next_generation()
         return dx, dw
 
     def forward_with_grad(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
@@ -531,7 +531,6 @@ class FusedTPLinearRMSNorm:
         if residual is not None and (residual.shape != (rows, hl) or residual.dtype != a.dtype
                                      or not residual.is_contiguous()):
             raise AssertionError(f"residual must be contiguous [{rows}, {hl}] of a's dtype")
-        self.comm_buf.next_generation()
         check(
             LIB.rmsnorm_tp_linear_forward(self.comm_buf._comm, out.data_ptr(),
                                           None if residual is None else residual.data_ptr(),
@@ -541,6 +540,7 @@ class FusedTPLinearRMSNorm:
                                           _stream_of(a.device.index)),
             "rmsnorm_tp_linear_forward",
         )
+        self.comm_buf.next_generation()
         return out
 
     __call__ = forward
@@ -592,8 +592,6 @@ class EmulatedTPLinearGroup:
         hl = self.hidden_dim // tp
         outs = [torch.empty(rows, hl, dtype=as_[0].dtype, device=as_[0].device) for _ in range(tp)]
         P = ctypes.c_void_p * tp
-        for b in self.bufs:
-            b.next_generation()
         rptr = None if residuals is None else P(*[r.data_ptr() for r in residuals])
         check(
             LIB.rmsnorm_tp_linear_forward_emulated(
@@ -603,6 +601,8 @@ class EmulatedTPLinearGroup:
                 float(self.eps), _stream_of(as_[0].device.index)),
             "rmsnorm_tp_linear_forward_emulated",
         )
+        for b in self.bufs:
+            b.next_generation()
         return outs
 
     def destroy(self) -> None:
@@ -659,8 +659,6 @@ class EmulatedTPGroup:
         optr = P(*[o.data_ptr() for o in outs])
         xptr = P(*[x.data_ptr() for x in xs])
         wptr = P(*[w.data_ptr() for w in weights])
-        for b in self.bufs:
-            b.next_generation()
         if residuals is not None:
             if len(residuals) != tp:
                 raise AssertionError(f"need {tp} residuals")
@@ -673,6 +671,8 @@ class EmulatedTPGroup:
                                                          _stream_of(xs[0].device.index)),
                 "rmsnorm_tp_forward_emulated_residual",
             )
+            for b in self.bufs:
+                b.next_generation()
             return list(outs)
         check(
             LIB.rmsnorm_tp_forward_emulated(comms, tp, optr, xptr, wptr, rows, hl,
@@ -680,6 +680,8 @@ class EmulatedTPGroup:
                                             _stream_of(xs[0].device.index)),
             "rmsnorm_tp_forward_emulated",
         )
+        for b in self.bufs:
+            b.next_generation()
         return list(outs)
 
     def backward(self, dys: Sequence[torch.Tensor], xs: Sequence[torch.Tensor],
@@ -694,9 +696,6 @@ class EmulatedTPGroup:
             raise AssertionError("every rank needs the same shape and dtype")
         P = ctypes.c_void_p * tp
         comms = P(*[b._comm.value for b in self.bufs])
-        for b in self.bufs:
-            b.next_generation()
-            b.next_generation()
         check(
             LIB.rmsnorm_tp_backward_emulated(
                 comms, tp, P(*[o[0].data_ptr() for o in ops]), P(*[o[1].data_ptr() for o in ops]),
@@ -706,6 +705,9 @@ class EmulatedTPGroup:
                 _stream_of(xs[0].device.index)),
             "rmsnorm_tp_backward_emulated",
         )
+        for b in self.bufs:
+            b.next_generation()
+            b.next_generation()
         return [o[0] for o in ops], [o[1] for o in ops]
 
     def reset(self, generation: int = 0) -> None:

@@ -580,6 +580,22 @@ static int check_linear(const char* who, const rmsnorm_tp_comm* c, int64_t rows,
     const int rc = check_residual(who, rows, c->linear_hidden / c->tp, dtype, res, out);
     if (rc != RMSNORM_TP_OK) return rc;
   }
+  // out and the residual are written while other CTAs may still read a and the
+  // weights (the GEMM phase of the kernel): neither may overlap an input
+  const uintptr_t out_n = (uintptr_t)rows * (uintptr_t)(c->linear_hidden / c->tp) * 2u;
+  const uintptr_t in_p[3] = {reinterpret_cast<uintptr_t>(a), reinterpret_cast<uintptr_t>(w),
+                             reinterpret_cast<uintptr_t>(gamma)};
+  const uintptr_t in_n[3] = {(uintptr_t)rows * (uintptr_t)k * 2u,
+                             (uintptr_t)c->linear_hidden * (uintptr_t)k * 2u,
+                             (uintptr_t)(c->linear_hidden / c->tp) * 2u};
+  const uintptr_t dst[2] = {reinterpret_cast<uintptr_t>(out), reinterpret_cast<uintptr_t>(res)};
+  for (int d = 0; d < 2 && rows > 0; ++d) {
+    if (dst[d] == 0) continue;
+    for (int i = 0; i < 3; ++i)
+      if (dst[d] < in_p[i] + in_n[i] && in_p[i] < dst[d] + out_n)
+        return fail(RMSNORM_TP_ERR_INVALID, "%s: %s overlaps an input", who,
+                    d == 0 ? "out" : "residual");
+  }
   if (*reinterpret_cast<volatile unsigned*>(c->host_flag) != 0u)
     return fail(RMSNORM_TP_ERR_DEVICE,
                 "%s: an earlier launch recorded a device failure; reset the communicator on "

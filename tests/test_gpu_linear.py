@@ -122,3 +122,28 @@ def test_graph_capture_of_the_module():
         del gr
     finally:
         m.destroy()
+
+
+def test_output_overlapping_an_input_is_rejected_and_generation_unchanged():
+    """out (or the residual) is written while other CTAs may still read a and the
+    weights: an overlap is an argument error, raised before any launch, and a
+    rejected call advances neither the host's nor the device's generation."""
+    rows, k, hidden, dtype = 64, 128, 256, torch.bfloat16
+    as_, lws, gs = make_linear_group(rows, k, hidden, 1, dtype, 5, device="cuda")
+    m = rtp.FusedTPLinearRMSNorm(hidden, eps=1e-5, num_max_rows=rows)
+    try:
+        big = torch.empty(rows * max(k, hidden) * 2, dtype=dtype, device="cuda")
+        a = big[: rows * k].view(rows, k)
+        a.copy_(as_[0])
+        with pytest.raises(rtp.RMSNormTPError, match="overlaps"):
+            m.forward(a, lws[0], gs[0], out=big[: rows * hidden].view(rows, hidden))
+        with pytest.raises(rtp.RMSNormTPError, match="overlaps"):
+            m.forward(a, lws[0], gs[0], residual=big[64: 64 + rows * hidden].view(rows, hidden))
+        torch.cuda.synchronize()
+        assert m.comm_buf.generation == 0 and m.comm_buf.device_generation() == 0
+        y = m.forward(a, lws[0], gs[0])        # disjoint output: runs
+        torch.cuda.synchronize()
+        assert m.comm_buf.generation == 1 and m.comm_buf.device_generation() == 1
+    finally:
+        m.destroy()
+    _check("bf16", as_, lws, gs, 1e-5, [y])
