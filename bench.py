@@ -611,7 +611,9 @@ def parity_check(module, w, world, rank, x, wt, n_sample=128):
 def wait_counters(module, step, world, rank, n_capture=64, steps=256):
     """In-kernel exchange counters at N > 1 in steady state (a CUDA graph of
     back-to-back calls replayed with the counters on, untimed): per rank, the share
-    of peer polls that found the partial missing and the mean wait of those polls."""
+    of peer polls that found the partial missing, the mean wait of those polls,
+    the mean launch span and gap between launches, and (resident kernel) the
+    CTAs' mean time to push their partials and from there to their end."""
     import rmsnorm_tp_b200 as rtp
 
     c = rtp.profile_counters()
@@ -621,11 +623,8 @@ def wait_counters(module, step, world, rank, n_capture=64, steps=256):
     finally:
         module.comm_buf.set_profile(None)
     v = c.cpu().tolist()
-    polls = v[1] + v[2]
-    mine = {"slow_poll_share": round(v[1] / max(1, polls), 4),
-            "mean_wait_us": round(v[0] / max(1, v[1]) / 1e3, 3),
-            "polls_per_call": round(polls / (steps if steps >= n_capture else n_capture), 1),
-            "call_span_us": round((v[4] - v[3]) / 1e3 / max(1, steps), 3) if v[4] > v[3] else None}
+    mine = rtp.profile_summary(v)
+    mine["polls_per_call"] = round(mine.pop("polls") / max(1, v[11]), 1)
     gathered = [None] * world
     dist.all_gather_object(gathered, mine)
     if rank != 0:
@@ -849,10 +848,7 @@ class OursImpl:
             time_graph(step, n_capture, steps, world)
         finally:
             self.m.comm_buf.set_profile(None)
-        v = c.cpu().tolist()
-        polls = v[1] + v[2]
-        return {"polls": polls, "slow_poll_share": round(v[1] / max(1, polls), 4),
-                "mean_wait_us": round(v[0] / max(1, v[1]) / 1e3, 3)}
+        return rtp.profile_summary(c.cpu().tolist())
 
     def close(self):
         self.m.destroy()
@@ -1183,6 +1179,13 @@ def run_emulated(args):
             g.forward(xs, ws, outs=outs)
         torch.cuda.synchronize()
         ms = time_steps(lambda i: g.forward(xs, ws, outs=outs), args.steps)
+        # in-kernel counters over a second, untimed run of the same calls
+        c = rtp.profile_counters()
+        g.bufs[0].set_profile(c)              # the one launch takes rank 0's setting
+        for _ in range(args.steps):
+            g.forward(xs, ws, outs=outs)
+        g.bufs[0].set_profile(None)
+        prof = rtp.profile_summary(c.cpu().tolist())
         ok = all(b.poll_error() == 0 for b in g.bufs)
     finally:
         g.destroy()
@@ -1190,7 +1193,7 @@ def run_emulated(args):
                       "dtype": DTYPE_NAME[w["dtype"]], "steps": args.steps,
                       "us_per_call": round(ms * 1e3 / args.steps, 3),
                       "kernel": kernel_name(rtp, w["rows"], w["hidden"] // tp, tp, w["dtype"]),
-                      "device_errors": not ok}), flush=True)
+                      "profile": prof, "device_errors": not ok}), flush=True)
     return 0 if ok else 1
 
 

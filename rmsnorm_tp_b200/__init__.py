@@ -22,6 +22,7 @@ from .api import (
     plan,
     plan_coverage,
     profile_counters,
+    profile_summary,
     set_kernel_family,
     get_kernel_family,
     set_push_mode,
@@ -46,6 +47,7 @@ __all__ = [
     "plan",
     "plan_coverage",
     "profile_counters",
+    "profile_summary",
     "tag_of",
     "set_kernel_family",
     "get_kernel_family",

@@ -129,7 +129,7 @@ struct rmsnorm_tp_comm {
   bool finalized = false;
   unsigned long long probe_seq = 0;
   unsigned char uuid[16] = {};
-  unsigned long long* prof = nullptr;      // optional device counters (5 x u64)
+  unsigned long long* prof = nullptr;      // optional device counters (18 x u64)
   int64_t linear_hidden = 0;               // fused linear: hidden width of the receive region
   rtp::LinearLayout lin{};                 // fused linear: layout of the receive region
 };
@@ -153,7 +153,7 @@ extern "C" {
 
 const char* rmsnorm_tp_last_error(void) { return g_last_error.c_str(); }
 
-int rmsnorm_tp_abi_version(void) { return 102; }
+int rmsnorm_tp_abi_version(void) { return 103; }
 
 uint32_t rmsnorm_tp_tag_of(uint64_t generation) { return rtp::tag_of(generation); }
 uint32_t rmsnorm_tp_buffer_of(uint64_t generation) { return rtp::buffer_of(generation); }

@@ -259,11 +259,21 @@ __device__ __forceinline__ float push_poll(const KArgs& a, int rank, const RankP
   return poll_slot(a, rank, rp, buf, tag, call, row, q, active, mine, failed, ws);
 }
 
-// Adds the lanes' wait counters and the CTA's start/end times to KArgs::prof:
+// Adds the lanes' wait counters and the CTA's timings to KArgs::prof (global
+// timer, ns; every CTA of a launch calls this exactly once, at its end):
 // [0] wait ns summed over lanes, [1] slow waits, [2] fast waits,
-// [3] earliest CTA start, [4] latest CTA end (global timer, ns).
+// [3] earliest CTA start, [4] latest CTA end,
+// [5] sum over CTAs of (t_mid - start), [6] sum of (end - t_mid), [7] CTAs
+//     that passed a t_mid (the resident kernel: t_mid = its partials pushed),
+// [8] sum over CTAs of (end - start), [9] CTAs,
+// [10] sum over launches of (last CTA end - first CTA start), [11] launches,
+// [12] sum over launches after the first of (first CTA start - the previous
+//      launch's end), [13] launches counted in [12],
+// [14]..[17] scratch: this launch's first start (initialise to UINT64_MAX),
+//      the previous launch's end, the CTAs of this launch seen so far, unused.
 __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
-                                            unsigned long long t_start) {
+                                            unsigned long long t_start,
+                                            unsigned long long t_mid = 0ull) {
   if (a.prof == nullptr) return;
   if (ws.slow) {
     atomicAdd(a.prof + 0, ws.ns);
@@ -272,8 +282,34 @@ __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
   if (ws.fast) atomicAdd(a.prof + 2, (unsigned long long)ws.fast);
   __syncthreads();
   if (threadIdx.x == 0) {
-    atomicMin(a.prof + 3, t_start);
-    atomicMax(a.prof + 4, ptx::globaltimer());
+    unsigned long long* P = a.prof;
+    const unsigned long long t_end = ptx::globaltimer();
+    atomicMin(P + 3, t_start);
+    atomicMax(P + 4, t_end);
+    if (t_mid) {
+      atomicAdd(P + 5, t_mid - t_start);
+      atomicAdd(P + 6, t_end - t_mid);
+      atomicAdd(P + 7, 1ull);
+    }
+    atomicAdd(P + 8, t_end - t_start);
+    atomicAdd(P + 9, 1ull);
+    atomicMin(P + 14, t_start);
+    __threadfence();
+    const unsigned long long seen = atomicAdd(P + 16, 1ull);
+    if (seen == (unsigned long long)gridDim.x * gridDim.y - 1ull) {   // the launch's last CTA
+      __threadfence();
+      const unsigned long long first = atomicAdd(P + 14, 0ull);
+      const unsigned long long prev_end = atomicAdd(P + 15, 0ull);
+      atomicAdd(P + 10, t_end - first);
+      atomicAdd(P + 11, 1ull);
+      if (prev_end != 0ull) {
+        atomicAdd(P + 12, first > prev_end ? first - prev_end : 0ull);
+        atomicAdd(P + 13, 1ull);
+      }
+      atomicExch(P + 15, t_end);
+      atomicExch(P + 14, ~0ull);
+      atomicExch(P + 16, 0ull);
+    }
   }
 }
 

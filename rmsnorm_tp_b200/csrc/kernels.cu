@@ -361,6 +361,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
     }
   }
 
+  const unsigned long long t_mid = a.prof ? ptx::globaltimer() : 0ull;
+
   // one look at every tile's slot, all loads issued back to back (independent
   // round trips), so that partials that have already arrived cost one round
   // trip for the whole team instead of one per tile
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
     }
   }
   finish_launch(rp.state, call);
-  flush_stats(a, ws, t_start);
+  flush_stats(a, ws, t_start, t_mid);
 }
 
 // ---------------------------------------------------------------------------

@@ -35,7 +35,7 @@ def test_python_binding_covers_the_header():
 
 
 def test_abi_version():
-    assert _lib.LIB.rmsnorm_tp_abi_version() == 102
+    assert _lib.LIB.rmsnorm_tp_abi_version() == 103
 
 
 @pytest.mark.parametrize("rank,tp,nmax", [(2, 2, 16), (-1, 2, 16), (0, 0, 16), (0, 9, 16), (0, 2, 0)])

@@ -23,6 +23,19 @@ def test_profile_counters_count_every_remote_wait(family):
         assert c[1] + c[2] == rows * tp * (tp - 1)
         assert c[0] >= 0 and (c[1] == 0 or c[0] > 0)
         assert 0 < c[3] <= c[4]
+        # one launch: every CTA counted once, one span, no gap yet, scratch reset
+        ctas = c[9]
+        assert ctas > 0 and ctas % tp == 0
+        assert c[11] == 1 and c[10] > 0 and c[13] == 0 and c[12] == 0
+        assert c[14] == -1 and c[16] == 0 and c[15] == c[4]
+        assert c[8] >= 0 and c[7] in (0, ctas)
+        g.forward(xs, ws)
+        torch.cuda.synchronize()
+        c2 = prof.cpu().tolist()
+        assert c2[9] == 2 * ctas and c2[11] == 2 and c2[13] == 1 and c2[12] >= 0
+        s = rtp.profile_summary(c2)
+        assert s["launch_span_us"] > 0 and s["launch_gap_us"] is not None
+        c = c2
         assert all(r["ok"] for r in check_against_oracle("bf16", xs, ws, 1e-5, outs))
         g.bufs[0].set_profile(None)
         g.forward(xs, ws)
