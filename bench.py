@@ -1032,7 +1032,7 @@ def run_sweeps(args, impl_cls, group, world, rank, dev):
         for dtype in (cfg.dtype, torch.float32):
             if dtype not in impl.dtypes:
                 continue
-            for rows in (1, 16, 128, 1024, 4096, 16384, 65536):
+            for rows in [args.rows] if args.rows else (1, 16, 128, 1024, 4096, 16384, 65536):
                 rec = measure(impl, rows, hl, dtype, cfg.seed_base + rank,
                               1000 if rows <= 1024 else 200)
                 rec.update(sweep="llama", hidden=cfg.hidden)

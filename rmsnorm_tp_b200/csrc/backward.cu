@@ -411,9 +411,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   flush_stats(a, wst, t_start);
 }
 
-// dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 8 warps
+// dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 16 warps
 // each sum a contiguous range of parts (lane = column, coalesced), and warp 0
-// adds the 8 range sums in range order -- the same order on every call.
+// adds the 16 range sums in range order -- the same order on every call.
 // ---------------------------------------------------------------------------
 // Local register backward (TP = 1: no exchange): the register backward's teams,
 // column mapping and dw slices, one row at a time but double-buffered -- the
@@ -549,25 +549,34 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   }
 }
 
+constexpr int kDwWarps = 16;
+constexpr int kDwMaxPer = (kBackwardMaxGrid + kDwWarps - 1) / kDwWarps;
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDwWarps * 32)
     backward_dw_reduce_kernel(const float* __restrict__ ws, int parts, int64_t hl,
                               T* __restrict__ dw) {
-  __shared__ float s_part[8][32];
+  __shared__ float s_part[kDwWarps][32];
   ptx::grid_dep_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t j = (int64_t)blockIdx.x * 32 + lane;
-  const int per = (parts + 7) / 8;
+  const int per = (parts + kDwWarps - 1) / kDwWarps;
   const int c0 = warp * per, c1 = min(parts, c0 + per);
+  // every load of the range in flight before the first add (one L2 round trip
+  // instead of one per part); the adds then run in part order
+  float v[kDwMaxPer];
+#pragma unroll
+  for (int i = 0; i < kDwMaxPer; ++i)
+    v[i] = (j < hl && c0 + i < c1) ? ws[(int64_t)(c0 + i) * hl + j] : 0.f;
   float s = 0.f;
-  if (j < hl)
-    for (int c = c0; c < c1; ++c) s += ws[(int64_t)c * hl + j];
+#pragma unroll
+  for (int i = 0; i < kDwMaxPer; ++i) s += v[i];
   s_part[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && j < hl) {
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += s_part[w][lane];
+    for (int w = 0; w < kDwWarps; ++w) t += s_part[w][lane];
     dw[j] = Pack<T>::from_f(t);
   }
 }
@@ -726,7 +735,7 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
 
 cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, int dtype,
                              cudaStream_t stream) {
-  const dim3 grid((unsigned)((hl + 31) / 32)), blk(256);
+  const dim3 grid((unsigned)((hl + 31) / 32)), blk(kDwWarps * 32);
   const void* fn = dtype == kF32    ? reinterpret_cast<const void*>(backward_dw_reduce_kernel<float>)
                    : dtype == kBF16 ? reinterpret_cast<const void*>(
                                           backward_dw_reduce_kernel<__nv_bfloat16>)
