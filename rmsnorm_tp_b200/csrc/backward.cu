@@ -411,9 +411,189 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   flush_stats(a, wst, t_start);
 }
 
-// dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 16 warps
-// each sum a contiguous range of parts (lane = column, coalesced), and warp 0
-// adds the 16 range sums in range order -- the same order on every call.
+// ---------------------------------------------------------------------------
+// Local ring backward (TP = 1, aligned rows; the default there): the register
+// backward's teams, rows and column mapping, but a team's rows of x and dy are
+// staged in shared memory by bulk copies -- kStages stages per team, a row's x
+// and dy on one mbarrier -- and each thread accumulates dw for its columns in
+// registers. With the row buffers out of the registers, kStages - 1 rows per
+// team are in flight while one is processed (the bytes in flight per SM are
+// set by shared memory), and dw needs no shared-memory read-modify-write per
+// row. A stage is refilled once every thread of the team is past the team
+// barrier of the following row. At the end the teams' dw registers are summed
+// in team order through shared memory into the CTA's fp32 part of the
+// workspace, as in the register kernels.
+// ---------------------------------------------------------------------------
+template <typename T, int kVec, int kW, int kBlock, int kStages>
+__global__ void __launch_bounds__(kBlock, 512 / kBlock)
+    rmsnorm_local_backward_ring_kernel(const __grid_constant__ BArgs b) {
+  constexpr int kTeams = kBlock / 32 / kW;
+  constexpr int kE = Pack<T>::kE;
+  static_assert(kTeams >= 1 && kTeams <= 15, "team count must fit the named barriers");
+  static_assert(kStages >= 2, "one stage in use, at least one in flight");
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch_dependents();
+  const KArgs& a = b.k;
+  extern __shared__ __align__(128) unsigned char smem[];   // [kTeams][kStages][x row | dy row]
+  __shared__ __align__(8) unsigned long long s_bar[kTeams][kStages];
+  __shared__ float s_red[kTeams][2][kW][2];
+  __shared__ int s_ok[kTeams][2][kW];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int team = warp / kW;
+  const int wit = warp - team * kW;
+  const RankPtrs& rp = a.rp[0];
+  const int64_t V = a.hl / kE;
+  const uint32_t row_bytes = (uint32_t)V * 16u;
+  const uint32_t stage_bytes = 2u * row_bytes;
+  const uint32_t ring_addr = ptx::smem_addr(smem) + (uint32_t)team * kStages * stage_bytes;
+  const unsigned char* ring = smem + (size_t)team * kStages * stage_bytes;
+  const uint32_t bar0 = ptx::smem_addr(&s_bar[team][0]);
+  const unsigned char* xg = reinterpret_cast<const unsigned char*>(rp.x);
+  const unsigned char* dyg = reinterpret_cast<const unsigned char*>(b.dy[0]);
+  const uint4* __restrict__ wg = ptx::launder(reinterpret_cast<const uint4*>(rp.w));
+  uint4* dxg = reinterpret_cast<uint4*>(rp.out);
+  const int64_t teams_total = (int64_t)gridDim.x * kTeams;
+  const int64_t tg = (int64_t)blockIdx.x * kTeams + team;
+  const int64_t my_rows = tg < a.rows ? (a.rows - 1 - tg) / teams_total + 1 : 0;
+  const bool producer = wit == 0 && lane == 0;
+
+  auto issue = [&](int64_t kk) {   // the team's kk-th row -> stage kk % kStages
+    const uint32_t st = (uint32_t)(kk % kStages);
+    const int64_t row = tg + kk * teams_total;
+    const uint32_t bar = bar0 + 8u * st;
+    ptx::mbar_arrive_expect_tx(bar, stage_bytes);
+    ptx::bulk_load(ring_addr + st * stage_bytes, xg + row * (int64_t)row_bytes, row_bytes, bar);
+    ptx::bulk_load(ring_addr + st * stage_bytes + row_bytes, dyg + row * (int64_t)row_bytes,
+                   row_bytes, bar);
+  };
+  int64_t issued = my_rows < kStages ? my_rows : kStages;
+  if (producer) {
+#pragma unroll
+    for (int st = 0; st < kStages; ++st) ptx::mbar_init(bar0 + 8u * st, 1u);
+    ptx::fence_mbar_init();
+    for (int64_t kk = 0; kk < issued; ++kk) issue(kk);
+  }
+  // this thread's weight vectors, and its dw columns' accumulators
+  uint4 wv[kVec];
+  float dw[kVec][kE];
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    wv[j] = c < V ? ptx::ld_cached_v4(wg + c) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int e = 0; e < kE; ++e) dw[j][e] = 0.f;
+  }
+  if constexpr (kW > 1)
+    ptx::team_bar(1 + team, kW * 32);   // the barriers' initialisation, before any wait
+  else
+    __syncwarp();
+
+  bool load_ok = true;
+  int64_t k = 0;
+  for (; k < my_rows; ++k) {
+    const int slot = (int)(k & 1);
+    const uint32_t st = (uint32_t)(k % kStages);
+    bool ok = mbar_wait_bounded(bar0 + 8u * st, (uint32_t)((k / kStages) & 1), kLoadTimeoutNs);
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + (size_t)st * stage_bytes);
+    const uint4* ds = reinterpret_cast<const uint4*>(ring + (size_t)st * stage_bytes + row_bytes);
+    float s = 0.f, d = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      const bool in = ok && c < V;
+      float xf[kE], df[kE], wf[kE];
+      Pack<T>::unpack(in ? xs[c] : make_uint4(0u, 0u, 0u, 0u), xf);
+      Pack<T>::unpack(in ? ds[c] : make_uint4(0u, 0u, 0u, 0u), df);
+      Pack<T>::unpack(wv[j], wf);
+#pragma unroll
+      for (int e = 0; e < kE; ++e) {
+        s = fmaf(xf[e], xf[e], s);
+        d = fmaf(df[e] * wf[e], xf[e], d);
+      }
+    }
+    float S = warp_allreduce_sum(s), D = warp_allreduce_sum(d);
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    if constexpr (kW > 1) {
+      if (lane == 0) {
+        s_red[team][slot][wit][0] = S;
+        s_red[team][slot][wit][1] = D;
+        s_ok[team][slot][wit] = ok ? 1 : 0;
+      }
+      ptx::team_bar(1 + team, kW * 32);
+      S = 0.f;
+      D = 0.f;
+#pragma unroll
+      for (int w = 0; w < kW; ++w) {
+        S += s_red[team][slot][w][0];
+        D += s_red[team][slot][w][1];
+        ok = ok && s_ok[team][slot][w] != 0;
+      }
+    } else {
+      __syncwarp();
+    }
+    if (!ok) {   // uniform over the team
+      load_ok = false;
+      break;
+    }
+    // every thread of the team is past its reads of the previous row's stage
+    if (producer && k >= 1 && k - 1 + kStages < my_rows) {
+      ptx::fence_proxy_async_smem();
+      issue(k - 1 + kStages);
+      ++issued;
+    }
+    const int64_t row = tg + k * teams_total;
+    const float inv = rsqrtf(S / a.hidden_f + a.eps);
+    const float coef = (inv * inv * inv) * (D / a.hidden_f);
+    // x and dy read from the stage again (it is refilled only after the next
+    // row's team barrier): fewer live registers than keeping them
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      if (c < V) {
+        float xf[kE], df[kE], wf[kE], o[kE];
+        Pack<T>::unpack(xs[c], xf);
+        Pack<T>::unpack(ds[c], df);
+        Pack<T>::unpack(wv[j], wf);
+#pragma unroll
+        for (int e = 0; e < kE; ++e) {
+          dw[j][e] += (df[e] * xf[e]) * inv;
+          o[e] = inv * (df[e] * wf[e]) - xf[e] * coef;
+        }
+        ptx::st_v4(dxg + row * V + c, Pack<T>::pack(o));
+      }
+    }
+  }
+  if (!load_ok && producer) {
+    // a copy never landed: wait (bounded) for the copies still in flight, so
+    // none lands in shared memory that this CTA no longer owns
+    for (int64_t kk = k; kk < issued; ++kk)
+      mbar_wait_bounded(bar0 + 8u * (uint32_t)(kk % kStages), (uint32_t)((kk / kStages) & 1),
+                        kLoadTimeoutNs);
+  }
+  __syncthreads();   // every stage read and every copy landed: the ring becomes [kTeams][hl] fp32
+  float* s_dw = reinterpret_cast<float*>(smem);
+  float* tdw = s_dw + (int64_t)team * a.hl;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    if (c < V) {
+#pragma unroll
+      for (int e = 0; e < kE; e += 4)
+        *reinterpret_cast<float4*>(tdw + (int64_t)c * kE + e) =
+            make_float4(dw[j][e], dw[j][e + 1], dw[j][e + 2], dw[j][e + 3]);
+    }
+  }
+  __syncthreads();
+  float* wsr = b.ws[0] + (int64_t)blockIdx.x * a.hl;
+  for (int64_t i = threadIdx.x; i < a.hl; i += kBlock) {
+    float acc = s_dw[i];
+#pragma unroll
+    for (int t = 1; t < kTeams; ++t) acc += s_dw[(int64_t)t * a.hl + i];
+    wsr[i] = acc;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Local register backward (TP = 1: no exchange): the register backward's teams,
 // column mapping and dw slices, one row at a time but double-buffered -- the
@@ -549,6 +729,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   }
 }
 
+// dw[j] = sum over the parts of ws[part][j]: a CTA takes 32 columns; its 16 warps
+// each sum a contiguous range of parts (lane = column, coalesced), and warp 0
+// adds the 16 range sums in range order -- the same order on every call.
 constexpr int kDwWarps = 16;
 constexpr int kDwMaxPer = (kBackwardMaxGrid + kDwWarps - 1) / kDwWarps;
 
@@ -637,6 +820,32 @@ struct BwdLocalTable {
 #undef RTP_BWDL
 };
 
+// the ring kernel: the same (vec, w) shapes; the block of the last shape is
+// 512 threads (one team), the others 256; three stages per team, so a CTA's
+// ring is at most 3 x 2 rows x 32 KB x 1 team = 192 KB (one CTA per SM), else
+// at most 96 KB (two CTAs per SM)
+constexpr int kBwdRingStages = 3;
+template <typename T>
+struct BwdRingTable {
+#define RTP_BWDR(V, W, B) rmsnorm_local_backward_ring_kernel<T, V, W, B, kBwdRingStages>
+  static constexpr BwdFn fn[kNumBwdShapes] = {
+      RTP_BWDR(1, 1, 256), RTP_BWDR(2, 1, 256), RTP_BWDR(4, 1, 256), RTP_BWDR(4, 2, 256),
+      RTP_BWDR(4, 4, 256), RTP_BWDR(4, 8, 256), RTP_BWDR(4, 16, 512),
+  };
+#undef RTP_BWDR
+};
+
+BwdFn backward_ring_fn(int dtype, int shape) {
+  switch (dtype) {
+    case kF32:
+      return BwdRingTable<float>::fn[shape];
+    case kBF16:
+      return BwdRingTable<__nv_bfloat16>::fn[shape];
+    default:
+      return BwdRingTable<__half>::fn[shape];
+  }
+}
+
 BwdFn backward_local_fn(int dtype, int shape) {
   switch (dtype) {
     case kF32:
@@ -660,6 +869,7 @@ BwdFn backward_vec_fn(int dtype, int shape) {
 }
 std::atomic<unsigned int> g_vec_smem_set[kMaxDevices][3][kNumBwdShapes];
 std::atomic<unsigned int> g_local_smem_set[kMaxDevices][3][kNumBwdShapes];
+std::atomic<unsigned int> g_ring_smem_set[kMaxDevices][3][kNumBwdShapes];
 
 }  // namespace
 
@@ -683,19 +893,28 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   if (vec16 && get_family() != kFamilyBulk)
     for (int i = 0; i < kNumBwdShapes && shape < 0; ++i)
       if (V <= 32ll * kBwdShapes[i].w * kBwdShapes[i].vec) shape = i;
-  // TP = 1 (no exchange): the double-buffered local register kernel
+  // TP = 1 (no exchange): the ring kernel (bulk copies of x and dy into shared
+  // memory), or with the register family forced the double-buffered register kernel
   const bool local = shape >= 0 && a.tp == 1 && !a.emulated;
-  const BwdFn fn = local ? backward_local_fn(dtype, shape)
-                         : shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
+  const bool ring = local && get_family() != kFamilyRegister;
+  const BwdFn fn = ring    ? backward_ring_fn(dtype, shape)
+                   : local ? backward_local_fn(dtype, shape)
+                   : shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
   const int block = shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
   const void* fp = reinterpret_cast<const void*>(fn);
-  // dw partials: one [hl] fp32 slice per team (register kernel) or per CTA
+  // dw partials: one [hl] fp32 slice per team (register kernels) or per CTA; the
+  // ring kernel's shared memory is its stages (which later hold the slices)
   const int teams = shape >= 0 ? kBwdShapes[shape].block / 32 / kBwdShapes[shape].w : 1;
-  const size_t smem = (size_t)teams * (size_t)a.hl * sizeof(float);
+  size_t smem = (size_t)teams * (size_t)a.hl * sizeof(float);
+  if (ring) {
+    const size_t stages = (size_t)teams * kBwdRingStages * 2u * (size_t)V * 16u;
+    if (stages > smem) smem = stages;
+  }
   cudaError_t err;
   if (smem > 48u * 1024u) {
     const bool cacheable = device >= 0 && device < kMaxDevices;
-    std::atomic<unsigned int>& set = local        ? g_local_smem_set[device][dtype][shape]
+    std::atomic<unsigned int>& set = ring         ? g_ring_smem_set[device][dtype][shape]
+                                     : local      ? g_local_smem_set[device][dtype][shape]
                                      : shape >= 0 ? g_vec_smem_set[device][dtype][shape]
                                                   : g_smem_set[device][dtype][vec16 ? 1 : 0];
     if (!cacheable || set.load() < smem) {

@@ -259,6 +259,20 @@ __device__ __forceinline__ float push_poll(const KArgs& a, int rank, const RankP
   return poll_slot(a, rank, rp, buf, tag, call, row, q, active, mine, failed, ws);
 }
 
+// Wait (bounded) for an mbarrier phase that a bulk copy completes; false when
+// the copy has not landed within limit_ns.
+constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  unsigned long long limit_ns) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (;;) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (ptx::globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
 // Adds the lanes' wait counters and the CTA's timings to KArgs::prof (global
 // timer, ns; every CTA of a launch calls this exactly once, at its end):
 // [0] wait ns summed over lanes, [1] slow waits, [2] fast waits,

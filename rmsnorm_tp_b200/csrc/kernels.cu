@@ -690,17 +690,6 @@ __global__ void __launch_bounds__(kBlock)
 // faster than none.) Tiles go to warps round-robin (tile t -> warp
 // t mod all warps), the same on every rank, over at most one resident wave.
 // ---------------------------------------------------------------------------
-constexpr unsigned long long kLoadTimeoutNs = 2000000000ull;   // a bulk copy that never lands
-
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  unsigned long long limit_ns) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = ptx::globaltimer();
-  for (;;) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if (ptx::globaltimer() - t0 > limit_ns) return false;
-  }
-}
 
 // kRes (fused residual add): a stage holds the x tile and, stage_bytes / 2
 // further, the residual tile (two copies on the same mbarrier); the reduction

@@ -44,10 +44,20 @@ def bwd_family(request):
     rtp.set_kernel_family("auto")
 
 
+@pytest.fixture(params=["auto", "register", "bulk"])
+def local_bwd_family(request):
+    """TP = 1: the ring kernel (automatic choice for aligned rows: bulk copies of
+    x and dy into shared memory), the double-buffered register kernel (register
+    family) and the one-CTA-per-row kernel (bulk family)."""
+    rtp.set_kernel_family(request.param)
+    yield request.param
+    rtp.set_kernel_family("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hidden", [37, 96, 512, 4096, 8192, 16384])
 @pytest.mark.parametrize("rows", [1, 7, 300, 2500])
-def test_local_backward(bwd_family, dtype, hidden, rows):
+def test_local_backward(local_bwd_family, dtype, hidden, rows):
     xs, ws, dys = _inputs(rows, hidden, 1, dtype, 13)
     dx, dw = rtp.local_rmsnorm_backward(dys[0], xs[0], ws[0], 1e-6)
     torch.cuda.synchronize()
