@@ -911,7 +911,8 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
     if (stages > smem) smem = stages;
   }
   cudaError_t err;
-  if (smem > 48u * 1024u) {
+  // the 48 KB default limit counts static shared memory too: raise it early
+  if (smem > 32u * 1024u) {
     const bool cacheable = device >= 0 && device < kMaxDevices;
     std::atomic<unsigned int>& set = ring         ? g_ring_smem_set[device][dtype][shape]
                                      : local      ? g_local_smem_set[device][dtype][shape]

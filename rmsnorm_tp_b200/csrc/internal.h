@@ -142,11 +142,13 @@ cudaError_t launch_dw_reduce(const float* ws, int parts, int64_t hl, void* dw, i
 //
 // Receive region of a rank (inside its IPC-mapped mailbox allocation, after
 // the slots and the probe area): flags u32 [2 buffers][tp src][mblocks][nblocks]
-// (a tile of 128 rows x 128 columns from src has landed when its flag equals the
-// call's tag), then partials T [tp src][num_max_rows][hl].
+// (a tile of 128 rows x the call's tile width from src has landed when its flag
+// equals the call's tag; nblocks counts the narrowest, 64-column tiles), then
+// partials T [tp src][num_max_rows][hl].
 // ---------------------------------------------------------------------------
 constexpr int kLinTileM = 128;
-constexpr int kLinTileN = 128;
+constexpr int kLinTileN = 128;      // hidden / tp must be a multiple of this
+constexpr int kLinTileNMin = 64;    // the narrowest tile width of a call
 constexpr int kLinTileK = 64;
 
 struct LinearLayout {
@@ -190,6 +192,8 @@ struct alignas(64) LArgs {
 // grid_y > 1: emulated ranks on one GPU). `as`/`ws`: per rank A_r and W_r.
 cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws, int dtype,
                           int device, int grid_y, cudaStream_t stream);
+// Tile width (64, 128 or 256 columns) launch_linear picks for a call.
+int linear_tile_width(int64_t rows, int64_t hidden, int64_t hl, int sms);
 
 cudaError_t launch_probe(unsigned long long* remote_slot, unsigned long long* local_slot,
                          unsigned long long seq, int iters, int initiator,

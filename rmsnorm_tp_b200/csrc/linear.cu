@@ -56,13 +56,16 @@ constexpr uint32_t kLinPitch = 128 * 2 + 16;                        // staging r
 constexpr uint32_t kLinStagingBytes = kLinTileM * kLinPitch;        // 128 columns at a time
 constexpr unsigned long long kLinWaitNs = 2000000000ull;           // an internal wait that never ends
 
-// Tile shapes: 128 rows x kBN columns (128 or 256) per tile, 64-element K steps.
-// 256-column tiles load 48 KB per K step for 4.2 MFLOP (128-column: 32 KB for
-// 2.1 MFLOP), so they need less L2 bandwidth per FLOP; they take the whole
-// tensor memory (two 256-column fp32 accumulators) and 3 ring stages.
+// Tile shapes: 128 rows x kBN columns (64, 128 or 256) per tile, 64-element K
+// steps. 256-column tiles load 48 KB per K step for 4.2 MFLOP (128-column: 32 KB
+// for 2.1 MFLOP), so they need less L2 bandwidth per FLOP; they take the whole
+// tensor memory (two 256-column fp32 accumulators) and 3 ring stages. 64-column
+// tiles serve calls of few row blocks, where wider tiles would leave most SMs
+// idle while the weights stream from HBM (6 stages of 24 KB in flight).
 template <int kBN>
 struct LinCfg {
-  static constexpr int kStages = kBN == 256 ? 3 : 4;
+  static_assert(kBN == 64 || kBN == 128 || kBN == 256, "tile width");
+  static constexpr int kStages = kBN == 256 ? 3 : kBN == 128 ? 4 : 6;
   static constexpr uint32_t kABytes = kLinTileM * kLinTileK * 2;    // 16 KB
   static constexpr uint32_t kBBytes = kBN * kLinTileK * 2;          // 16 or 32 KB
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -277,12 +280,14 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       unsigned char* dst = a.region[owner] + a.recv_off +
                            (((int64_t)rank * a.nmax + mb * kLinTileM) * hl + nbo * kBN) *
                                (int64_t)sizeof(T);
+      constexpr int kCW = kBN < 128 ? kBN : 128;   // columns per pass through the staging
+      constexpr int kChunks = kCW * 2 / 16;         // 16-byte chunks of a staged row
 #pragma unroll 1
-      for (int h = 0; h < kBN / 128; ++h) {   // 128 columns at a time through the staging
+      for (int h = 0; h < kBN / kCW; ++h) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kCW / 32; ++c) {
           uint32_t r[32];
-          sm100::tmem_ld_32x32(tmem + (uint32_t)(acc * kBN + h * 128 + c * 32) +
+          sm100::tmem_ld_32x32(tmem + (uint32_t)(acc * kBN + h * kCW + c * 32) +
                                    ((uint32_t)(q4 * 32) << 16),
                                r);
           sm100::tmem_wait_ld();
@@ -296,19 +301,20 @@ __global__ void __launch_bounds__(kLinThreads, 1)
             *reinterpret_cast<uint4*>(srow + c * 64 + j * 16) = v;
           }
         }
-        if (h == kBN / 128 - 1) {   // the whole accumulator has been read
+        if (h == kBN / kCW - 1) {   // the whole accumulator has been read
           sm100::fence_before_sync();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(bar_acce + 8u * acc);
         }
         ptx::team_bar(1, 128);   // staging complete
-        // 128 rows x 256 bytes; a warp instruction stores 2 rows x 256 contiguous bytes
-        for (int idx = et; idx < kLinTileM * 16; idx += 128) {
-          const int i = idx >> 4, ch = idx & 15;
+        // 128 rows x kCW * 2 bytes; a warp instruction stores whole rows of the pass
+        // (2 rows x 256 contiguous bytes at 128 columns, 4 x 128 at 64)
+        for (int idx = et; idx < kLinTileM * kChunks; idx += 128) {
+          const int i = idx / kChunks, ch = idx % kChunks;
           if (mb * kLinTileM + i < a.rows) {
             const uint4 v =
                 *reinterpret_cast<const uint4*>(staging + (size_t)i * kLinPitch + ch * 16);
-            ptx::st_v4(dst + (int64_t)i * hl * (int64_t)sizeof(T) + h * 256 + ch * 16, v);
+            ptx::st_v4(dst + (int64_t)i * hl * (int64_t)sizeof(T) + h * kCW * 2 + ch * 16, v);
           }
         }
         ptx::team_bar(1, 128);   // every store issued (and the staging free)
@@ -440,7 +446,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 LinearLayout linear_layout(int tp, int64_t nmax, int64_t hidden, int64_t base) {
   LinearLayout L{};
   L.mblocks = (nmax + kLinTileM - 1) / kLinTileM;
-  L.nblocks = hidden / tp / kLinTileN;   // flags for the narrowest tiles (128 columns)
+  L.nblocks = hidden / tp / kLinTileNMin;   // flags for the narrowest tiles (64 columns)
   L.flags_off = (base + 1023) & ~(int64_t)1023;
   const int64_t flag_bytes = 2 * (int64_t)tp * L.mblocks * L.nblocks * 4;
   L.recv_off = (L.flags_off + flag_bytes + 1023) & ~(int64_t)1023;
@@ -489,15 +495,31 @@ cudaError_t encode_2d(EncodeTiledFn fn, unsigned char* out, const void* base, in
 }
 
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_lin_attr[kMaxDevices][2][2];
+std::atomic<int> g_lin_attr[kMaxDevices][2][3];
 
-const void* linear_kernel(int dtype, int bn) {
-  if (dtype == kBF16)
-    return bn == 256 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16, 256>)
-                     : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__nv_bfloat16, 128>);
-  return bn == 256 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half, 256>)
-                   : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<__half, 128>);
+template <typename T>
+const void* linear_kernel_of(int bn) {
+  return bn == 256   ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 256>)
+         : bn == 128 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 128>)
+                     : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 64>);
 }
+const void* linear_kernel(int dtype, int bn) {
+  return dtype == kBF16 ? linear_kernel_of<__nv_bfloat16>(bn) : linear_kernel_of<__half>(bn);
+}
+uint32_t linear_smem(int bn) {
+  return bn == 256 ? LinCfg<256>::kSmem : bn == 128 ? LinCfg<128>::kSmem : LinCfg<64>::kSmem;
+}
+}  // namespace
+
+// Tile width of a call: the widest of 256 (when every owner's columns are whole
+// 256-column tiles), 128 and 64 that still gives every SM a tile; 64 otherwise.
+int linear_tile_width(int64_t rows, int64_t hidden, int64_t hl, int sms) {
+  const int64_t mt = (rows + kLinTileM - 1) / kLinTileM;
+  if (hl % 256 == 0 && mt * (hidden / 256) >= sms) return 256;
+  if (mt * (hidden / 128) >= sms) return 128;
+  return 64;
+}
+namespace {
 }  // namespace
 
 static_assert(sizeof(CUtensorMap) == 128, "a tensor map is 128 bytes");
@@ -509,10 +531,12 @@ cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws
   const EncodeTiledFn fn = encode_tiled(&err);
   if (err != cudaSuccess) return err;
   const int nranks = a.emulated ? grid_y : 1;
-  // 256-column tiles whenever every owner's columns are whole 256-column tiles
-  const int bn = (a.hl % 256 == 0) ? 256 : 128;
+  int sms = 0;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return err;
+  const int bn = linear_tile_width(a.rows, a.hidden, a.hl, sms / (grid_y > 1 ? grid_y : 1));
   a.nblocks = a.hl / bn;
-  const uint32_t smem = bn == 256 ? LinCfg<256>::kSmem : LinCfg<128>::kSmem;
+  const uint32_t smem = linear_smem(bn);
   for (int r = 0; r < nranks; ++r) {
     err = encode_2d(fn, a.tmaps[2 * r], as[r], dtype, (uint64_t)a.k, (uint64_t)a.rows, kLinTileM);
     if (err != cudaSuccess) return err;
@@ -521,7 +545,7 @@ cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws
     if (err != cudaSuccess) return err;
   }
   const void* kfn = linear_kernel(dtype, bn);
-  const int ti = dtype == kBF16 ? 0 : 1, bi = bn == 256 ? 1 : 0;
+  const int ti = dtype == kBF16 ? 0 : 1, bi = bn == 256 ? 2 : bn == 128 ? 1 : 0;
   const bool cacheable = device >= 0 && device < kMaxDevices;
   if (!cacheable || g_lin_attr[device][ti][bi].load() == 0) {
     err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -531,10 +555,8 @@ cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws
     if (err != cudaSuccess) return err;
     if (cacheable) g_lin_attr[device][ti][bi].store(1);
   }
-  int per_sm = 0, sms = 0;
+  int per_sm = 0;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kLinThreads, smem);
-  if (err != cudaSuccess) return err;
-  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return err;
   const int64_t resident = (int64_t)per_sm * sms / (grid_y > 1 ? grid_y : 1);
   const int64_t tiles = ((a.rows + kLinTileM - 1) / kLinTileM) * (a.hidden / bn);

@@ -87,11 +87,15 @@ def test_rows_vary_between_calls_and_tiles_of_every_owner():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_tp1_module(dtype):
-    """TP = 1: the GEMM and the norm without an exchange."""
-    name, rows, k, hidden = NAMES[dtype], 200, 512, 1024
+@pytest.mark.parametrize("rows,k,hidden", [(200, 512, 1024),    # 64-column tiles (few row blocks)
+                                           (1280, 128, 2048),   # 128-column tiles
+                                           (2048, 256, 4096)])  # 256-column tiles
+def test_tp1_module(dtype, rows, k, hidden):
+    """TP = 1: the GEMM and the norm without an exchange, at every tile width
+    (the widest that still gives each of the 148 SMs a tile)."""
+    name = NAMES[dtype]
     as_, lws, gs = make_linear_group(rows, k, hidden, 1, dtype, 3, device="cuda")
-    m = rtp.FusedTPLinearRMSNorm(hidden, eps=1e-5, num_max_rows=256)
+    m = rtp.FusedTPLinearRMSNorm(hidden, eps=1e-5, num_max_rows=rows)
     try:
         y = m.forward(as_[0], lws[0], gs[0])
         torch.cuda.synchronize()
