@@ -820,17 +820,20 @@ struct BwdLocalTable {
 #undef RTP_BWDL
 };
 
-// the ring kernel: the same (vec, w) shapes; the block of the last shape is
-// 512 threads (one team), the others 256; three stages per team, so a CTA's
-// ring is at most 3 x 2 rows x 32 KB x 1 team = 192 KB (one CTA per SM), else
-// at most 96 KB (two CTAs per SM)
+// the ring kernel: the same (vec, w) shapes; teams of two or more warps in
+// 512-thread CTAs (one CTA per SM: a ring of 3 stages x 2 rows per team is at
+// most 192 KB, and one dw part per SM instead of two halves the workspace and
+// the reduction), single-warp teams in 256-thread CTAs (two per SM)
 constexpr int kBwdRingStages = 3;
+constexpr int kBwdRingBlock[kNumBwdShapes] = {256, 256, 256, 512, 512, 512, 512};
+// below this many rows the register kernel's shorter start wins
+constexpr int64_t kBwdRingMinRows = 1024;
 template <typename T>
 struct BwdRingTable {
-#define RTP_BWDR(V, W, B) rmsnorm_local_backward_ring_kernel<T, V, W, B, kBwdRingStages>
+#define RTP_BWDR(V, W, I) rmsnorm_local_backward_ring_kernel<T, V, W, kBwdRingBlock[I], kBwdRingStages>
   static constexpr BwdFn fn[kNumBwdShapes] = {
-      RTP_BWDR(1, 1, 256), RTP_BWDR(2, 1, 256), RTP_BWDR(4, 1, 256), RTP_BWDR(4, 2, 256),
-      RTP_BWDR(4, 4, 256), RTP_BWDR(4, 8, 256), RTP_BWDR(4, 16, 512),
+      RTP_BWDR(1, 1, 0), RTP_BWDR(2, 1, 1), RTP_BWDR(4, 1, 2), RTP_BWDR(4, 2, 3),
+      RTP_BWDR(4, 4, 4), RTP_BWDR(4, 8, 5), RTP_BWDR(4, 16, 6),
   };
 #undef RTP_BWDR
 };
@@ -896,15 +899,15 @@ cudaError_t launch_backward(const BArgs& b, int dtype, int device, int grid_y, c
   // TP = 1 (no exchange): the ring kernel (bulk copies of x and dy into shared
   // memory), or with the register family forced the double-buffered register kernel
   const bool local = shape >= 0 && a.tp == 1 && !a.emulated;
-  const bool ring = local && get_family() != kFamilyRegister;
+  const bool ring = local && get_family() != kFamilyRegister && a.rows >= kBwdRingMinRows;
   const BwdFn fn = ring    ? backward_ring_fn(dtype, shape)
                    : local ? backward_local_fn(dtype, shape)
                    : shape >= 0 ? backward_vec_fn(dtype, shape) : backward_fn(dtype, vec16);
-  const int block = shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
+  const int block = ring ? kBwdRingBlock[shape] : shape >= 0 ? kBwdShapes[shape].block : kBwdBlock;
   const void* fp = reinterpret_cast<const void*>(fn);
   // dw partials: one [hl] fp32 slice per team (register kernels) or per CTA; the
   // ring kernel's shared memory is its stages (which later hold the slices)
-  const int teams = shape >= 0 ? kBwdShapes[shape].block / 32 / kBwdShapes[shape].w : 1;
+  const int teams = shape >= 0 ? block / 32 / kBwdShapes[shape].w : 1;
   size_t smem = (size_t)teams * (size_t)a.hl * sizeof(float);
   if (ring) {
     const size_t stages = (size_t)teams * kBwdRingStages * 2u * (size_t)V * 16u;
