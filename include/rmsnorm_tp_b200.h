@@ -245,8 +245,8 @@ int rmsnorm_tp_poll_error(const rmsnorm_tp_comm* comm, uint32_t* code);
 int rmsnorm_tp_status(rmsnorm_tp_comm* comm, rmsnorm_tp_status_info* out);
 
 /* Blocking: wait for the device, zero the mailbox, clear the failure record
- * and set the generation counter to `generation`. Every rank must call it
- * between two group barriers, with the same generation. */
+ * and set the generation counter to `generation` (at most 2^44 - 1). Every
+ * rank must call it between two group barriers, with the same generation. */
 int rmsnorm_tp_reset(rmsnorm_tp_comm* comm, uint64_t generation);
 
 /* Blocking: read the device generation counter (launches completed). */

@@ -876,19 +876,22 @@ int rmsnorm_tp_status(rmsnorm_tp_comm* c, rmsnorm_tp_status_info* out) {
   out->expected_tag = st.err_expected;
   out->seen_tag = st.err_seen;
   out->generation = st.err_call;
-  out->next_generation = st.call;
+  out->next_generation = st.call >> rtp::kGenShift;
   return RMSNORM_TP_OK;
 }
 
 int rmsnorm_tp_reset(rmsnorm_tp_comm* c, uint64_t generation) {
   if (!c) return fail(RMSNORM_TP_ERR_INVALID, "reset: NULL communicator");
+  if (generation > rtp::kGenMax)
+    return fail(RMSNORM_TP_ERR_INVALID, "reset: generation %llu above the counter's %llu",
+                (unsigned long long)generation, (unsigned long long)rtp::kGenMax);
   DeviceGuard guard(c->device);
   if (guard.err != cudaSuccess) return cuda_fail(guard.err, "reset: cudaSetDevice");
   RTP_CUDA(cudaDeviceSynchronize(), "reset: cudaDeviceSynchronize");
   RTP_CUDA(cudaMemset(c->mailbox, 0, c->mailbox_bytes), "reset: zero mailbox");
   DeviceState st;
   std::memset(&st, 0, sizeof(st));
-  st.call = generation;
+  st.call = generation << rtp::kGenShift;
   RTP_CUDA(cudaMemcpy(c->state, &st, sizeof(st), cudaMemcpyHostToDevice), "reset: write state");
   RTP_CUDA(cudaDeviceSynchronize(), "reset: cudaDeviceSynchronize");
   *reinterpret_cast<volatile unsigned*>(c->host_flag) = 0u;
@@ -903,7 +906,7 @@ int rmsnorm_tp_get_generation(rmsnorm_tp_comm* c, uint64_t* out) {
   unsigned long long g = 0;
   RTP_CUDA(cudaMemcpy(&g, &c->state->call, sizeof(g), cudaMemcpyDeviceToHost),
            "get_generation: copy");
-  *out = g;
+  *out = g >> rtp::kGenShift;
   return RMSNORM_TP_OK;
 }
 

@@ -610,7 +610,7 @@ __global__ void __launch_bounds__(kBlock)
   unsigned long long call = 0ull;
   uint32_t buf = 0u, tag = 0u;
   if (exchange) {
-    if (threadIdx.x == 0) s_call = *reinterpret_cast<volatile unsigned long long*>(&rp.state->call);
+    if (threadIdx.x == 0) s_call = read_generation(rp.state);
     __syncthreads();
     call = s_call;
     buf = buffer_of(call);

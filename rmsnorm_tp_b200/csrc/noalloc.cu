@@ -176,7 +176,7 @@ extern "C" int rmsnorm_tp_forward_group_static_status(rmsnorm_tp_status_info* ou
     if (e != cudaSuccess)
       return fail_static(RMSNORM_TP_ERR_CUDA, "forward_group_static_status: reading state: %s",
                          cudaGetErrorString(e));
-    if (r == 0) out->next_generation = st.call;
+    if (r == 0) out->next_generation = st.call >> rtp::kGenShift;
     if (st.err_code != rtp::kStatusOk && out->code == rtp::kStatusOk) {
       out->code = st.err_code;
       out->src_rank = st.err_src;

@@ -40,9 +40,22 @@ enum DeviceStatus : uint32_t {
 };
 
 // Per-rank state in local device memory (never mapped to peers).
+// The generation counter advances without a returning atomic: `call` holds
+// kGenUnit x (the generation of the next launch) plus the shares that the CTAs
+// of a running launch have added so far. At its end, CTA 0 of a launch adds
+// step x kGenUnit - (grid - 1) and every other CTA adds 1 (fire-and-forget), so
+// a finished launch of any grid size advances `call` by exactly step x kGenUnit.
+// A CTA reads `call` before it adds its own share, so it sees at most
+// kGenUnit - 1 of its launch's shares and call >> kGenShift is the launch's
+// generation (grids stay far below kGenUnit CTAs); the next launch reads it
+// only after this grid has completed.
+constexpr int kGenShift = 20;
+constexpr unsigned long long kGenUnit = 1ull << kGenShift;
+constexpr unsigned long long kGenMax = (1ull << (64 - kGenShift)) - 1ull;   // largest generation
+
 struct alignas(64) DeviceState {
-  unsigned long long call;      // launches completed so far = generation of the next launch
-  unsigned int done;            // CTAs of the running launch that have finished
+  unsigned long long call;      // kGenUnit x generation of the next launch (+ running shares)
+  unsigned int done;            // unused
   unsigned int abort;           // set once any CTA gave up; the rest give up fast
   unsigned int err_code;        // first failure (DeviceStatus), set with atomicCAS
   unsigned int err_src;         // source rank whose partial never arrived

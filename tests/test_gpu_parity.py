@@ -243,6 +243,34 @@ def test_stress_pattern_zero_rows_and_outlier_channels(family):
     _sampled_oracle_check("bf16", xs, ws, cfg.eps, outs, n=128)
 
 
+def test_generation_counter_at_its_top_and_every_grid_size(family):
+    """The device counter advances by exactly one per forward launch and two per
+    backward launch whatever the grid (row counts from 1 to many waves), up to
+    the largest generation it holds; a larger reset is an argument error."""
+    tp, hl = 2, 1024
+    top = 2**44 - 1
+    g = rtp.EmulatedTPGroup(tp, eps=1e-5, num_max_rows=70000, timeout_s=5.0)
+    try:
+        with pytest.raises(rtp.RMSNormTPError):
+            g.bufs[0].reset(top + 1)
+        g.reset(top - 20)
+        n = 0
+        for rows in (1, 7, 300, 4096, 70000, 1):
+            xs, ws = make_group(rows, hl * tp, tp, torch.bfloat16, rows, device="cuda")
+            outs = g.forward(xs, ws)
+            n += 1
+            torch.cuda.synchronize()
+            _sampled_oracle_check("bf16", xs, ws, 1e-5, outs, n=min(rows, 64))
+            assert all(b.device_generation() == top - 20 + n for b in g.bufs)
+        dys = [torch.randn_like(x) for x in xs]
+        g.backward(dys, xs, ws)
+        torch.cuda.synchronize()
+        assert all(b.device_generation() == top - 20 + n + 2 for b in g.bufs)
+        assert all(b.status()["next_generation"] == top - 20 + n + 2 for b in g.bufs)
+    finally:
+        g.destroy()
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_prefill_config_full_size_tp8(family, dtype):
     cfg = BY_NAME["prefill"]
