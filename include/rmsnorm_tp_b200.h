@@ -224,7 +224,7 @@ int rmsnorm_local_backward(void* dx, void* dw, const void* dy, const void* x, co
 int rmsnorm_tp_set_timeout(rmsnorm_tp_comm* comm, uint64_t timeout_ns);
 
 /* Optional in-kernel counters for later launches of this communicator (NULL
- * turns them off): dev_counters points to 18 uint64 in device memory that the
+ * turns them off): dev_counters points to 20 uint64 in device memory that the
  * kernels add to (times in ns of the GPU global timer) -- [0] ns spent waiting
  * for peers' partial sums (summed over waiting lanes), [1] waits that found the
  * slot not yet written, [2] waits satisfied by the first poll, [3] earliest CTA
@@ -233,8 +233,9 @@ int rmsnorm_tp_set_timeout(rmsnorm_tp_comm* comm, uint64_t timeout_ns);
  * kernel only), [8] sum of start -> end, [9] CTAs; per launch: [10] sum of
  * first CTA start -> last CTA end, [11] launches, [12] sum of the gaps between
  * one launch's last CTA end and the next launch's first CTA start, [13] gaps
- * counted; [14]..[17] scratch. Initialise [3] and [14] to UINT64_MAX, the rest
- * to 0. */
+ * counted; [14]..[16] scratch; [17] sum over the CTAs of every launch but the
+ * first of (CTA start - the previous launch's end), [18] those CTAs; [19]
+ * unused. Initialise [3] and [14] to UINT64_MAX, the rest to 0. */
 int rmsnorm_tp_set_profile(rmsnorm_tp_comm* comm, uint64_t* dev_counters);
 
 /* Non-blocking: nonzero in *code once a launch has recorded a device failure
@@ -371,7 +372,7 @@ const char* rmsnorm_tp_last_error(void);
  * added rmsnorm_tp_forward_group_static_status, the batch kernel family
  * (rmsnorm_tp_set_kernel_family(3)), the push encodings and the fused
  * row-parallel linear entry points; 1.03 widened the profile counters of
- * rmsnorm_tp_set_profile from 5 to 18. */
+ * rmsnorm_tp_set_profile from 5 to 20. */
 int rmsnorm_tp_abi_version(void);
 
 #ifdef __cplusplus

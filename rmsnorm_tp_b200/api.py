@@ -274,7 +274,7 @@ class TPCommBuffer:
         check(LIB.rmsnorm_tp_set_timeout(self._comm, int(seconds * 1e9)), "rmsnorm_tp_set_timeout")
 
     def set_profile(self, counters: Optional[torch.Tensor]) -> None:
-        """Point later launches at 18 int64 device counters (see profile_counters), or None."""
+        """Point later launches at 20 int64 device counters (see profile_counters), or None."""
         ptr = None if counters is None else ctypes.c_void_p(counters.data_ptr())
         check(LIB.rmsnorm_tp_set_profile(self._comm, ptr), "rmsnorm_tp_set_profile")
 
@@ -735,15 +735,17 @@ class _TPRMSNormFunction(torch.autograd.Function):
         return None, dx, dw
 
 
-PROFILE_COUNTERS = 18
+PROFILE_COUNTERS = 20
 
 
 def profile_counters(device=None) -> torch.Tensor:
-    """Fresh in-kernel counters for TPCommBuffer.set_profile: int64[18] =
+    """Fresh in-kernel counters for TPCommBuffer.set_profile: int64[20] =
     [wait ns, slow waits, fast waits, earliest CTA start, latest CTA end,
     sum of CTA start -> partials pushed, sum of pushed -> CTA end, CTAs with the
     pushed mark, sum of CTA start -> end, CTAs, sum of launch spans, launches,
-    sum of gaps between launches, gaps, 4 x scratch] (ns of the GPU timer)."""
+    sum of gaps between launches, gaps, 3 x scratch, sum of CTA start delays
+    after the previous launch's end, CTAs counted there, unused] (ns of the
+    GPU timer)."""
     t = torch.zeros(PROFILE_COUNTERS, dtype=torch.int64, device=device or "cuda")
     t[3] = -1    # UINT64_MAX for the atomicMin of the start time
     t[14] = -1   # and for the per-launch first start
@@ -751,13 +753,14 @@ def profile_counters(device=None) -> torch.Tensor:
 
 
 def profile_summary(v) -> dict:
-    """Readable means of profile_counters values (a list of 18 ints)."""
+    """Readable means of profile_counters values (a list of 20 ints)."""
     u = [x & 0xFFFFFFFFFFFFFFFF for x in v]
     polls = u[1] + u[2]
     d = lambda a, b: round(u[a] / u[b] / 1e3, 3) if u[b] else None
     return {"polls": polls, "slow_poll_share": round(u[1] / max(1, polls), 4),
             "mean_wait_us": round(u[0] / max(1, u[1]) / 1e3, 3),
             "launch_span_us": d(10, 11), "launch_gap_us": d(12, 13),
+            "cta_start_delay_us": d(17, 18),
             "cta_us": d(8, 9), "cta_load_reduce_push_us": d(5, 7),
             "cta_poll_store_us": d(6, 7)}
 

@@ -129,7 +129,7 @@ struct rmsnorm_tp_comm {
   bool finalized = false;
   unsigned long long probe_seq = 0;
   unsigned char uuid[16] = {};
-  unsigned long long* prof = nullptr;      // optional device counters (18 x u64)
+  unsigned long long* prof = nullptr;      // optional device counters (20 x u64)
   int64_t linear_hidden = 0;               // fused linear: hidden width of the receive region
   rtp::LinearLayout lin{};                 // fused linear: layout of the receive region
 };

@@ -274,7 +274,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 }
 
 // Adds the lanes' wait counters and the CTA's timings to KArgs::prof (global
-// timer, ns; every CTA of a launch calls this exactly once, at its end):
+// timer, ns; every CTA of a launch calls this exactly once, at its end, with
+// every thread). The CTA's end is stamped once all its threads arrive and
+// before any counter is written; the lanes' counters are summed per CTA first
+// (warp shuffles, then shared memory), so a CTA makes one global atomic per
+// counter and the counters disturb the timings they record as little as possible:
 // [0] wait ns summed over lanes, [1] slow waits, [2] fast waits,
 // [3] earliest CTA start, [4] latest CTA end,
 // [5] sum over CTAs of (t_mid - start), [6] sum of (end - t_mid), [7] CTAs
@@ -283,21 +287,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 // [10] sum over launches of (last CTA end - first CTA start), [11] launches,
 // [12] sum over launches after the first of (first CTA start - the previous
 //      launch's end), [13] launches counted in [12],
-// [14]..[17] scratch: this launch's first start (initialise to UINT64_MAX),
-//      the previous launch's end, the CTAs of this launch seen so far, unused.
+// [14]..[16] scratch: this launch's first start (initialise to UINT64_MAX),
+//      the previous launch's end, the CTAs of this launch seen so far,
+// [17] sum over CTAs of launches after the first of (CTA start - the previous
+//      launch's end), [18] CTAs counted in [17], [19] unused.
 __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
                                             unsigned long long t_start,
                                             unsigned long long t_mid = 0ull) {
   if (a.prof == nullptr) return;
-  if (ws.slow) {
-    atomicAdd(a.prof + 0, ws.ns);
-    atomicAdd(a.prof + 1, (unsigned long long)ws.slow);
+  __shared__ unsigned long long s_wait[3];
+  if (threadIdx.x == 0) s_wait[0] = s_wait[1] = s_wait[2] = 0ull;
+  unsigned long long ns = ws.ns, slow = ws.slow, fast = ws.fast;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ns += __shfl_xor_sync(0xFFFFFFFFu, ns, o);
+    slow += __shfl_xor_sync(0xFFFFFFFFu, slow, o);
+    fast += __shfl_xor_sync(0xFFFFFFFFu, fast, o);
   }
-  if (ws.fast) atomicAdd(a.prof + 2, (unsigned long long)ws.fast);
+  __syncthreads();   // every thread of the CTA is done
+  const unsigned long long t_end = ptx::globaltimer();
+  if ((threadIdx.x & 31) == 0 && (slow | fast)) {
+    atomicAdd(&s_wait[0], ns);
+    atomicAdd(&s_wait[1], slow);
+    atomicAdd(&s_wait[2], fast);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned long long* P = a.prof;
-    const unsigned long long t_end = ptx::globaltimer();
+    if (s_wait[1]) {
+      atomicAdd(P + 0, s_wait[0]);
+      atomicAdd(P + 1, s_wait[1]);
+    }
+    if (s_wait[2]) atomicAdd(P + 2, s_wait[2]);
     atomicMin(P + 3, t_start);
     atomicMax(P + 4, t_end);
     if (t_mid) {
@@ -307,6 +328,13 @@ __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
     }
     atomicAdd(P + 8, t_end - t_start);
     atomicAdd(P + 9, 1ull);
+    // the previous launch's end: stable until this launch's last CTA, which
+    // arrives after this one, overwrites it
+    const unsigned long long prev = atomicAdd(P + 15, 0ull);
+    if (prev != 0ull) {
+      atomicAdd(P + 17, t_start > prev ? t_start - prev : 0ull);
+      atomicAdd(P + 18, 1ull);
+    }
     atomicMin(P + 14, t_start);
     __threadfence();
     const unsigned long long seen = atomicAdd(P + 16, 1ull);

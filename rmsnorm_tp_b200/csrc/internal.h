@@ -39,7 +39,7 @@ struct KArgs {
                                        // the rows one after another (else interleaved), bit 1 =
                                        // normalise them one after another (else interleaved)
   unsigned long long timeout_ns;
-  unsigned long long* prof;            // optional wait/timing counters (18 x u64), or null
+  unsigned long long* prof;            // optional wait/timing counters (20 x u64), or null
   int push_mode;                       // kPushPacked (default) or kPushRelease
   int depth;                           // batch kernels: shared-memory ring slots
 };

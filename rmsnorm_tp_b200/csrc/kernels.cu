@@ -318,9 +318,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   // store of kTeams * kRows slots (one NVLink write per peer, CTA and depth,
   // instead of one per peer and team).
   const int64_t cta_tile0 = (int64_t)blockIdx.x * kTeams;
-#pragma unroll
-  for (int d = 0; d < kDepth; ++d) {
-    if (cta_tile0 + d * stride >= tiles) break;   // uniform over the CTA
+  const bool xlane = kW == 1 || wit == 0;   // the team's exchange warp
+  auto reduce_push = [&](int d) {
     const int64_t tt = first + d * stride;
     if (tt < tiles) {
 #pragma unroll
@@ -344,7 +343,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
           ss[d][r] = s;
         }
       }
-      if ((kW == 1 || wit == 0) && lane < kRows) {
+      if (xlane && lane < kRows) {
         float m = 0.f;
 #pragma unroll
         for (int r = 0; r < kRows; ++r)
@@ -359,49 +358,33 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
         store_slot(a.push_mode, a.mbox[warp] + slot_index(buf, rank, tp, a.nmax, row),
                    s_cpart[d][lane], tag);
     }
-  }
-
-  const unsigned long long t_mid = a.prof ? ptx::globaltimer() : 0ull;
-
-  // one look at every tile's slot, all loads issued back to back (independent
-  // round trips), so that partials that have already arrived cost one round
-  // trip for the whole team instead of one per tile
-  // (packed encoding: the raw words first, the tag tests after, so that no test
-  // waits between two loads; the release encoding's acquire must precede its
-  // value read, so it polls tile by tile)
-  unsigned long long seen[kDepth];
-  bool have[kDepth];
-  if (kW == 1 || wit == 0) {
-#pragma unroll
-    for (int d = 0; d < kDepth; ++d) {
-      const int64_t tt = first + d * stride;
-      const bool remote = tt < tiles && lr < nrows_of(tt) && lq != rank;
-      seen[d] = remote && a.push_mode == kPushPacked
-                    ? ptx::ld_relaxed_sys_u64(a.mbox[rank] +
-                                              slot_index(buf, lq, tp, a.nmax, tt * kRows + lr))
-                    : 0ull;
-      have[d] = !remote;
-    }
-#pragma unroll
-    for (int d = 0; d < kDepth; ++d)
-      if (!have[d] && a.push_mode == kPushPacked) have[d] = slot_tag(seen[d]) == tag;
-  }
-  // poll (what has not arrived yet), normalise and store every tile
-#pragma unroll
-  for (int d = 0; d < kDepth; ++d) {
+  };
+  // one look at a tile's slot (packed encoding; the release encoding's acquire
+  // must precede its value read, so it polls in finish)
+  auto probe = [&](int d) -> unsigned long long {
     const int64_t tt = first + d * stride;
-    if (tt >= tiles) break;
+    const bool remote = xlane && tt < tiles && lr < nrows_of(tt) && lq != rank;
+    return remote && a.push_mode == kPushPacked
+               ? ptx::ld_relaxed_sys_u64(a.mbox[rank] +
+                                         slot_index(buf, lq, tp, a.nmax, tt * kRows + lr))
+               : 0ull;
+  };
+  // the peers' partials of a tile (the probed word, else a bounded poll), the
+  // team's sum, then normalise and store the tile from the registers
+  auto finish = [&](int d, unsigned long long seen) {
+    const int64_t tt = first + d * stride;
+    if (tt >= tiles) return;   // uniform over the team
     float S[kRows];
     bool ok = true;
-    if (kW == 1 || wit == 0) {
+    if (xlane) {
       bool failed = false;
       const bool active = lr < nrows_of(tt);
       float val;
       if (!active || lq == rank) {
         val = mine_of(ss[d]);
-      } else if (have[d]) {
+      } else if (a.push_mode == kPushPacked && slot_tag(seen) == tag) {
         ws.fast += 1;
-        val = slot_value(seen[d]);
+        val = slot_value(seen);
       } else {
         val = poll_slot(a, rank, rp, buf, tag, call, tt * kRows + lr, lq, true, 0.f, failed, ws);
       }
@@ -437,7 +420,27 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
         }
       }
     }
+  };
+
+  // Depth f is finished kLag depths after its push, so its stores overlap the
+  // loads and reductions of the later depths and its peers' partials have an
+  // NVLink round trip's worth of that work to arrive; its slot is probed
+  // before the reduction in between (the probe's round trip overlaps it).
+  // Every push precedes every wait on a depth at least kLag lower, on every
+  // rank, so the waits end.
+  constexpr int kLag = kDepth > 2 ? 2 : kDepth - 1;
+  unsigned long long seen[kDepth];
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d) {
+    if (d >= kLag) seen[d - kLag] = probe(d - kLag);
+    if (cta_tile0 + d * stride < tiles) reduce_push(d);   // uniform over the CTA
+    if (d >= kLag) finish(d - kLag, seen[d - kLag]);
   }
+  const unsigned long long t_mid = a.prof ? ptx::globaltimer() : 0ull;
+#pragma unroll
+  for (int d = kDepth - kLag; d < kDepth; ++d) seen[d] = probe(d);
+#pragma unroll
+  for (int d = kDepth - kLag; d < kDepth; ++d) finish(d, seen[d]);
   finish_launch(rp.state, call);
   flush_stats(a, ws, t_start, t_mid);
 }

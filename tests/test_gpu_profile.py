@@ -34,6 +34,7 @@ def test_profile_counters_count_every_remote_wait(family):
         torch.cuda.synchronize()
         c2 = prof.cpu().tolist()
         assert c2[9] == 2 * ctas and c2[11] == 2 and c2[13] == 1 and c2[12] >= 0
+        assert c2[18] == ctas and c2[17] >= 0   # only the second launch's CTAs
         s = rtp.profile_summary(c2)
         assert s["launch_span_us"] > 0 and s["launch_gap_us"] is not None
         c = c2
