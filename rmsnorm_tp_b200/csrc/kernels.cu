@@ -87,6 +87,16 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
   WaitStats ws;
 
   auto nrows_of = [&](int64_t tt) { return (int)min((int64_t)kRows, a.rows - tt * kRows); };
+  // this thread's weight vectors -> L1 while the first loads are in flight, so
+  // the normalisation's weight reads (after the reduction and the exchange)
+  // hit L1 instead of waiting an L2 round trip
+  auto prefetch_weights = [&] {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int c = (j * kW + wit) * 32 + lane;
+      if (c < V) ptx::prefetch_l1(wg + c);
+    }
+  };
 
   auto load = [&](int64_t tt, uint4 (&xv)[kRows][kVec]) {
     const int64_t row0 = tt * kRows;
@@ -216,6 +226,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
     float ss0[kRows], ss1[kRows], ss2[kRows];
     load(t, x0);
     if (t + stride < tiles) load(t + stride, x1);
+    prefetch_weights();
     if (exchange) {   // read after the first loads are in flight: its latency overlaps theirs
       call = read_generation(rp.state);
       buf = buffer_of(call);
@@ -308,6 +319,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
         xv[d][r][j] = (r < nr && c < V) ? ptx::ld_stream_v4(xr + c) : make_uint4(0u, 0u, 0u, 0u);
       }
     }
+  }
+  // this thread's weight vectors -> L1 while the loads are in flight (the
+  // normalisation reads them after the exchange)
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    if (c < V && first < tiles) ptx::prefetch_l1(wg + c);
   }
   const unsigned long long call = read_generation(rp.state);
   const uint32_t buf = buffer_of(call), tag = tag_of(call);
@@ -567,6 +585,12 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks)
 #pragma unroll
   for (int d = 0; d < kDepth; ++d)
     if (first + d * stride < tiles) load(first + d * stride, xb[d], rb[kRes ? d : 0]);
+  // this thread's weight vectors -> L1 while the first loads are in flight
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const int c = (j * kW + wit) * 32 + lane;
+    if (c < V && first < tiles) ptx::prefetch_l1(wg + c);
+  }
   int slot = 0;
   for (int64_t base = first; base < tiles; base += kDepth * stride) {
 #pragma unroll

@@ -35,6 +35,11 @@ __device__ __forceinline__ uint4 ld_cached_v4(const void* p) {
   return v;
 }
 
+// Brings the line holding p into L1 (no register, nothing waits for it).
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ void st_v4(void* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
