@@ -62,33 +62,15 @@ constexpr unsigned long long kLinWaitNs = 2000000000ull;           // an interna
 // tensor memory (two 256-column fp32 accumulators) and 3 ring stages. 64-column
 // tiles serve calls of few row blocks, where wider tiles would leave most SMs
 // idle while the weights stream from HBM (6 stages of 24 KB in flight).
-//
-// kSmallA (64-column tiles of calls of at most kSmallARows rows): the A tile is
-// loaded as a kSmallARows-row box (4 KB) instead of 128 rows of mostly zero
-// fill. The MMA still reads a 128-row A operand from the stage's address; its
-// rows past the box are whatever lies after it in this CTA's shared memory (the
-// stage's W tile, the next stages, the staging buffer -- all inside the CTA's
-// allocation), and the accumulator rows they produce are never stored (the
-// epilogue stores rows below the call's row count only). A stage then carries
-// 8 KB of weight per 12 KB instead of per 24 KB: 14 stages, 112 KB of weight in
-// flight per SM.
-constexpr int kSmallARows = 32;
-
-template <int kBN, bool kSmallA = false>
+template <int kBN>
 struct LinCfg {
   static_assert(kBN == 64 || kBN == 128 || kBN == 256, "tile width");
-  static_assert(!kSmallA || kBN == 64, "the small A box comes with 64-column tiles");
-  static constexpr int kStages = kSmallA ? 14 : kBN == 256 ? 3 : kBN == 128 ? 4 : 6;
-  static constexpr uint32_t kABytes = (kSmallA ? kSmallARows : kLinTileM) * kLinTileK * 2;
+  static constexpr int kStages = kBN == 256 ? 3 : kBN == 128 ? 4 : 6;
+  static constexpr uint32_t kABytes = kLinTileM * kLinTileK * 2;    // 16 KB
   static constexpr uint32_t kBBytes = kBN * kLinTileK * 2;          // 16 or 32 KB
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kSmem = 1024 + kStages * kStageBytes + kLinStagingBytes;
   static constexpr uint32_t kTmemCols = 2 * kBN;
-  // the last stage's 128-row A operand must end inside the allocation
-  static_assert(kStages * kStageBytes - kStageBytes + kLinTileM * kLinTileK * 2 <=
-                    kStages * kStageBytes + kLinStagingBytes,
-                "A operand reach");
-  static_assert(kStageBytes % 1024 == 0, "stages on 1024-byte swizzle atoms");
 };
 
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity) {
@@ -125,10 +107,10 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 }
 }  // namespace
 
-template <typename T, int kBN, bool kSmallA = false>
+template <typename T, int kBN>
 __global__ void __launch_bounds__(kLinThreads, 1)
     tp_linear_rmsnorm_kernel(const __grid_constant__ LArgs a) {
-  using Cfg = LinCfg<kBN, kSmallA>;
+  using Cfg = LinCfg<kBN>;
   constexpr int kLinStages = Cfg::kStages;
   constexpr uint32_t kLinStageBytes = Cfg::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -513,24 +495,19 @@ cudaError_t encode_2d(EncodeTiledFn fn, unsigned char* out, const void* base, in
 }
 
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_lin_attr[kMaxDevices][2][4];
+std::atomic<int> g_lin_attr[kMaxDevices][2][3];
 
 template <typename T>
-const void* linear_kernel_of(int bn, bool small_a) {
+const void* linear_kernel_of(int bn) {
   return bn == 256   ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 256>)
          : bn == 128 ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 128>)
-         : small_a   ? reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 64, true>)
                      : reinterpret_cast<const void*>(tp_linear_rmsnorm_kernel<T, 64>);
 }
-const void* linear_kernel(int dtype, int bn, bool small_a) {
-  return dtype == kBF16 ? linear_kernel_of<__nv_bfloat16>(bn, small_a)
-                        : linear_kernel_of<__half>(bn, small_a);
+const void* linear_kernel(int dtype, int bn) {
+  return dtype == kBF16 ? linear_kernel_of<__nv_bfloat16>(bn) : linear_kernel_of<__half>(bn);
 }
-uint32_t linear_smem(int bn, bool small_a) {
-  return bn == 256   ? LinCfg<256>::kSmem
-         : bn == 128 ? LinCfg<128>::kSmem
-         : small_a   ? LinCfg<64, true>::kSmem
-                     : LinCfg<64>::kSmem;
+uint32_t linear_smem(int bn) {
+  return bn == 256 ? LinCfg<256>::kSmem : bn == 128 ? LinCfg<128>::kSmem : LinCfg<64>::kSmem;
 }
 }  // namespace
 
@@ -559,18 +536,16 @@ cudaError_t launch_linear(LArgs& a, const void* const* as, const void* const* ws
   if (err != cudaSuccess) return err;
   const int bn = linear_tile_width(a.rows, a.hidden, a.hl, sms / (grid_y > 1 ? grid_y : 1));
   a.nblocks = a.hl / bn;
-  const bool small_a = bn == 64 && a.rows <= kSmallARows;
-  const uint32_t smem = linear_smem(bn, small_a);
+  const uint32_t smem = linear_smem(bn);
   for (int r = 0; r < nranks; ++r) {
-    err = encode_2d(fn, a.tmaps[2 * r], as[r], dtype, (uint64_t)a.k, (uint64_t)a.rows,
-                    small_a ? (uint32_t)kSmallARows : (uint32_t)kLinTileM);
+    err = encode_2d(fn, a.tmaps[2 * r], as[r], dtype, (uint64_t)a.k, (uint64_t)a.rows, kLinTileM);
     if (err != cudaSuccess) return err;
     err = encode_2d(fn, a.tmaps[2 * r + 1], ws[r], dtype, (uint64_t)a.k, (uint64_t)a.hidden,
                     (uint32_t)bn);
     if (err != cudaSuccess) return err;
   }
-  const void* kfn = linear_kernel(dtype, bn, small_a);
-  const int ti = dtype == kBF16 ? 0 : 1, bi = bn == 256 ? 2 : bn == 128 ? 1 : small_a ? 3 : 0;
+  const void* kfn = linear_kernel(dtype, bn);
+  const int ti = dtype == kBF16 ? 0 : 1, bi = bn == 256 ? 2 : bn == 128 ? 1 : 0;
   const bool cacheable = device >= 0 && device < kMaxDevices;
   if (!cacheable || g_lin_attr[device][ti][bi].load() == 0) {
     err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
