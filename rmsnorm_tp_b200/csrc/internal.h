@@ -89,6 +89,7 @@ constexpr int kBatchBase = 500;   // batch kernels: base + index of the warp cou
 // base + register shape
 constexpr int kResidentBase = 600;
 constexpr int kResidentDepth = 4;
+constexpr int64_t kResidentMaxRows = 256;   // the resident kernel serves calls of at most this many rows
 // The register plan `v` (TP > 1) becomes the resident register kernel when every
 // team of a grid of `resident_ctas` CTAs holds at most kResidentDepth tiles.
 VariantDesc finalize_variant(const VariantDesc& v, int tp, int64_t rows, int resident_ctas);

@@ -1657,6 +1657,10 @@ VariantDesc choose_variant(int64_t hl, int dtype, bool aligned, int tp, int64_t 
 
 VariantDesc finalize_variant(const VariantDesc& v, int tp, int64_t rows, int resident_ctas) {
   if (tp < 2 || v.id < 0 || v.id >= kNumShapes || get_family() == kFamilyRegister) return v;
+  // decode-sized calls only: for the 4096-row benchmark call the rotating kernel
+  // measured faster on B200 at every group size (TP 2 / 4 / 8: 11.5 / 10.0 / 9.4
+  // us against 12.0 / 10.6 / 9.8 us per call)
+  if (rows > kResidentMaxRows) return v;
   const int64_t teams = (int64_t)resident_ctas * (v.block_threads / 32 / v.team_warps);
   const int64_t tiles = (rows + v.rows_per_tile - 1) / v.rows_per_tile;
   if (tiles > teams * kResidentDepth) return v;

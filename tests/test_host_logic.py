@@ -130,7 +130,8 @@ def test_kernel_family_switch():
     resident = range(600, 700)
     assert rtp.plan(10, 1024, torch.bfloat16)["variant"] >= 200          # small call: register (TP 1)
     assert rtp.plan(10, 1024, torch.bfloat16, tp=2)["variant"] in resident   # with an exchange
-    assert rtp.plan(4096, 2048, torch.bfloat16, tp=2)["variant"] in resident  # the bench call at N=2
+    assert rtp.plan(256, 2048, torch.bfloat16, tp=2)["variant"] in resident   # decode sizes
+    assert rtp.plan(4096, 2048, torch.bfloat16, tp=2)["variant"] < 100  # the bench call at N=2: rotating
     assert rtp.plan(65536, 1024, torch.bfloat16, tp=2)["variant"] in bulk    # 128 MiB: bulk
     assert rtp.plan(10, 1000, torch.float32, tp=2)["variant"] in resident    # 4000-byte rows
     assert rtp.plan(10, 16384, torch.float32, tp=2)["variant"] == -1         # 64 KB rows: generic
@@ -248,13 +249,15 @@ def test_protocol_simulation_catches_an_early_second_push(tmp_path):
 @pytest.mark.parametrize("hl", [64, 512, 1000, 1024, 2048, 4096, 8192])
 @pytest.mark.parametrize("rows", [1, 300, 4096, 9000])
 def test_resident_plan_holds_at_most_four_tiles_per_team(tp, hl, rows):
-    """With an exchange, a register plan whose teams would hold at most 4 tiles
-    each runs the resident register kernel (every tile's loads in flight at once);
-    its depth is the tiles per team."""
+    """With an exchange, a register plan of at most 256 rows whose teams would
+    hold at most 4 tiles each runs the resident register kernel (every tile's
+    loads in flight at once; its depth is the tiles per team); larger calls keep
+    the rotating kernel."""
     p = rtp.plan(rows, hl, torch.float32, tp=tp, resident_ctas=296)
     teams = 296 * p["teams_per_cta"]
     if 600 <= p["variant"] < 700:
+        assert rows <= 256
         assert p["tiles"] <= teams * 4 and p["depth"] == -(-p["tiles"] // teams)
         assert p["grid"] == min(296, -(-p["tiles"] // p["teams_per_cta"]))
     elif 0 <= p["variant"] < 100:
-        assert p["tiles"] > teams * 4
+        assert p["tiles"] > teams * 4 or rows > 256
