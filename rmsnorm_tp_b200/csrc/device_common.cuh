@@ -355,29 +355,30 @@ __device__ __forceinline__ void flush_stats(const KArgs& a, const WaitStats& ws,
   }
 }
 
-// The CTA's share of the advance of the rank's generation counter by `step`
-// (one per exchange the launch made: forward 1, backward 2; see DeviceState):
-// CTA 0 adds step x kGenUnit - (gridDim.x - 1), the others 1, each once every
-// thread of the CTA has read the counter. A reduction whose result is unused
-// (red.global.add): no CTA waits for it, and the next launch reads the counter
-// only once this grid has completed (stream order, or its griddepcontrol.wait),
-// when every write of the grid is visible. No fence: one would hold each CTA's
-// exit until its outstanding stores, the pushes to peers included, were
-// acknowledged.
+// Advances the rank's generation counter by `step` (one per exchange the launch
+// made: forward and linear 1, backward 2; see DeviceState) once every thread of
+// the CTA has read it. One generation: this CTA's share, a reduction whose
+// result is unused (red.global.add) -- no CTA waits for it. Two: the last CTA
+// of the launch (a returning atomic on `done`) stores the advanced value. The
+// next launch reads the counter only once this grid has completed (stream
+// order, or its griddepcontrol.wait), when every write of the grid is visible.
+// No fence: one would hold each CTA's exit until its outstanding stores, the
+// pushes to peers included, were acknowledged.
 __device__ __forceinline__ void finish_launch(DeviceState* st, unsigned long long call,
                                               unsigned long long step = 1ull) {
-  (void)call;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long share =
-        blockIdx.x == 0 ? step * kGenUnit - (unsigned long long)(gridDim.x - 1) : 1ull;
-    atomicAdd(&st->call, share);
+  if (threadIdx.x != 0) return;
+  if (step == 1ull) {
+    atomicAdd(&st->call, (unsigned long long)gen_share(blockIdx.x, gridDim.x));
+  } else if (atomicAdd(&st->done, 1u) == gridDim.x - 1u) {
+    st->done = 0u;
+    st->call = (call + step) << kGenShift;
   }
 }
 
 // The generation of the running launch (read before the CTA adds its share).
 __device__ __forceinline__ unsigned long long read_generation(const DeviceState* st) {
-  return *reinterpret_cast<const volatile unsigned long long*>(&st->call) >> kGenShift;
+  return gen_of(*reinterpret_cast<const volatile unsigned long long*>(&st->call));
 }
 
 }  // namespace rtp

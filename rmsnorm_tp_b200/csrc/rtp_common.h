@@ -40,22 +40,25 @@ enum DeviceStatus : uint32_t {
 };
 
 // Per-rank state in local device memory (never mapped to peers).
-// The generation counter advances without a returning atomic: `call` holds
-// kGenUnit x (the generation of the next launch) plus the shares that the CTAs
-// of a running launch have added so far. At its end, CTA 0 of a launch adds
-// step x kGenUnit - (grid - 1) and every other CTA adds 1 (fire-and-forget), so
-// a finished launch of any grid size advances `call` by exactly step x kGenUnit.
-// A CTA reads `call` before it adds its own share, so it sees at most
-// kGenUnit - 1 of its launch's shares and call >> kGenShift is the launch's
-// generation (grids stay far below kGenUnit CTAs); the next launch reads it
-// only after this grid has completed.
+// `call` holds kGenUnit x (the generation of the next launch), plus, while a
+// one-generation launch (forward, linear) runs, the shares its CTAs have added
+// so far: at its end CTA 0 adds kGenUnit - (grid - 1) and every other CTA adds
+// 1 (fire-and-forget, no returning atomic), so a finished launch of any grid
+// size advances `call` by exactly kGenUnit. A CTA reads `call` before it adds
+// its own share, so the shares it can see leave out its own: with CTA 0's they
+// sum to at most kGenUnit - 1, without it to at most grid - 1 (grids stay far
+// below kGenUnit CTAs), and call >> kGenShift is the launch's generation. A
+// two-generation launch (backward) cannot split its advance that way (one share
+// alone would reach a unit), so its last CTA -- found by a returning atomic on
+// `done` -- stores the advanced value. The next launch reads `call` only after
+// this grid has completed.
 constexpr int kGenShift = 20;
 constexpr unsigned long long kGenUnit = 1ull << kGenShift;
 constexpr unsigned long long kGenMax = (1ull << (64 - kGenShift)) - 1ull;   // largest generation
 
 struct alignas(64) DeviceState {
   unsigned long long call;      // kGenUnit x generation of the next launch (+ running shares)
-  unsigned int done;            // unused
+  unsigned int done;            // CTAs of a running two-generation launch that have finished
   unsigned int abort;           // set once any CTA gave up; the rest give up fast
   unsigned int err_code;        // first failure (DeviceStatus), set with atomicCAS
   unsigned int err_src;         // source rank whose partial never arrived
@@ -83,6 +86,13 @@ struct alignas(64) DeviceState {
 // buffer) is never taken for call g, unlike the reference's `< generation`
 // test (rmsnorm_tp.cu:128), which also accepts newer generations.
 // ---------------------------------------------------------------------------
+// The device counter's share of CTA `cta` of a one-generation launch of `grid`
+// CTAs, and the generation a counter value holds (see DeviceState).
+RTP_HD uint64_t gen_share(uint32_t cta, uint32_t grid) {
+  return cta == 0u ? kGenUnit - (uint64_t)(grid - 1u) : 1ull;
+}
+RTP_HD uint64_t gen_of(uint64_t counter) { return counter >> kGenShift; }
+
 RTP_HD uint32_t tag_of(uint64_t g) { return (uint32_t)(g % 0xFFFFFFFFull) + 1u; }
 RTP_HD uint32_t buffer_of(uint64_t g) { return (uint32_t)(g & 1ull); }
 

@@ -232,6 +232,33 @@ def test_protocol_host_program(tmp_path):
     assert "ALL PASS" in res.stdout
 
 
+def _build_generation_program(tmp_path, *defines):
+    exe = tmp_path / ("test_generation" + "".join(d.lower() for d in defines))
+    src = os.path.join(ROOT, "tests", "cpp", "test_generation.cpp")
+    inc = os.path.join(ROOT, "rmsnorm_tp_b200", "csrc")
+    subprocess.run(["g++", "-O2", "-std=c++17", "-pthread", "-Wall", *[f"-D{d}" for d in defines],
+                    "-I", inc, src, "-o", str(exe)], check=True)
+    return exe
+
+
+def test_generation_counter_host_program(tmp_path):
+    """The device generation counter (shares of one-generation launches, the
+    last CTA's store for two-generation ones) played by threads over launches of
+    random grid sizes, orders and delays: every CTA reads its launch's generation
+    and every launch advances the counter by exactly its step."""
+    res = subprocess.run([str(_build_generation_program(tmp_path))], capture_output=True,
+                         text=True, timeout=300)
+    assert res.returncode == 0 and "ALL PASS" in res.stdout, res.stdout + res.stderr
+
+
+def test_generation_counter_simulation_catches_an_advance_before_the_read(tmp_path):
+    """Negative control: a CTA that advances the counter before reading it lets
+    the launch's last CTA read the next generation -- the program must fail."""
+    exe = _build_generation_program(tmp_path, "RTP_PLANT_ADD_BEFORE_READ")
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert res.returncode != 0 and "FAIL" in res.stdout, res.stdout
+
+
 def test_protocol_simulation_catches_an_early_second_push(tmp_path):
     """Negative control of the mixed forward / backward simulation: pushing a
     backward call's second partial before the row's first exchange completes lets
