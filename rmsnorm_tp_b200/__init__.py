@@ -23,6 +23,7 @@ from .api import (
     plan_coverage,
     profile_counters,
     profile_summary,
+    PROFILE_COUNTERS,
     set_kernel_family,
     get_kernel_family,
     set_push_mode,
@@ -48,6 +49,7 @@ __all__ = [
     "plan_coverage",
     "profile_counters",
     "profile_summary",
+    "PROFILE_COUNTERS",
     "tag_of",
     "set_kernel_family",
     "get_kernel_family",

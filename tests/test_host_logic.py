@@ -288,3 +288,26 @@ def test_resident_plan_holds_at_most_four_tiles_per_team(tp, hl, rows):
         assert p["grid"] == min(296, -(-p["tiles"] // p["teams_per_cta"]))
     elif 0 <= p["variant"] < 100:
         assert p["tiles"] > teams * 4 or rows > 256
+
+
+def test_profile_summary_means():
+    """profile_summary turns the 20 in-kernel counters into means: waits per slow
+    poll, launch span per launch, gap per counted gap, CTA figures per CTA; a
+    counter that was never counted gives None, and the start-of-launch scratch
+    value (UINT64_MAX as int64 -1) does not leak into any figure."""
+    c = [0] * rtp.PROFILE_COUNTERS
+    c[0], c[1], c[2] = 3_000, 2, 6              # 2 slow polls waiting 3 us in all, 6 fast
+    c[3], c[4] = 1_000, 9_000
+    c[5], c[6], c[7] = 8_000, 4_000, 4          # 4 CTAs with the pushed mark
+    c[8], c[9] = 24_000, 4                      # 4 CTAs, 6 us each
+    c[10], c[11] = 20_000, 2                    # 2 launches of 10 us
+    c[12], c[13] = 1_500, 1                     # one gap of 1.5 us
+    c[14] = -1
+    c[17], c[18] = 6_000, 2                     # CTA start delays after the previous launch
+    s = rtp.profile_summary(c)
+    assert s["polls"] == 8 and s["slow_poll_share"] == 0.25 and s["mean_wait_us"] == 1.5
+    assert s["launch_span_us"] == 10.0 and s["launch_gap_us"] == 1.5
+    assert s["cta_us"] == 6.0 and s["cta_start_delay_us"] == 3.0
+    assert s["cta_load_reduce_push_us"] == 2.0 and s["cta_poll_store_us"] == 1.0
+    empty = rtp.profile_summary([0] * rtp.PROFILE_COUNTERS)
+    assert empty["launch_gap_us"] is None and empty["cta_us"] is None and empty["polls"] == 0
