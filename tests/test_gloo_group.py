@@ -97,13 +97,16 @@ def test_handle_exchange_over_gloo():
 def _missing_peer_worker(rank, world, port, results):
     from rmsnorm_tp_b200 import IpcHandle, exchange_handles
 
-    _init(rank, world, port, timeout_s=3)
+    # the rendezvous waits as long as the ranks' start-up may take; only the
+    # exchange runs over a group with a short timeout
+    _init(rank, world, port)
+    short = dist.new_group(ranks=[0, 1], timeout=datetime.timedelta(seconds=3))
     try:
         if rank == 1:
             results[rank] = "left"      # never joins the exchange
             return
         try:
-            exchange_handles(dist.group.WORLD, 0, IpcHandle(b"\0" * 128))
+            exchange_handles(short, 0, IpcHandle(b"\0" * 128))
             results[rank] = "no error"
         except Exception as e:          # the group timeout ends the wait
             results[rank] = type(e).__name__
